@@ -1,0 +1,193 @@
+/*
+ * yapd_select.h — C ABI of the B200 (sm_100a) block-diffusion select step.
+ *
+ * One call replaces the select body of Chatterbox-Flash's continuous-batching
+ * engine, FlashEngine._step_gpu (m8than/yapd server/engine.py:533-612):
+ *   CFG combine of cond/uncond speech logits (server/engine.py:533-540,
+ *   chatterbox_flash/cfg_guidance.py:33-47), temperature + Gumbel-max token
+ *   sampling (server/engine.py:546-550), the Turbo filter chain top-k / top-p /
+ *   repetition penalty (server/engine_ar.py:220-243) plus min-p, prior-
+ *   calibrated PMI (server/engine.py:553-558, chatterbox_flash/calibration.py:
+ *   39-82, cfg_guidance.py:50-57), position noise, the time-shifted quantile
+ *   threshold and rank-based unmask (server/engine.py:559-593), and the
+ *   per-request state update (server/engine.py:586-612).
+ *
+ * A second entry point, yapd_sample_rows, is TurboEngine._sample
+ * (server/engine_ar.py:220-243): one token per V-wide row, no CFG, no PMI.
+ *
+ * Conventions: every pointer is a device pointer unless stated; shapes are
+ * row-major; the functions enqueue work on `stream` (a cudaStream_t, or NULL
+ * for the legacy default stream) and never synchronise.  They allocate no
+ * memory: scratch comes from the caller's workspace.  A negative return value
+ * is a host-side validation error (nothing was launched); YAPD_OK means the
+ * kernels were enqueued.  Device-side conditions (a bounded wait that expired)
+ * are recorded in the workspace status word, read by yapd_read_status.
+ */
+#ifndef YAPD_SELECT_H_
+#define YAPD_SELECT_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define YAPD_ABI_VERSION 1
+
+/* Return codes (host-side validation; nothing is launched on error). */
+#define YAPD_OK 0
+#define YAPD_ERR_NULL_POINTER -1
+#define YAPD_ERR_BAD_SHAPE -2
+#define YAPD_ERR_BAD_DTYPE -3
+#define YAPD_ERR_MISALIGNED -4
+#define YAPD_ERR_V_TOO_LARGE -5
+#define YAPD_ERR_WORKSPACE -6
+#define YAPD_ERR_LAUNCH -7
+#define YAPD_ERR_BAD_ARG -8
+#define YAPD_ERR_NO_DEVICE -9
+
+/* Device status bits (yapd_read_status). */
+#define YAPD_STATUS_WAIT_TIMEOUT 1u   /* a bounded pipeline wait expired */
+#define YAPD_STATUS_INTERNAL 2u       /* a kernel invariant check failed */
+
+/* Largest vocabulary one logit row may have (register-resident rows). */
+#define YAPD_MAX_V 8208
+/* Largest block length (positions per request). */
+#define YAPD_MAX_L 32
+
+enum yapd_dtype { YAPD_DTYPE_F32 = 0, YAPD_DTYPE_BF16 = 1 };
+enum yapd_history_kind {
+  YAPD_HISTORY_NONE = 0,
+  YAPD_HISTORY_BITMAP = 1, /* int32 words: bit (v&31) of word (v>>5) */
+  YAPD_HISTORY_BYTES = 2   /* one byte (bool) per token, as TurboEngine.seen */
+};
+enum yapd_noise_kind {
+  YAPD_NOISE_PHILOX = 0,  /* in-kernel Philox4x32-10 Gumbel noise */
+  YAPD_NOISE_EXPLICIT = 1 /* caller-supplied Gumbel tensors (parity mode) */
+};
+
+/* Per-request sampling parameters: a NULL array means "use the scalar". */
+typedef struct yapd_sampling {
+  const float* temperature;  /* (B,) ; T <= 0: see zero_temp_greedy */
+  const int32_t* top_k;      /* (B,) ; <= 0 or >= V: off */
+  const float* top_p;        /* (B,) ; >= 1: off */
+  const float* min_p;        /* (B,) ; <= 0: off */
+  const float* rep_penalty;  /* (B,) ; == 1 or no history: off */
+  float temperature_s;
+  int32_t top_k_s;
+  float top_p_s;
+  float min_p_s;
+  float rep_penalty_s;
+  /* 1: T <= 0 takes the argmax without noise (server/engine.py:549-550).
+   * 0: T <= 0 skips the division but still samples (server/engine_ar.py:230). */
+  int32_t zero_temp_greedy;
+  int32_t history_kind;      /* enum yapd_history_kind */
+  const void* history;       /* (B, history_stride) words or bytes */
+  int64_t history_stride;    /* in words (bitmap) or bytes (bytes) */
+} yapd_sampling;
+
+typedef struct yapd_noise {
+  int32_t kind;              /* enum yapd_noise_kind */
+  uint64_t seed;             /* Philox key */
+  uint64_t offset;           /* Philox counter offset (advance per step) */
+  const float* gumbel_tok;   /* explicit: (B, L, V) token noise, strides below */
+  int64_t gt_stride_req;     /* elements between requests */
+  int64_t gt_stride_pos;     /* elements between positions */
+  const float* gumbel_pos;   /* explicit: (B, L) contiguous position noise */
+} yapd_noise;
+
+/*
+ * yapd_select_args — one block-diffusion step over B requests.
+ *
+ * logits element (request b, branch r, position l, token v) lives at
+ *   logits + b*stride_req + r*stride_branch + l*stride_pos + v   (elements),
+ * branch 0 = conditional, 1 = unconditional (FlashEngine's interleaving,
+ * server/engine.py:397-401, 534); the base must be 16-byte aligned and
+ * logits_numel bounds every element the call may read.
+ */
+typedef struct yapd_select_args {
+  int32_t B, nb, L, V, K;       /* nb: 2 with CFG, 1 without */
+  int64_t mask_id, stop_id;
+  int32_t logits_dtype;         /* enum yapd_dtype */
+  const void* logits;
+  int64_t stride_req, stride_branch, stride_pos, logits_numel;
+  const int64_t* xt;            /* (B, L) block tokens */
+  const int64_t* k_step;        /* (B,) */
+  const uint8_t* is_commit;     /* (B,) bool */
+  const float* log_prior;       /* (V,) log of the clamped prior */
+  const int64_t* sched_t;       /* (K,) count schedule */
+  const float* q_t;             /* (K,) quantile table */
+  float cfg_scale;              /* w */
+  float cfg_one_plus;           /* float(1.0 + w), rounded once on the host */
+  float pmi_lambda;             /* prior weight; 1 in the engine */
+  int32_t pos_noise;            /* position_temperature > 0 */
+  int32_t use_quantile;         /* time_shift_tau > 0 */
+  int32_t dense;                /* 1: sample every position (the reference's
+                                   dense pass); 0: only masked positions of
+                                   non-commit requests */
+  yapd_sampling sampling;
+  yapd_noise noise;
+  /* outputs (all required) */
+  int64_t* xt_out;              /* (B, L) xt_final; may alias xt */
+  int32_t* sampled;             /* (B, L) sampled ids; -1 where not sampled */
+  float* pmi;                   /* (B, L) ranked PMI; NaN where not sampled */
+  int32_t* n_unmask;            /* (B,) */
+  int32_t* n_mask_after;        /* (B,) */
+  uint8_t* hit_eos;             /* (B,) */
+  int64_t* k_step_out;          /* (B,) may alias k_step */
+  uint8_t* is_commit_out;       /* (B,) may alias is_commit */
+  void* workspace;
+  size_t workspace_bytes;
+} yapd_select_args;
+
+/* Rows for TurboEngine._sample: logits (R, V) with row stride `stride_row`. */
+typedef struct yapd_sample_args {
+  int32_t R, V;
+  int32_t logits_dtype;
+  const void* logits;
+  int64_t stride_row, logits_numel;
+  yapd_sampling sampling;       /* per-row parameter arrays are (R,) */
+  yapd_noise noise;             /* explicit token noise is (R, V): gt_stride_req */
+  int32_t* sampled;             /* (R,) */
+  void* workspace;
+  size_t workspace_bytes;
+} yapd_sample_args;
+
+/* ABI version of the loaded library (YAPD_ABI_VERSION). */
+int yapd_abi_version(void);
+
+/* Human-readable text for a return code. */
+const char* yapd_status_string(int code);
+
+/* Workspace bytes a yapd_select_step call over B x L positions needs. */
+size_t yapd_select_workspace_size(int32_t B, int32_t L);
+
+/* Workspace bytes a yapd_sample_rows call over R rows needs. */
+size_t yapd_sample_workspace_size(int32_t R);
+
+/* Zero the workspace status word (enqueued on `stream`). */
+int yapd_clear_status(void* workspace, void* stream);
+
+/* Copy the workspace status word to *status_out (synchronises `stream`). */
+int yapd_read_status(const void* workspace, void* stream, uint32_t* status_out);
+
+/*
+ * One select step.  Replaces server/engine.py:533-612 (the select body and
+ * state update of FlashEngine._step_gpu, called from FlashEngine.tick at
+ * server/engine.py:634); cache_len / blk_start advancement stays with the
+ * caller.
+ */
+int yapd_select_step(const yapd_select_args* args, void* stream);
+
+/*
+ * Token sampling over independent rows.  Replaces TurboEngine._sample
+ * (server/engine_ar.py:220-243, called at :336 and :406).
+ */
+int yapd_sample_rows(const yapd_sample_args* args, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* YAPD_SELECT_H_ */

@@ -1,0 +1,54 @@
+"""C-ABI library: loads and exports every symbol the header declares (no GPU needed)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    txt = open(os.path.join(ROOT, "include", "yapd_select.h")).read()
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\*)\s+(yapd_\w+)\s*\(", txt, re.M)))
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    assert "yapd_select_step" in syms and "yapd_sample_rows" in syms
+
+
+def test_library_exports_all_declared_symbols():
+    from yapd_b200.build import build
+    lib_path = build()
+    lib = ctypes.CDLL(lib_path)
+    for s in declared_symbols():
+        assert hasattr(lib, s), f"missing export {s}"
+
+
+def test_binding_matches_header():
+    from yapd_b200 import _native as N
+    assert set(N.EXPORTED) == set(declared_symbols())
+    lib = N.lib()
+    assert lib.yapd_abi_version() == 1
+    assert lib.yapd_select_workspace_size(64, 32) >= 64 * 32 * 4
+    assert b"NULL" in lib.yapd_status_string(-1)
+
+
+def test_host_validation_without_gpu():
+    """Invalid arguments are rejected on the host before any CUDA call."""
+    import ctypes as C
+    from yapd_b200 import _native as N
+    lib = N.lib()
+    a = N.SelectArgs()
+    assert lib.yapd_select_step(C.byref(a), None) == -2          # B = 0
+    a.B, a.nb, a.L, a.V, a.K = 1, 2, 16, 9000, 4
+    assert lib.yapd_select_step(C.byref(a), None) == -5          # V too large
+    a.V = 8194
+    a.logits_dtype = 7
+    assert lib.yapd_select_step(C.byref(a), None) == -3
+    a.logits_dtype = 1
+    assert lib.yapd_select_step(C.byref(a), None) == -1          # NULL pointers
+    a.L = 33
+    assert lib.yapd_select_step(C.byref(a), None) == -2          # L > 32
+    assert lib.yapd_sample_rows(None, None) == -1

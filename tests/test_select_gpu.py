@@ -1,0 +1,175 @@
+"""GPU parity of the select step against the CPU oracle (and the reference fixtures)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import select_oracle as O
+from tests.golden import cases
+from tests.parity_util import compare, run_gpu
+from yapd_b200.workloads import make_config
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def _noise(inp, noise, seed, offset):
+    if noise == "explicit":
+        return inp.gumbel_tok
+    gt, _ = O.philox_noise(seed, offset, inp.B, inp.L, inp.V)
+    return gt
+
+
+def check(inp, noise="explicit", seed=0, offset=0, dense=True, history_as="bitmap"):
+    gpu = run_gpu(inp, noise=noise, seed=seed, offset=offset, dense=dense, history_as=history_as)
+    orc = O.select_step(inp, noise=noise, seed=seed, offset=offset)
+    if dense:
+        pos = torch.ones(inp.B, inp.L, dtype=torch.bool)
+    else:
+        pos = (inp.xt == inp.mask_id) & ~inp.is_commit[:, None]
+        assert bool((gpu["sampled"][~pos] == -1).all())
+        assert bool(torch.isnan(gpu["pmi"][~pos]).all())
+    rep = {}
+    compare(inp, gpu, orc, _noise(inp, noise, seed, offset), positions=pos, report=rep)
+    return gpu, orc, rep
+
+
+@pytest.mark.parametrize("name", cases.REFERENCE_CASES)
+def test_reference_fixture(name):
+    inp = cases.build(name)
+    gpu, orc, rep = check(inp)
+    fx = dict(np.load(os.path.join(HERE, f"{name}.npz")))
+    if rep.get("certified", 0) == 0:
+        assert np.array_equal(gpu["sampled"].numpy(), fx["sampled"])
+        if "xt_final" in fx:
+            assert np.array_equal(gpu["xt"].numpy(), fx["xt_final"])
+
+
+@pytest.mark.parametrize("config,kw", [
+    (0, {}),
+    (0, dict(masked="ragged", k_step=2)),
+    (1, dict(B=8, masked="ragged")),
+    (2, dict(B=24, masked="ragged", commit_frac=0.2)),
+    (3, dict(B=24, masked="ragged")),
+])
+def test_configs_explicit_noise(config, kw):
+    inp = make_config(config, seed=5, **kw)
+    check(inp)
+
+
+@pytest.mark.parametrize("config", [0, 1, 2])
+def test_sparse_mode(config):
+    inp = make_config(config, seed=9, B=8 if config else None, masked="ragged", commit_frac=0.25)
+    check(inp, dense=False)
+
+
+@pytest.mark.parametrize("config", [0, 2, 3])
+def test_philox_noise(config):
+    inp = make_config(config, seed=13, B=6 if config else None, masked="ragged",
+                      explicit_noise=False)
+    check(inp, noise="philox", seed=1234 + config, offset=7 * config + 1)
+
+
+def test_history_as_bytes():
+    inp = make_config(2, seed=17, B=8, masked="ragged")
+    check(inp, history_as="bytes")
+
+
+def _uniform(inp, **kv):
+    B = inp.B
+    for name, val in kv.items():
+        dt = torch.int32 if name == "top_k" else torch.float32
+        setattr(inp, name if name != "rep" else "rep_penalty", torch.full((B,), val, dtype=dt))
+    return inp
+
+
+@pytest.mark.parametrize("kv", [
+    dict(temperature=1.2, top_p=0.99),          # large top-p sets (register bisection path)
+    dict(temperature=1.0, top_k=1000, top_p=0.97),
+    dict(temperature=0.9, top_k=1),
+    dict(temperature=0.9, top_k=8193),
+    dict(temperature=0.8, top_p=0.0),            # nothing kept -> top-1
+    dict(temperature=0.8, min_p=1.5),            # nothing kept -> top-1
+    dict(temperature=0.8, rep=1.3),              # penalty only
+    dict(temperature=0.0),                       # greedy
+    dict(temperature=-1.0, top_p=0.9),
+])
+def test_parameter_edges(kv):
+    inp = make_config(0, seed=21, B=3, L=8)
+    inp = _uniform(inp, top_k=0, top_p=1.0, min_p=0.0, rep=1.0)
+    inp = _uniform(inp, **kv)
+    check(inp)
+
+
+@pytest.mark.parametrize("V", [17, 33, 64, 6563, 8194])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_vocab_sizes_and_dtypes(V, dtype):
+    inp = make_config(0, seed=V, B=2, L=5, V=V, dtype=dtype, masked="ragged")
+    check(inp)
+
+
+def test_no_cfg_branch():
+    inp = make_config(0, seed=31, B=4, L=16)
+    inp.logits = inp.logits.view(4, 2, 16, -1)[:, 0].contiguous()
+    inp.nb = 1
+    inp.cfg_scale = 0.0
+    check(inp)
+
+
+def test_ties_bf16_no_cfg():
+    # bf16 logits without CFG: many exact ties among vals; top-k/top-p boundaries fall on ties
+    inp = make_config(1, seed=41, B=4, L=8, masked="ragged")
+    inp.logits = inp.logits.view(4, 2, 8, -1)[:, 0].contiguous()
+    inp.nb = 1
+    inp.cfg_scale = 0.0
+    inp = _uniform(inp, temperature=1.0, top_k=300, top_p=0.9)
+    check(inp)
+
+
+def test_constant_logits_ties():
+    inp = make_config(0, seed=43, B=2, L=4)
+    inp.logits = torch.zeros_like(inp.logits)
+    inp = _uniform(inp, temperature=1.0, top_k=0, top_p=0.5, min_p=0.0, rep=1.0)
+    check(inp)
+
+
+def test_neg_inf_logits():
+    inp = make_config(0, seed=47, B=2, L=6)
+    inp.logits[:, :, 100:4000] = float("-inf")
+    inp = _uniform(inp, temperature=0.8, top_k=0, top_p=0.95, min_p=0.0, rep=1.0)
+    check(inp)
+
+
+def test_edge_masks_and_commit_rows():
+    inp = cases.build("flash_edge_masks")
+    inp.is_commit = torch.tensor([False, True, False, True])
+    check(inp)
+    check(inp, dense=False)
+
+
+def test_sample_rows_matches_turbo_chain():
+    from yapd_b200.select import sample_rows
+    g = torch.Generator().manual_seed(3)
+    R, V = 64, 6563
+    logits = torch.randn(R, V, generator=g) * 2
+    seen = torch.rand(R, V, generator=g) < 0.02
+    G = O.gumbel_from_uniform(torch.rand(R, V, generator=g))
+    T = torch.full((R,), 0.8)
+    kk = torch.full((R,), 1000, dtype=torch.int32)
+    tp = torch.full((R,), 0.95)
+    mp = torch.zeros(R)
+    rp = torch.full((R,), 1.2)
+    want = O.sample_tokens(logits, T, kk, tp, mp, rp, seen, G, zero_temp="unscaled")
+    dev = torch.device("cuda")
+    got = sample_rows(logits.to(dev), temperature=T.to(dev), top_k=kk.to(dev), top_p=tp.to(dev),
+                      min_p=mp.to(dev), rep_penalty=rp.to(dev), seen=seen.to(dev),
+                      gumbel=G.to(dev)).cpu().long()
+    assert torch.equal(got, want)
+
+
+def test_status_word_clear():
+    from yapd_b200 import select as S
+    inp = make_config(0, seed=1)
+    run_gpu(inp)
+    assert S.read_status() == 0

@@ -1,0 +1,301 @@
+// Shared device helpers for the select-step kernels: bulk copies with
+// mbarriers and bounded waits, exact division, block reductions and sorts.
+#pragma once
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+namespace yapd {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kNegInf = -__builtin_inff();
+
+// --------------------------------------------------------------------- math
+
+// 2^x on the SFU (PTX ex2.approx, relative error about 2^-22).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Correctly rounded a / b from the correctly rounded reciprocal rb = RN(1/b):
+// q = RN(a*rb); r = a - b*q (exact with one FMA); RN(q + r*rb) (Markstein,
+// IBM J. Res. Dev. 34(1), 1990).  Outside the normal range it defers to the
+// IEEE divide.
+__device__ __forceinline__ float div_rn(float a, float b, float rb) {
+  const float q = __fmul_rn(a, rb);
+  const float r = __fmaf_rn(-q, b, a);
+  const float q2 = __fmaf_rn(r, rb, q);
+  const float aq = fabsf(q2);
+  if (!(aq > 1e-30f && aq < 1e30f)) return (a == 0.0f) ? q2 : __fdiv_rn(a, b);
+  return q2;
+}
+
+// Order-preserving map float -> uint32 (larger float -> larger key).
+__device__ __forceinline__ uint32_t ord_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float ord_key_inv(uint32_t k) {
+  const uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(u);
+}
+
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// ------------------------------------------------------------ bulk / mbarrier
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Global -> shared bulk copy completing on `bar` (no multicast, CTA-local).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Wait for phase `parity` of `bar`, giving up after `limit_ns` nanoseconds.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 0u && globaltimer_ns() - t0 > limit_ns) return false;
+  }
+}
+
+// ---------------------------------------------------------------- reductions
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ int warp_sum_i(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide reductions over NW warps through a two-slot ping-pong scratch,
+// one __syncthreads each.  Every thread receives the result.
+template <int NW>
+struct BlockRed {
+  float* f;    // [2][4][NW]
+  double* d;   // [2][2][NW]
+  int* i;      // [2][4][NW]
+  int slot;
+
+  __device__ __forceinline__ float2 max2(float a, float b) {
+    a = warp_max(a);
+    b = warp_max(b);
+    float* s = f + slot * 4 * NW;
+    slot ^= 1;
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) {
+      s[w] = a;
+      s[NW + w] = b;
+    }
+    __syncthreads();
+    float ra = s[0], rb = s[NW];
+#pragma unroll
+    for (int k = 1; k < NW; ++k) {
+      ra = fmaxf(ra, s[k]);
+      rb = fmaxf(rb, s[NW + k]);
+    }
+    return make_float2(ra, rb);
+  }
+  __device__ __forceinline__ float2 sum2(float a, float b) {
+    a = warp_sum(a);
+    b = warp_sum(b);
+    float* s = f + slot * 4 * NW;
+    slot ^= 1;
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) {
+      s[w] = a;
+      s[NW + w] = b;
+    }
+    __syncthreads();
+    float ra = 0.f, rb = 0.f;
+#pragma unroll
+    for (int k = 0; k < NW; ++k) {
+      ra += s[k];
+      rb += s[NW + k];
+    }
+    return make_float2(ra, rb);
+  }
+  // Sum of two doubles and two ints.
+  __device__ __forceinline__ void sum_mixed(double& a, double& b, int& c, int& e) {
+    a = warp_sum_d(a);
+    b = warp_sum_d(b);
+    c = warp_sum_i(c);
+    e = warp_sum_i(e);
+    double* sd = d + slot * 2 * NW;
+    int* si = i + slot * 4 * NW;
+    slot ^= 1;
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) {
+      sd[w] = a;
+      sd[NW + w] = b;
+      si[w] = c;
+      si[NW + w] = e;
+    }
+    __syncthreads();
+    double ra = 0.0, rb = 0.0;
+    int rc = 0, re = 0;
+#pragma unroll
+    for (int k = 0; k < NW; ++k) {
+      ra += sd[k];
+      rb += sd[NW + k];
+      rc += si[k];
+      re += si[NW + k];
+    }
+    a = ra;
+    b = rb;
+    c = rc;
+    e = re;
+  }
+  // Four int sums.
+  __device__ __forceinline__ int4 sum4i(int4 v) {
+    v.x = warp_sum_i(v.x);
+    v.y = warp_sum_i(v.y);
+    v.z = warp_sum_i(v.z);
+    v.w = warp_sum_i(v.w);
+    int* s = i + slot * 4 * NW;
+    slot ^= 1;
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) {
+      s[w] = v.x;
+      s[NW + w] = v.y;
+      s[2 * NW + w] = v.z;
+      s[3 * NW + w] = v.w;
+    }
+    __syncthreads();
+    int4 r = make_int4(0, 0, 0, 0);
+#pragma unroll
+    for (int k = 0; k < NW; ++k) {
+      r.x += s[k];
+      r.y += s[NW + k];
+      r.z += s[2 * NW + k];
+      r.w += s[3 * NW + k];
+    }
+    return r;
+  }
+  // Lexicographic max of (hi, lo) 64-bit keys packed as unsigned long long.
+  __device__ __forceinline__ unsigned long long max_u64(unsigned long long v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long x = __shfl_xor_sync(0xffffffffu, v, o);
+      v = x > v ? x : v;
+    }
+    unsigned long long* s = reinterpret_cast<unsigned long long*>(d + slot * 2 * NW);
+    slot ^= 1;
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) s[w] = v;
+    __syncthreads();
+    unsigned long long r = s[0];
+#pragma unroll
+    for (int k = 1; k < NW; ++k) r = s[k] > r ? s[k] : r;
+    return r;
+  }
+};
+
+// Bitonic sort of n (power of two, n <= 32 * blockDim-limited) u64 keys in
+// shared memory, DESCENDING; all threads of the block take part.
+__device__ __forceinline__ void block_bitonic_desc(unsigned long long* a, int n, int nthreads) {
+  for (int k = 2; k <= n; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int t = threadIdx.x; t < n; t += nthreads) {
+        const int p = t ^ j;
+        if (p > t) {
+          const unsigned long long x = a[t], y = a[p];
+          const bool desc = (t & k) == 0;
+          if (desc ? (x < y) : (x > y)) {
+            a[t] = y;
+            a[p] = x;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Bitonic sort of one value per lane across a warp, DESCENDING.
+__device__ __forceinline__ unsigned long long warp_bitonic_desc(unsigned long long x) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const unsigned long long y = __shfl_xor_sync(0xffffffffu, x, j);
+      const bool up = ((lane & k) == 0);        // this pair sorts descending
+      const bool lower = ((lane & j) == 0);     // this lane holds the first slot
+      const bool take_max = (up == lower);
+      x = take_max ? (x > y ? x : y) : (x < y ? x : y);
+    }
+  }
+  return x;
+}
+
+// Ascending bitonic sort of one float per lane across a warp (values only).
+__device__ __forceinline__ float warp_bitonic_asc_f(float x) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const float y = __shfl_xor_sync(0xffffffffu, x, j);
+      const bool up = ((lane & k) == 0);
+      const bool lower = ((lane & j) == 0);
+      const bool take_min = (up == lower);
+      x = take_min ? fminf(x, y) : fmaxf(x, y);
+    }
+  }
+  return x;
+}
+
+}  // namespace yapd

@@ -18,6 +18,8 @@
 #include <stdint.h>
 #include <math.h>
 
+#include <cuda_bf16.h>
+
 #include "yapd_select.h"
 #include "philox.cuh"
 #include "select_common.cuh"
@@ -33,7 +35,7 @@ struct KCfg {
   static constexpr int W = W_;          // elements per 16-byte vector
   static constexpr int ELEM = ELEM_;    // bytes per logit
   static constexpr int NSTAGE = NSTAGE_;
-  static constexpr int CAP = CAP_;      // candidate-list capacity (power of two)
+  static constexpr int BAND = NT_;      // candidate band capacity (one thread per element)
   static constexpr int MINB = MINB_;    // CTAs per SM the launch bounds target
   static constexpr int NS = NVT * W;    // element slots per thread per row
   static constexpr int NW = NT / 32;
@@ -76,13 +78,11 @@ struct SampleParams {
   uint64_t seed, offset;
   const float* gumbel_tok;
   int64_t gt_stride_req, gt_stride_pos;
-  // PMI
-  const float* log_prior;
-  float cfg_w, cfg_1pw, pmi_lambda;
-  int want_pmi;
+  // CFG weights
+  float cfg_w, cfg_1pw;
   // outputs
   int32_t* sampled;
-  float* pmi;
+  float2* pcu;  // softmax(c)[s], softmax(u)[s] of the sampled token (PMI inputs), or null
   uint32_t* status;
 };
 
@@ -116,16 +116,18 @@ __device__ __forceinline__ RowGeom row_geom(const SampleParams& P, int64_t elem_
 __device__ __forceinline__ float param_f(const float* a, float s, int b) { return a ? a[b] : s; }
 __device__ __forceinline__ int param_i(const int32_t* a, int s, int b) { return a ? a[b] : s; }
 
-__device__ __forceinline__ bool history_has(const SampleParams& P, int b, int v) {
+// Word w of request b's history as a bitmap (bit v&31 of word v>>5).
+__device__ __forceinline__ uint32_t history_word(const SampleParams& P, int b, int w) {
   if (P.history_kind == YAPD_HISTORY_BITMAP) {
-    const uint32_t* w = reinterpret_cast<const uint32_t*>(P.history) + (int64_t)b * P.history_stride;
-    return (__ldg(w + (v >> 5)) >> (v & 31)) & 1u;
+    const uint32_t* h = reinterpret_cast<const uint32_t*>(P.history) + (int64_t)b * P.history_stride;
+    return __ldg(h + w);
   }
-  if (P.history_kind == YAPD_HISTORY_BYTES) {
-    const uint8_t* h = reinterpret_cast<const uint8_t*>(P.history) + (int64_t)b * P.history_stride;
-    return __ldg(h + v) != 0;
-  }
-  return false;
+  // one byte (bool) per token: pack 32 of them
+  const uint8_t* h = reinterpret_cast<const uint8_t*>(P.history) + (int64_t)b * P.history_stride;
+  uint32_t word = 0;
+  const int v0 = w * 32;
+  for (int j = 0; j < 32 && v0 + j < P.V; ++j) word |= (__ldg(h + v0 + j) != 0 ? 1u : 0u) << j;
+  return word;
 }
 
 __device__ __forceinline__ float token_noise(const SampleParams& P, int b, int pos_flat, int l, int v) {
@@ -151,13 +153,13 @@ __device__ __forceinline__ float cand_val(unsigned long long c) { return ord_key
 template <class C>
 struct Smem {
   uint64_t full[C::NSTAGE];
-  float redf[2 * 4 * C::NW];
-  double redd[2 * 2 * C::NW];
-  int redi[2 * 4 * C::NW];
+  float red8[2 * 8 * C::NW];
+  unsigned long long redu[2 * C::NW];
   int misc[8];
-  float miscf[8];
-  unsigned long long cand[C::CAP];
-  double scan[C::NW + 1];
+  unsigned long long cand[C::BAND];
+  float cande[C::BAND];
+  unsigned char cflag[C::BAND];
+  uint32_t hist[(YAPD_MAX_V + 31) / 32 + 1];
   alignas(128) unsigned char stage[C::NSTAGE][C::STAGE_BYTES];
 };
 
@@ -194,6 +196,39 @@ struct Tile {
     }
   }
 };
+
+// Per-thread maxima of the cond and uncond tiles (bf16 pairs compared packed).
+template <class C>
+__device__ __forceinline__ float2 tile_max2(const Tile<C>& tc, const Tile<C>& tu, bool cfg) {
+  if constexpr (C::BF16) {
+    const uint32_t ninf2 = 0xff80ff80u;
+    __nv_bfloat162 mc2 = *reinterpret_cast<const __nv_bfloat162*>(&ninf2);
+    __nv_bfloat162 mu2 = mc2;
+#pragma unroll
+    for (int k = 0; k < C::NVT; ++k) {
+      const uint32_t* a = reinterpret_cast<const uint32_t*>(&tc.v[k]);
+      const uint32_t* u = reinterpret_cast<const uint32_t*>(&tu.v[k]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        mc2 = __hmax2(mc2, *reinterpret_cast<const __nv_bfloat162*>(&a[j]));
+        if (cfg) mu2 = __hmax2(mu2, *reinterpret_cast<const __nv_bfloat162*>(&u[j]));
+      }
+    }
+    const float mc = fmaxf(__bfloat162float(__low2bfloat16(mc2)), __bfloat162float(__high2bfloat16(mc2)));
+    const float mu = fmaxf(__bfloat162float(__low2bfloat16(mu2)), __bfloat162float(__high2bfloat16(mu2)));
+    return make_float2(mc, cfg ? mu : kNegInf);
+  } else {
+    float mc = kNegInf, mu = kNegInf;
+#pragma unroll
+    for (int k = 0; k < C::NVT; ++k)
+#pragma unroll
+      for (int i = 0; i < C::W; ++i) {
+        mc = fmaxf(mc, tc.get(k, i));
+        if (cfg) mu = fmaxf(mu, tu.get(k, i));
+      }
+    return make_float2(mc, mu);
+  }
+}
 
 template <class C>
 __device__ __forceinline__ float load_elem_global(const char* row, int v) {
@@ -323,592 +358,949 @@ __device__ __forceinline__ int item_pos(const SampleParams& P, int idx) {
   return P.n_identity > 0 ? idx : P.work[idx];
 }
 
-// Argmax record: (score, tie-break key, vocabulary id) packed so that the
-// largest u64 wins.  `tb` is the order key used for exact score ties: for the
-// vocabulary-order rule (server/engine.py:548) only the id matters; for the
-// sorted-candidate rule (server/engine_ar.py:242) larger vals come first.
-struct ArgBest {
-  float score;
-  float tb;
-  int v;
+// ------------------------------------------------------------ per-position core
+//
+// Hot path (registers, fully unrolled): row maxima, the sums of exp(x - max),
+// and z2 = log2(e) * (guided / T) - const for every element, computed with two
+// FMAs from the cond/uncond logits; then either the unfiltered argmax, or the
+// min-p candidate band.  Cold paths (top-k / top-p bracketing, massive ties,
+// NaN rows) recompute z2 from the staged shared-memory rows in rolled loops.
+// Every decision that the reference's float rounding can flip is taken on
+// exact values recomputed with the reference's op order (exact_val).
+
+struct PosCtx {
+  float mc, mu;   // row maxima
+  float lc, lu;   // log of sum(exp(x - max)) per row
+  float Sc, Su;   // the sums
+  float zmax, S;  // max of z2 and sum of 2^(z2 - zmax)
+  float A2, B2, K2;  // z2 = A2*c - B2*u + K2
+  float Kval;     // guided/T ~= z2*ln2 + Kval
+  float T, rT;
+  bool scale, cfg;
 };
-__device__ __forceinline__ bool better(float s, float tb, int v, const ArgBest& b, bool use_tb) {
-  if (s > b.score) return true;
-  if (s < b.score) return false;
-  if (s != s) return false;
-  if (use_tb && tb != b.tb) return tb > b.tb;
-  return v < b.v;
+
+constexpr float kLn2 = 0.69314718055994531f;
+constexpr float kBig = 3.0e38f;
+
+// Bound on |z2 - log2(e)*vals - const| (float rounding of the FMA form against
+// the reference's op sequence), with a wide safety factor.
+__device__ __forceinline__ float zmargin(float z) { return 2e-4f + 2e-5f * fabsf(z); }
+
+template <class C>
+struct RowRef {
+  const unsigned char* sc;
+  const unsigned char* su;
+  RowGeom gc, gu;
+};
+
+// guided / T exactly as the reference rounds it (server/engine.py:536-538, :548).
+template <class C>
+__device__ __forceinline__ float exact_val(const SampleParams& P, const PosCtx& X, const RowRef<C>& R, int v) {
+  const float c = load_elem_smem<C>(R.sc, R.gc, v);
+  float g;
+  if (X.cfg) {
+    const float u = load_elem_smem<C>(R.su, R.gu, v);
+    const float lsc = __fsub_rn(__fsub_rn(c, X.mc), X.lc);
+    const float lsu = __fsub_rn(__fsub_rn(u, X.mu), X.lu);
+    g = __fadd_rn(lsc, __fmul_rn(P.cfg_w, __fsub_rn(lsc, lsu)));
+  } else {
+    g = c;
+  }
+  return X.scale ? div_rn(g, X.T, X.rT) : g;
 }
 
-// Count and e-mass (double) of the register-resident elements with
-// ord_key(key) >= x, restricted to `lo_key` (elements with ord_key < lo_key are
-// ignored when lo_key > 0).
+__device__ __forceinline__ float z2_of(const PosCtx& X, float c, float u) {
+  return X.cfg ? __fmaf_rn(c, X.A2, __fmaf_rn(u, -X.B2, X.K2)) : __fmaf_rn(c, X.A2, X.K2);
+}
+
+// The register pass's z2 for token v, recomputed from the staged rows.
 template <class C>
-__device__ __forceinline__ void count_mass_ge(const float (&key)[C::NS], const float (&e)[C::NS],
-                                              int vbase, int V, uint32_t x, int& cnt, double& mass) {
-  int c = 0;
-  float m = 0.f;
+__device__ __forceinline__ float z2_smem(const PosCtx& X, const RowRef<C>& R, int v) {
+  const float c = load_elem_smem<C>(R.sc, R.gc, v);
+  const float u = X.cfg ? load_elem_smem<C>(R.su, R.gu, v) : 0.f;
+  return z2_of(X, c, u);
+}
+
+// ---------------------------------------------------------------- reductions
+
+template <class C>
+__device__ __forceinline__ float2 red_max2(float a, float c, Smem<C>& sm, int& slot) {
+  a = warp_max(a);
+  c = warp_max(c);
+  float* s = sm.red8 + slot * 8 * C::NW;
+  slot ^= 1;
+  if ((threadIdx.x & 31) == 0) {
+    s[threadIdx.x >> 5] = a;
+    s[C::NW + (threadIdx.x >> 5)] = c;
+  }
+  __syncthreads();
+  float ra = s[0], rc = s[C::NW];
+#pragma unroll
+  for (int q = 1; q < C::NW; ++q) {
+    ra = fmaxf(ra, s[q]);
+    rc = fmaxf(rc, s[C::NW + q]);
+  }
+  return make_float2(ra, rc);
+}
+
+template <class C>
+__device__ __forceinline__ float red_max1(float v, Smem<C>& sm, int& slot) {
+  return red_max2<C>(v, kNegInf, sm, slot).x;
+}
+
+template <class C>
+__device__ __forceinline__ unsigned long long red_max_u64(unsigned long long v, Smem<C>& sm, int& slot) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long x = __shfl_xor_sync(0xffffffffu, v, o);
+    v = x > v ? x : v;
+  }
+  unsigned long long* s = sm.redu + slot * C::NW;
+  slot ^= 1;
+  if ((threadIdx.x & 31) == 0) s[threadIdx.x >> 5] = v;
+  __syncthreads();
+  unsigned long long r = s[0];
+#pragma unroll
+  for (int q = 1; q < C::NW; ++q) r = s[q] > r ? s[q] : r;
+  return r;
+}
+
+// Sum of 8 floats over the block (one barrier).
+template <class C>
+__device__ __forceinline__ void block_sum8(float (&v)[8], Smem<C>& sm, int& slot) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = warp_sum(v[j]);
+  float* s = sm.red8 + slot * 8 * C::NW;
+  slot ^= 1;
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j * C::NW + w] = v[j];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float a = 0.f;
+#pragma unroll
+    for (int q = 0; q < C::NW; ++q) a += s[j * C::NW + q];
+    v[j] = a;
+  }
+}
+
+template <class C>
+__device__ __forceinline__ float block_sum1(float v, Smem<C>& sm, int& slot) {
+  float a[8] = {v, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  block_sum8<C>(a, sm, slot);
+  return a[0];
+}
+
+__device__ __forceinline__ void lse2_merge(float& m, float& s, float m2, float s2) {
+  const float M = fmaxf(m, m2);
+  if (M == kNegInf || !(M == M)) {
+    s = s + s2;
+    m = M;
+    return;
+  }
+  s = __fadd_rn(__fmul_rn(s, ex2_approx(__fsub_rn(m, M))), __fmul_rn(s2, ex2_approx(__fsub_rn(m2, M))));
+  m = M;
+}
+
+// Block reduction of the (Sc, Su) sums and the (zmax, S) log-sum-exp pair.
+template <class C>
+__device__ __forceinline__ void block_reduce_sums(float& sc, float& su, float& zm, float& s, Smem<C>& sm,
+                                                  int& slot) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    sc += __shfl_xor_sync(0xffffffffu, sc, o);
+    su += __shfl_xor_sync(0xffffffffu, su, o);
+    const float m2 = __shfl_xor_sync(0xffffffffu, zm, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    lse2_merge(zm, s, m2, s2);
+  }
+  float* b = sm.red8 + slot * 8 * C::NW;
+  slot ^= 1;
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    b[w] = sc;
+    b[C::NW + w] = su;
+    b[2 * C::NW + w] = zm;
+    b[3 * C::NW + w] = s;
+  }
+  __syncthreads();
+  sc = 0.f;
+  su = 0.f;
+  zm = kNegInf;
+  s = 0.f;
+#pragma unroll
+  for (int q = 0; q < C::NW; ++q) {
+    sc += b[q];
+    su += b[C::NW + q];
+    lse2_merge(zm, s, b[2 * C::NW + q], b[3 * C::NW + q]);
+  }
+}
+
+// ---------------------------------------------------------------- scoring
+
+struct Pick {
+  float score;
+  float vals;  // order key for exact score ties (sorted-candidate rule)
+  int v;
+};
+__device__ __forceinline__ bool pick_better(const Pick& a, const Pick& b, bool turbo) {
+  if (a.score > b.score) return true;
+  if (a.score < b.score) return false;
+  if (turbo && a.vals != b.vals) return a.vals > b.vals;
+  return a.v < b.v;
+}
+
+__device__ __noinline__ float philox_noise_nl(uint64_t seed, uint64_t offset, int pos, int v) {
+  return philox_token_gumbel(seed, offset, (uint32_t)pos, (uint32_t)v);
+}
+
+__device__ __forceinline__ float noise_at(const SampleParams& P, int b, int pos, int l, int v) {
+  if (P.noise_kind == YAPD_NOISE_EXPLICIT)
+    return __ldg(P.gumbel_tok + (int64_t)b * P.gt_stride_req + (int64_t)l * P.gt_stride_pos + v);
+  return philox_noise_nl(P.seed, P.offset, pos, v);
+}
+
+struct ScoreCtx {
+  const uint32_t* hist;  // request history bitmap in shared memory
+  int b, pos, l;
+  bool pen_on, noisy, turbo, minp_on;
+  float rep, rrep;
+  float r, minp_thr;  // min-p: keep iff 2^(z2-zmax) * r >= minp_thr
+};
+
+template <class C>
+__device__ __forceinline__ float exact_score(const SampleParams& P, const ScoreCtx& K, int v, float vals) {
+  float s = vals;
+  if (K.pen_on && ((K.hist[v >> 5] >> (v & 31)) & 1u)) s = penalize(vals, K.rep, K.rrep);
+  if (K.noisy) s = __fadd_rn(s, noise_at(P, K.b, K.pos, K.l, v));
+  return s;
+}
+
+template <class C>
+__device__ __forceinline__ float approx_score(const SampleParams& P, const PosCtx& X, const ScoreCtx& K, int v,
+                                              float z) {
+  float va = __fmaf_rn(z, kLn2, X.Kval);
+  if (K.pen_on && ((K.hist[v >> 5] >> (v & 31)) & 1u)) va = va > 0.f ? __fmul_rn(va, K.rrep) : __fmul_rn(va, K.rep);
+  return K.noisy ? __fadd_rn(va, noise_at(P, K.b, K.pos, K.l, v)) : va;
+}
+
+__device__ __forceinline__ float score_margin(float s) { return 2e-3f + 4e-5f * fabsf(s); }
+
+// Block argmax of per-thread Picks; -1 when nothing was picked.
+template <class C>
+__device__ __forceinline__ int block_pick(const Pick& bp, bool turbo, Smem<C>& sm, int& slot) {
+  const bool has = bp.score > kNegInf && bp.score == bp.score;
+  const uint32_t ks = has ? ord_key(bp.score) : 0u;
+  const uint32_t kv = has && turbo ? ord_key(bp.vals) : 0u;
+  const unsigned long long me = ((unsigned long long)ks << 32) | kv;
+  const unsigned long long w1 = red_max_u64<C>(has ? me : 0ull, sm, slot);
+  if (w1 == 0ull) return -1;
+  const unsigned long long w2 =
+      red_max_u64<C>((has && me == w1) ? (unsigned long long)(uint32_t)(0x7fffffff - bp.v) : 0ull, sm, slot);
+  return 0x7fffffff - (int)(uint32_t)w2;
+}
+
+// Hot argmax over the register tile: every valid element with z2 >= H kept
+// (and the min-p test), scored approximately, the near-best rescored exactly.
+template <class C>
+__device__ __forceinline__ int argmax_regs(const SampleParams& P, const PosCtx& X, const RowRef<C>& R,
+                                           const float (&z2)[C::NS], int vbase, float H, const ScoreCtx& K,
+                                           Pick bp, Smem<C>& sm, int& slot) {
+  const int V = P.V;
+  float sa[C::NS];
+  float best = kNegInf;
 #pragma unroll
   for (int s = 0; s < C::NS; ++s) {
     const int v = vbase + (s / C::W) * C::NT * C::W + (s % C::W);
-    const bool in = v >= 0 && v < V && ord_key(key[s]) >= x && key[s] == key[s];
-    c += in ? 1 : 0;
-    m += in ? e[s] : 0.f;
+    float sc = kNegInf;
+    bool keep = v >= 0 && v < V && z2[s] >= H;
+    if (keep && K.minp_on)
+      keep = __fmul_rn(ex2_approx(__fsub_rn(z2[s], X.zmax)), K.r) >= K.minp_thr;
+    if (keep) sc = approx_score<C>(P, X, K, v, z2[s]);
+    sa[s] = sc;
+    best = fmaxf(best, sc);
   }
-  cnt = c;
-  mass = (double)m;
-}
-
-// Sampling with top-k / top-p / min-p / penalty (server/engine_ar.py:230-243
-// and the min-p extension).  Returns the chosen vocabulary id.
-template <class C>
-__device__ __forceinline__ int filtered_select(const SampleParams& P, Smem<C>& sm, BlockRed<C::NW>& red,
-                                            const float (&key)[C::NS], int vbase, int b, int pos,
-                                            int l, int topk_raw, float top_p, float min_p, float rep,
-                                            bool topk_on, bool topp_on, bool minp_on, bool pen_on,
-                                            bool noisy) {
-  const int tid = threadIdx.x;
-  const int V = P.V;
-  const int k_eff = topk_on ? topk_raw : V;
-  const float rrep = pen_on ? __fdiv_rn(1.0f, rep) : 1.0f;
-
-  // ---- softmax over the candidates: vmax, e = exp(vals - vmax), S ----
-  float vm_l = kNegInf;
-#pragma unroll
-  for (int s = 0; s < C::NS; ++s) vm_l = fmaxf(vm_l, key[s]);
-  const float vmax = red.max2(vm_l, 0.f).x;
-  float e[C::NS];
-  float s_l = 0.f;
-#pragma unroll
-  for (int s = 0; s < C::NS; ++s) {
-    e[s] = ex2_approx(__fmul_rn(__fsub_rn(key[s], vmax), kLog2e));
-    if (!(e[s] == e[s])) e[s] = 0.f;
-    s_l += e[s];
-  }
-  const float S = red.sum2(s_l, 0.f).x;
-
-  // ---- candidate threshold: kept (and the top-k set when needed) lie at or above it ----
-  float thr = kNegInf;
-  int n_c = 0;
-  int pick_out = 6;
-  {
-    // ladder on d = vmax - vals; slot 6 is "everything"
-    constexpr int NL = 7;
-    const float D[NL] = {1.f, 2.f, 4.f, 8.f, 16.f, 32.f, 3.0e38f};
-    float t_m = kNegInf;
-    if (minp_on) t_m = fminf(__fsub_rn(__fadd_rn(vmax, logf(min_p)), kMinPMargin), vmax);
-    int cnt[NL];
-    float mass[NL];
-#pragma unroll
-    for (int j = 0; j < NL; ++j) {
-      cnt[j] = 0;
-      mass[j] = 0.f;
-    }
-    int cnt_m = 0;
+  const float gbest = red_max1<C>(best, sm, slot);
+  if (gbest > kNegInf) {
+    const float thr = gbest - score_margin(gbest);
 #pragma unroll
     for (int s = 0; s < C::NS; ++s) {
-      const float d = __fsub_rn(vmax, key[s]);
-#pragma unroll
-      for (int j = 0; j < NL; ++j) {
-        const bool in = d <= D[j];
-        cnt[j] += in ? 1 : 0;
-        mass[j] += in ? e[s] : 0.f;
-      }
-      cnt_m += (key[s] >= t_m && minp_on) ? 1 : 0;
-    }
-    // block totals (counts exact, masses in float)
-    int4 c0 = red.sum4i(make_int4(cnt[0], cnt[1], cnt[2], cnt[3]));
-    int4 c1 = red.sum4i(make_int4(cnt[4], cnt[5], cnt[6], cnt_m));
-    float2 m01 = red.sum2(mass[0], mass[1]);
-    float2 m23 = red.sum2(mass[2], mass[3]);
-    float2 m45 = red.sum2(mass[4], mass[5]);
-    const int ct[NL] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z};
-    const float mt[NL] = {m01.x, m01.y, m23.x, m23.y, m45.x, m45.y, S};
-    const float need_mass = __fmul_rn(__fmul_rn(top_p, S), 1.0001f);
-    int pick = NL - 1;
-    if (!topk_on && minp_on) {
-      thr = t_m;
-      n_c = c1.w;
-      pick = -1;
-    } else {
-#pragma unroll
-      for (int j = NL - 1; j >= 0; --j) {
-        const bool ok = topk_on ? (ct[j] >= k_eff)
-                                : ((topp_on && mt[j] >= need_mass) || (minp_on && vmax - D[j] <= t_m));
-        if (ok) pick = j;
-      }
-      thr = (pick == NL - 1) ? kNegInf : __fsub_rn(vmax, D[pick]);
-      n_c = ct[pick];
-      // the ladder compares d = vmax - key <= D; keep the same predicate below
-    }
-    pick_out = pick;
-  }
-  const int pick = pick_out;
-  const float Dpick[7] = {1.f, 2.f, 4.f, 8.f, 16.f, 32.f, 3.0e38f};
-  auto in_c = [&](float kv) -> bool {
-    if (pick < 0) return kv >= thr;
-    return __fsub_rn(vmax, kv) <= Dpick[pick];
-  };
-
-  if (n_c <= C::CAP) {
-    // ================= small path: compact, sort, resolve exactly =================
-    __syncthreads();
-    if (tid == 0) sm.misc[0] = 0;
-    __syncthreads();
-#pragma unroll
-    for (int s = 0; s < C::NS; ++s) {
-      const int v = vbase + (s / C::W) * C::NT * C::W + (s % C::W);
-      const bool in = (v >= 0 && v < V) && in_c(key[s]);
-      const unsigned bal = __ballot_sync(0xffffffffu, in);
-      if (bal) {
-        int basew = 0;
-        const int lane = tid & 31;
-        if (lane == 0) basew = atomicAdd(&sm.misc[0], __popc(bal));
-        basew = __shfl_sync(0xffffffffu, basew, 0);
-        if (in) {
-          const int at = basew + __popc(bal & ((1u << lane) - 1u));
-          if (at < C::CAP) sm.cand[at] = cand_key(key[s], v);
-        }
-      }
-    }
-    __syncthreads();
-    int nc = sm.misc[0];
-    if (nc > C::CAP) nc = C::CAP;
-    int npad = 1;
-    while (npad < nc) npad <<= 1;
-    for (int q = nc + tid; q < npad; q += C::NT) sm.cand[q] = 0ull;
-    __syncthreads();
-    if (npad <= 32) {
-      if (tid < 32) {
-        unsigned long long x = tid < npad ? sm.cand[tid] : 0ull;
-        x = warp_bitonic_desc(x);
-        if (tid < npad) sm.cand[tid] = x;
-      }
-      __syncthreads();
-    } else {
-      block_bitonic_desc(sm.cand, npad, C::NT);
-    }
-    // ---- normaliser: S over all tokens, or over the top-k list ----
-    float Sn = S;
-    if (topk_on) {
-      float part = 0.f;
-      for (int q = tid; q < nc && q < k_eff; q += C::NT)
-        part += ex2_approx(__fmul_rn(__fsub_rn(cand_val(sm.cand[q]), vmax), kLog2e));
-      Sn = red.sum2(part, 0.f).x;
-    }
-    const float r = __fdiv_rn(1.0f, Sn);
-    const float p0 = __fmul_rn(ex2_approx(__fmul_rn(__fsub_rn(cand_val(sm.cand[0]), vmax), kLog2e)), r);
-    const float minp_thr = __fmul_rn(min_p, p0);
-    // ---- inclusive prefix sums of p in sorted order (double), block scan ----
-    constexpr int PER = C::CAP / C::NT;  // candidates per thread
-    double pre[PER];
-    float pv[PER];
-    double run = 0.0;
-#pragma unroll
-    for (int u = 0; u < PER; ++u) {
-      const int q = tid * PER + u;
-      float p = 0.f;
-      if (q < nc) p = __fmul_rn(ex2_approx(__fmul_rn(__fsub_rn(cand_val(sm.cand[q]), vmax), kLog2e)), r);
-      pv[u] = p;
-      run += (double)p;
-      pre[u] = run;
-    }
-    // exclusive scan of per-thread totals
-    double tot = run;
-    const int lane = tid & 31, wid = tid >> 5;
-    double incl = tot;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const double n = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += n;
-    }
-    if (lane == 31) sm.scan[wid] = incl;
-    __syncthreads();
-    double woff = 0.0;
-    for (int q = 0; q < wid; ++q) woff += sm.scan[q];
-    const double toff = woff + incl - tot;
-    // ---- keep masks and the penalised, noised score of kept candidates ----
-    unsigned long long best = 0ull;  // (score key, -q) max
-    bool any_kept = false;
-#pragma unroll
-    for (int u = 0; u < PER; ++u) {
-      const int q = tid * PER + u;
-      if (q >= nc) continue;
-      const unsigned long long c = sm.cand[q];
-      const float vals = cand_val(c);
-      const int v = cand_id(c);
-      bool keep = true;
-      if (topk_on) keep = keep && (q < k_eff);
-      if (topp_on) {
-        const float cum = __fsub_rn((float)(toff + pre[u]), pv[u]);
-        keep = keep && (cum < top_p);
-      }
-      if (minp_on) keep = keep && (pv[u] >= minp_thr);
-      if (!keep) continue;
-      float sc = vals;
-      if (pen_on && history_has(P, b, v)) sc = penalize(vals, rep, rrep);
-      if (noisy) sc = __fadd_rn(sc, token_noise(P, b, pos, l, v));
-      if (!(sc == sc) || sc == kNegInf) continue;
-      any_kept = true;
-      const unsigned long long rec = ((unsigned long long)ord_key(sc) << 32) | (uint32_t)(0x7fffffff - q);
-      best = rec > best ? rec : best;
-    }
-    (void)any_kept;
-    const unsigned long long win = red.max_u64(best);
-    const int qwin = (win == 0ull) ? 0 : (0x7fffffff - (int)(uint32_t)win);
-    return cand_id(sm.cand[qwin < nc ? qwin : 0]);
-  }
-
-  // ================= large path: exact boundaries by bisection over registers =================
-  // top-1 (lowest id at vmax) for the "nothing kept" case
-  const uint32_t kmax = ord_key(vmax);
-  // (i) top-k boundary x_k: largest x with count(ord >= x) >= k
-  uint32_t xk = 0u;
-  int Jk = 0, tk = 0;
-  double Sk = (double)S;
-  float rr = __fdiv_rn(1.0f, S);
-  if (topk_on) {
-    uint32_t lo = 0u, hi = kmax;
-    while (lo < hi) {
-      const uint32_t mid = lo + (hi - lo + 1u) / 2u;
-      int c;
-      double m;
-      count_mass_ge<C>(key, e, vbase, V, mid, c, m);
-      int dummy = 0;
-      double dm = 0.0;
-      red.sum_mixed(m, dm, c, dummy);
-      if (c >= k_eff) lo = mid;
-      else hi = mid - 1u;
-    }
-    xk = lo;
-    int cg, ce;
-    double mg, me;
-    count_mass_ge<C>(key, e, vbase, V, xk + 1u, cg, mg);
-    count_mass_ge<C>(key, e, vbase, V, xk, ce, me);
-    red.sum_mixed(mg, me, cg, ce);
-    Jk = k_eff - cg;
-    tk = ce - cg;
-    const double etie = (double)ex2_approx(__fmul_rn(__fsub_rn(ord_key_inv(xk), vmax), kLog2e));
-    Sk = mg + (double)Jk * etie;
-    rr = __fdiv_rn(1.0f, (float)Sk);
-  }
-  // (ii) top-p boundary x_p: smallest x >= xk with G(x) = sum_{ord > x} p < top_p
-  uint32_t xp = 0u;
-  int Jp = 0x7fffffff;
-  bool none_kept = false;
-  if (topp_on) {
-    if (!(top_p > 0.0f)) {
-      none_kept = true;
-    } else {
-      auto Gp = [&](uint32_t x) -> double {
-        int c = 0;
-        float m = 0.f;
-#pragma unroll
-        for (int s = 0; s < C::NS; ++s) {
-          const uint32_t o = ord_key(key[s]);
-          const bool in = o > x && key[s] == key[s] && (!topk_on || o > xk);
-          m += in ? __fmul_rn(e[s], rr) : 0.f;
-        }
-        double md = (double)m, d2 = 0.0;
-        int i2 = 0;
-        red.sum_mixed(md, d2, c, i2);
-        if (topk_on && x < xk) {
-          // ties at xk inside the top-k list also count when x < xk
-          int cg, ce;
-          double mg, me;
-          count_mass_ge<C>(key, e, vbase, V, xk + 1u, cg, mg);
-          count_mass_ge<C>(key, e, vbase, V, xk, ce, me);
-          red.sum_mixed(mg, me, cg, ce);
-          const float etie = ex2_approx(__fmul_rn(__fsub_rn(ord_key_inv(xk), vmax), kLog2e));
-          md += (double)Jk * (double)__fmul_rn(etie, rr);
-        }
-        return md;
-      };
-      uint32_t lo = topk_on ? xk : 0u, hi = kmax;
-      if (Gp(lo) < (double)top_p) {
-        xp = lo;
-      } else {
-        while (hi - lo > 1u) {
-          const uint32_t mid = lo + (hi - lo) / 2u;
-          if (Gp(mid) < (double)top_p) hi = mid;
-          else lo = mid;
-        }
-        xp = hi;
-      }
-      // ties at xp: j-th tie (by id) kept iff fl(fl(G + (j+1)p) - p) < top_p
-      int cg, ce;
-      double mg, me;
-      count_mass_ge<C>(key, e, vbase, V, xp + 1u, cg, mg);
-      count_mass_ge<C>(key, e, vbase, V, xp, ce, me);
-      red.sum_mixed(mg, me, cg, ce);
-      const int tp = ce - cg;
-      const double G = Gp(xp);
-      const float pt = __fmul_rn(ex2_approx(__fmul_rn(__fsub_rn(ord_key_inv(xp), vmax), kLog2e)), rr);
-      int lo_j = 0, hi_j = tp;  // first failing j in [0, tp]
-      while (lo_j < hi_j) {
-        const int mid = (lo_j + hi_j) / 2;
-        const float cum = __fsub_rn((float)(G + (double)(mid + 1) * (double)pt), pt);
-        if (cum < top_p) lo_j = mid + 1;
-        else hi_j = mid;
-      }
-      Jp = lo_j;
-      if (topk_on && xp == xk && Jp > Jk) Jp = Jk;
-    }
-  }
-  // (iii) min-p threshold on p
-  const float p0 = __fmul_rn(ex2_approx(__fmul_rn(__fsub_rn(vmax, vmax), kLog2e)), rr);
-  const float minp_thr = __fmul_rn(min_p, p0);
-  // tie-id limits for partially kept tie groups: keep the J smallest ids
-  auto id_limit = [&](uint32_t x, int J) -> int {
-    // largest id bound such that count(ord == x && id <= bound) <= J, via bisection
-    int lo = -1, hi = V - 1;
-    while (lo < hi) {
-      const int mid = lo + (hi - lo + 1) / 2;
-      int c = 0;
-#pragma unroll
-      for (int s = 0; s < C::NS; ++s) {
+      if (sa[s] >= thr) {
         const int v = vbase + (s / C::W) * C::NT * C::W + (s % C::W);
-        c += (v >= 0 && v < V && ord_key(key[s]) == x && v <= mid) ? 1 : 0;
+        const float vals = exact_val<C>(P, X, R, v);
+        const float es = exact_score<C>(P, K, v, vals);
+        const Pick cand{es, vals, v};
+        if (es == es && es > kNegInf && pick_better(cand, bp, K.turbo)) bp = cand;
       }
-      double a = 0.0, bb = 0.0;
-      int z = 0;
-      red.sum_mixed(a, bb, c, z);
-      if (c <= J) lo = mid;
-      else hi = mid - 1;
     }
-    return lo;
-  };
-  int idk = V, idp = V;
-  if (topk_on && Jk < tk) idk = id_limit(xk, Jk);
-  if (topp_on && !none_kept) {
-    int cg, ce;
-    double mg, me;
-    count_mass_ge<C>(key, e, vbase, V, xp + 1u, cg, mg);
-    count_mass_ge<C>(key, e, vbase, V, xp, ce, me);
-    red.sum_mixed(mg, me, cg, ce);
-    if (Jp < ce - cg) idp = id_limit(xp, Jp);
   }
-  // (iv) final argmax over kept: (score desc, vals desc, id asc)
-  ArgBest best{kNegInf, kNegInf, 0x7fffffff};
-  bool anyk = false;
-  if (!none_kept) {
+  return block_pick<C>(bp, K.turbo, sm, slot);
+}
+
+// Cold argmax from the staged rows (rolled loop): elements with z2 >= H are
+// kept (min-p test included); elements with band_lo <= z2 < H are kept iff
+// their composite (exact value, -id) key is >= Xcomp.
+template <class C>
+__device__ __noinline__ int argmax_smem(const SampleParams& P, const PosCtx& X, const RowRef<C>& R, float H,
+                                        float band_lo, unsigned long long Xcomp, const ScoreCtx& K, Pick bp,
+                                        Smem<C>& sm, int& slot) {
+  const int V = P.V;
+  float best = kNegInf;
+  for (int v = threadIdx.x; v < V; v += C::NT) {
+    const float z = z2_smem<C>(X, R, v);
+    if (!(z >= H)) continue;
+    if (K.minp_on && !(__fmul_rn(ex2_approx(__fsub_rn(z, X.zmax)), K.r) >= K.minp_thr)) continue;
+    best = fmaxf(best, approx_score<C>(P, X, K, v, z));
+  }
+  const float gbest = red_max1<C>(best, sm, slot);
+  const float thr = gbest > kNegInf ? gbest - score_margin(gbest) : kBig;
+  for (int v = threadIdx.x; v < V; v += C::NT) {
+    const float z = z2_smem<C>(X, R, v);
+    const bool in_main = z >= H;
+    const bool in_band = z >= band_lo && z < H;
+    if (!in_main && !in_band) continue;
+    if (K.minp_on && !(__fmul_rn(ex2_approx(__fsub_rn(z, X.zmax)), K.r) >= K.minp_thr)) continue;
+    float vals;
+    if (in_main) {
+      if (!(approx_score<C>(P, X, K, v, z) >= thr)) continue;
+      vals = exact_val<C>(P, X, R, v);
+    } else {
+      vals = exact_val<C>(P, X, R, v);
+      if (cand_key(vals, v) < Xcomp) continue;
+    }
+    const float es = exact_score<C>(P, K, v, vals);
+    const Pick cand{es, vals, v};
+    if (es == es && es > kNegInf && pick_better(cand, bp, K.turbo)) bp = cand;
+  }
+  return block_pick<C>(bp, K.turbo, sm, slot);
+}
+
+// Best kept band element (exact; band sorted in sm.cand with flags in sm.cflag).
+template <class C>
+__device__ __forceinline__ Pick band_pick(const SampleParams& P, const ScoreCtx& K, int nband, Smem<C>& sm) {
+  Pick bp{kNegInf, kNegInf, 0x7fffffff};
+  for (int q = threadIdx.x; q < nband; q += C::NT) {
+    if (!sm.cflag[q]) continue;
+    const unsigned long long c = sm.cand[q];
+    const int v = cand_id(c);
+    const float vals = cand_val(c);
+    const float s = exact_score<C>(P, K, v, vals);
+    const Pick cand{s, vals, v};
+    if (s == s && s > kNegInf && pick_better(cand, bp, K.turbo)) bp = cand;
+  }
+  return bp;
+}
+
+// ---------------------------------------------------------------- bands
+
+struct Band {
+  int n;          // elements in the band (<= BAND unless overflow)
+  float H;        // z2 >= H: outside and above the band
+  float n_above;  // count of z2 >= H
+  float m_above;  // mass (2^(z2-zmax)) of z2 >= H
+  bool overflow;
+};
+
+// Sort sm.cand[0..n) descending with sm.cande alongside (one thread per element).
+template <class C>
+__device__ __forceinline__ void rank_sort(int n, Smem<C>& sm) {
+  const int tid = threadIdx.x;
+  unsigned long long key = 0ull;
+  float ev = 0.f;
+  int rank = 0;
+  if (tid < n) {
+    key = sm.cand[tid];
+    ev = sm.cande[tid];
+    for (int j = 0; j < n; ++j) rank += (sm.cand[j] > key) ? 1 : 0;
+  }
+  __syncthreads();
+  if (tid < n) {
+    sm.cand[rank] = key;
+    sm.cande[rank] = ev;
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ void band_push(unsigned long long* cand, float* cande, int* counter, bool in,
+                                          unsigned long long key_if_in, float e_if_in, int cap) {
+  const int lane = threadIdx.x & 31;
+  const unsigned bal = __ballot_sync(0xffffffffu, in);
+  if (bal) {
+    int base = 0;
+    if (lane == 0) base = atomicAdd(counter, __popc(bal));
+    base = __shfl_sync(0xffffffffu, base, 0);
+    if (in) {
+      const int at = base + __popc(bal & ((1u << lane) - 1u));
+      if (at < cap) {
+        cand[at] = key_if_in;
+        cande[at] = e_if_in;
+      }
+    }
+  }
+}
+
+// Hot band from registers: {z2 >= lo_z} (nothing above it), unsorted in
+// sm.cand / sm.cande.  sm.misc[0] must be zero on entry (and a barrier passed).
+template <class C>
+__device__ __forceinline__ int band_regs(const SampleParams& P, const PosCtx& X, const RowRef<C>& R,
+                                         const float (&z2)[C::NS], int vbase, float lo_z, Smem<C>& sm) {
+  uint64_t cm = 0ull;
 #pragma unroll
-    for (int s = 0; s < C::NS; ++s) {
-      const int v = vbase + (s / C::W) * C::NT * C::W + (s % C::W);
-      if (v < 0 || v >= V) continue;
-      const float kv = key[s];
-      const uint32_t o = ord_key(kv);
-      bool keep = true;
-      if (topk_on) keep = keep && (o > xk || (o == xk && v <= idk));
-      if (topp_on) keep = keep && (o > xp || (o == xp && v <= idp));
-      if (minp_on) keep = keep && (__fmul_rn(e[s], rr) >= minp_thr);
-      if (!keep) continue;
-      float sc = kv;
-      if (pen_on && history_has(P, b, v)) sc = penalize(kv, rep, rrep);
-      if (noisy) sc = __fadd_rn(sc, token_noise(P, b, pos, l, v));
-      if (!(sc == sc) || sc == kNegInf) continue;
-      anyk = true;
-      if (better(sc, kv, v, best, true)) best = {sc, kv, v};
-    }
-  }
-  const uint32_t sk = anyk ? ord_key(best.score) : 0u;
-  const unsigned long long w1 = red.max_u64(((unsigned long long)sk << 32) | (anyk ? ord_key(best.tb) : 0u));
-  if (w1 == 0ull) {
-    // nothing kept: the first sorted candidate (largest vals, lowest id)
-    int c_id = 0x7fffffff;
+  for (int s = 0; s < C::NS; ++s) cm |= (z2[s] >= lo_z) ? (1ull << s) : 0ull;
+  const int lane = threadIdx.x & 31;
+  const int cnt = __popcll(cm);
+  int incl = cnt;
 #pragma unroll
-    for (int s = 0; s < C::NS; ++s) {
-      const int v = vbase + (s / C::W) * C::NT * C::W + (s % C::W);
-      if (v >= 0 && v < V && ord_key(key[s]) == kmax && v < c_id) c_id = v;
-    }
-    const unsigned long long w = red.max_u64((unsigned long long)(uint32_t)(0x7fffffff - c_id));
-    const int id = 0x7fffffff - (int)(uint32_t)w;
-    return (id >= 0 && id < V) ? id : 0;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
   }
-  const bool tie = anyk && ((((unsigned long long)sk << 32) | ord_key(best.tb)) == w1);
-  const unsigned long long w2 = red.max_u64(tie ? (unsigned long long)(uint32_t)(0x7fffffff - best.v) : 0ull);
-  const int id = 0x7fffffff - (int)(uint32_t)w2;
-  return (id >= 0 && id < V) ? id : 0;
+  const int wtot = __shfl_sync(0xffffffffu, incl, 31);
+  int base = 0;
+  if (lane == 31 && wtot > 0) base = atomicAdd(&sm.misc[0], wtot);
+  base = __shfl_sync(0xffffffffu, base, 31) + incl - cnt;
+  while (cm) {
+    const int s = __ffsll((long long)cm) - 1;
+    cm &= cm - 1ull;
+    const int v = vbase + (s / C::W) * C::NT * C::W + (s % C::W);
+    if (base < C::BAND) {
+      sm.cand[base] = cand_key(exact_val<C>(P, X, R, v), v);
+      sm.cande[base] = ex2_approx(__fsub_rn(z2_smem<C>(X, R, v), X.zmax));
+    }
+    ++base;
+  }
+  __syncthreads();
+  return sm.misc[0];
+}
+
+// Resolve a band of at most 32 candidates inside warp 0: sort, top-p / min-p
+// flags from the prefix sums, exact scores, argmax.  Returns the chosen id
+// (valid in warp 0 only).
+template <class C>
+__device__ __forceinline__ int band_warp_choose(const SampleParams& P, const PosCtx& X, const RowRef<C>& R,
+                                                const ScoreCtx& K, int n, bool topp_on, float top_p,
+                                                bool minp_on, float min_p, Smem<C>& sm) {
+  const int lane = threadIdx.x & 31;
+  unsigned long long key = lane < n ? sm.cand[lane] : 0ull;
+  key = warp_bitonic_desc(key);
+  const bool live = lane < n;
+  const int v = cand_id(key);
+  const float vals = cand_val(key);
+  const float e = live ? ex2_approx(__fsub_rn(z2_smem<C>(X, R, v), X.zmax)) : 0.f;
+  const float p = __fmul_rn(e, K.r);
+  double incl = (double)p;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  const float p0 = __shfl_sync(0xffffffffu, p, 0);
+  bool keep = live;
+  if (topp_on) keep = keep && (__fsub_rn((float)incl, p) < top_p);
+  if (minp_on) keep = keep && (p >= __fmul_rn(min_p, p0));
+  float sc = kNegInf;
+  if (keep) sc = exact_score<C>(P, K, v, vals);
+  if (!(sc == sc)) sc = kNegInf;
+  // argmax: score desc, then sorted position (lane) asc
+  const uint32_t ks = sc > kNegInf ? ord_key(sc) : 0u;
+  unsigned long long rec = ks ? (((unsigned long long)ks << 32) | (uint32_t)(31 - lane)) : 0ull;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long x = __shfl_xor_sync(0xffffffffu, rec, o);
+    rec = x > rec ? x : rec;
+  }
+  const int win_lane = rec ? 31 - (int)(uint32_t)(rec & 0xffffffffu) : 0;
+  return __shfl_sync(0xffffffffu, v, win_lane);
+}
+
+// Cold band from the staged rows: {lo_z <= z2 < hi_z}, with count and mass above hi_z.
+template <class C>
+__device__ __noinline__ Band band_smem(const SampleParams& P, const PosCtx& X, const RowRef<C>& R, float lo_z,
+                                       float hi_z, Smem<C>& sm, int& slot) {
+  const int V = P.V;
+  __syncthreads();
+  if (threadIdx.x == 0) sm.misc[0] = 0;
+  __syncthreads();
+  float na = 0.f, ma = 0.f;
+  for (int v0 = 0; v0 < V; v0 += C::NT) {
+    const int v = v0 + threadIdx.x;
+    float z = kNegInf;
+    if (v < V) z = z2_smem<C>(X, R, v);
+    const bool above = v < V && z >= hi_z;
+    na += above ? 1.f : 0.f;
+    ma += above ? ex2_approx(__fsub_rn(z, X.zmax)) : 0.f;
+    const bool in = v < V && z >= lo_z && z < hi_z;
+    unsigned long long key = 0ull;
+    float e = 0.f;
+    if (in) {
+      key = cand_key(exact_val<C>(P, X, R, v), v);
+      e = ex2_approx(__fsub_rn(z, X.zmax));
+    }
+    band_push(sm.cand, sm.cande, &sm.misc[0], in, key, e, C::BAND);
+  }
+  float acc[8] = {na, ma, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  block_sum8<C>(acc, sm, slot);
+  Band bd;
+  bd.n = sm.misc[0];
+  bd.overflow = bd.n > C::BAND;
+  if (bd.overflow) bd.n = C::BAND;
+  bd.H = hi_z;
+  bd.n_above = acc[0];
+  bd.m_above = acc[1];
+  if (!bd.overflow) rank_sort<C>(bd.n, sm);
+  return bd;
+}
+
+// Per band element (sorted position q): kept by top-k (q < k_left), top-p
+// (cum_before < top_p over the band's prefix on top of the mass above it)
+// and min-p (p >= minp_thr).  Writes sm.cflag[q].
+template <class C>
+__device__ __forceinline__ void band_flags(const Band& bd, bool use_k, int k_left, bool topp_on, float top_p,
+                                           float r, bool minp_on, float minp_thr, Smem<C>& sm) {
+  const int tid = threadIdx.x;
+  if (tid < 32) {
+    double run = (double)bd.m_above * (double)r;
+    for (int q0 = 0; q0 < bd.n; q0 += 32) {
+      const int q = q0 + tid;
+      const float p = q < bd.n ? __fmul_rn(sm.cande[q], r) : 0.f;
+      double incl = (double)p;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const double n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (tid >= o) incl += n;
+      }
+      incl += run;
+      if (q < bd.n) {
+        bool keep = true;
+        if (use_k) keep = keep && (q < k_left);
+        if (topp_on) keep = keep && (__fsub_rn((float)incl, p) < top_p);
+        if (minp_on) keep = keep && (p >= minp_thr);
+        sm.cflag[q] = keep ? 1 : 0;
+      }
+      run = __shfl_sync(0xffffffffu, incl, 31);
+    }
+  }
+  __syncthreads();
+}
+
+// Counts and masses of {z2 >= t[j]} over the staged rows.
+template <class C>
+__device__ __forceinline__ void stats4_smem(const PosCtx& X, const RowRef<C>& R, int V, const float (&t)[4],
+                                            float (&cnt)[4], float (&mass)[4], Smem<C>& sm, int& slot) {
+  float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int v = threadIdx.x; v < V; v += C::NT) {
+    const float z = z2_smem<C>(X, R, v);
+    const float e = ex2_approx(__fsub_rn(z, X.zmax));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const bool in = z >= t[j];
+      a[j] += in ? 1.f : 0.f;
+      a[4 + j] += in ? e : 0.f;
+    }
+  }
+  block_sum8<C>(a, sm, slot);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    cnt[j] = a[j];
+    mass[j] = a[4 + j];
+  }
+}
+
+// Bracket the z2 where stat(z2 >= t) (count or mass) crosses the target:
+// on return stat(hi) < tgt_lo and stat(lo) >= tgt_hi, with few elements
+// between them unless the values are (near) ties.
+template <class C>
+__device__ __noinline__ void bracket_smem(const PosCtx& X, const RowRef<C>& R, int V, bool by_mass, float tgt_lo,
+                                          float tgt_hi, float floor_t, float cnt_floor, float& lo, float& hi,
+                                          Smem<C>& sm, int& slot) {
+  lo = floor_t;
+  float cnt_lo = cnt_floor;
+  hi = X.zmax + 1.0f;
+  float cnt_hi = 0.f;
+  constexpr int kTarget = C::BAND / 2;
+  for (int round = 0; round < 12; ++round) {
+    float t[4];
+    if (round == 0) {
+      const float L[4] = {2.f, 6.f, 12.f, 24.f};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) t[j] = fmaxf(__fsub_rn(X.zmax, L[j]), floor_t);
+    } else {
+      const float lo_e = fmaxf(lo, __fsub_rn(hi, 64.f));
+#pragma unroll
+      for (int j = 0; j < 4; ++j) t[j] = lo_e + (hi - lo_e) * (float)(j + 1) * 0.2f;
+    }
+    float cnt[4], mass[4];
+    stats4_smem<C>(X, R, V, t, cnt, mass, sm, slot);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float F = by_mass ? mass[j] : cnt[j];
+      if (F >= tgt_hi && t[j] > lo) {
+        lo = t[j];
+        cnt_lo = cnt[j];
+      }
+      if (F < tgt_lo && t[j] < hi) {
+        hi = t[j];
+        cnt_hi = cnt[j];
+      }
+    }
+    if (cnt_lo - cnt_hi <= (float)kTarget) break;
+    if (hi - lo <= 8.f * zmargin(hi)) break;
+  }
+}
+
+// Massive-tie fallback for a band too large for shared memory: composite
+// (exact value, -id) thresholds by bisection (top-k by count, top-p by the
+// exclusive prefix mass).  Band elements with composite >= the result are kept.
+template <class C>
+__device__ __noinline__ unsigned long long overflow_resolve(const SampleParams& P, const PosCtx& X,
+                                                            const RowRef<C>& R, float lo_z, float hi_z,
+                                                            float n_above, float m_above, bool topk_on, int kk,
+                                                            bool topp_on, float top_p, float S_all, float& Sk_out,
+                                                            Smem<C>& sm, int& slot) {
+  const int V = P.V;
+  unsigned long long Xk = 0ull;
+  float Sn = S_all;
+  if (topk_on) {
+    const int need = kk - (int)n_above;
+    if (need <= 0) {
+      Xk = ~0ull;
+    } else {
+      unsigned long long lo = 0ull, hi = ~0ull;
+      while (lo < hi) {
+        const unsigned long long mid = lo + (hi - lo) / 2ull + 1ull;
+        float cnt = 0.f;
+        for (int v = threadIdx.x; v < V; v += C::NT) {
+          const float z = z2_smem<C>(X, R, v);
+          if (z >= lo_z && z < hi_z) cnt += (cand_key(exact_val<C>(P, X, R, v), v) >= mid) ? 1.f : 0.f;
+        }
+        if (block_sum1<C>(cnt, sm, slot) >= (float)need) lo = mid;
+        else hi = mid - 1ull;
+      }
+      Xk = lo;
+    }
+    float m = 0.f;
+    for (int v = threadIdx.x; v < V; v += C::NT) {
+      const float z = z2_smem<C>(X, R, v);
+      if (z >= lo_z && z < hi_z && cand_key(exact_val<C>(P, X, R, v), v) >= Xk)
+        m += ex2_approx(__fsub_rn(z, X.zmax));
+    }
+    Sn = __fadd_rn(m_above, block_sum1<C>(m, sm, slot));
+  }
+  Sk_out = Sn;
+  unsigned long long Xr = Xk;
+  if (topp_on) {
+    const double tgt = (double)top_p * (double)Sn;
+    unsigned long long lo = 0ull, hi = ~0ull;
+    while (lo < hi) {
+      const unsigned long long mid = lo + (hi - lo) / 2ull;
+      float m = 0.f;
+      for (int v = threadIdx.x; v < V; v += C::NT) {
+        const float z = z2_smem<C>(X, R, v);
+        if (z >= lo_z && z < hi_z) {
+          const unsigned long long ck = cand_key(exact_val<C>(P, X, R, v), v);
+          if (ck > mid && ck >= Xk) m += ex2_approx(__fsub_rn(z, X.zmax));
+        }
+      }
+      if ((double)m_above + (double)block_sum1<C>(m, sm, slot) < tgt) hi = mid;
+      else lo = mid + 1ull;
+    }
+    Xr = lo > Xr ? lo : Xr;
+  }
+  return Xr;
+}
+
+// Lowest id whose z2 is NaN, else +inf, else -1 (torch orders NaN first).
+template <class C>
+__device__ __noinline__ int first_nan_or_inf(const PosCtx& X, const RowRef<C>& R, int V, Smem<C>& sm, int& slot) {
+  int fn = 0x7fffffff, fi = 0x7fffffff;
+  for (int v = threadIdx.x; v < V; v += C::NT) {
+    const float z = z2_smem<C>(X, R, v);
+    if (!(z == z) && v < fn) fn = v;
+    if (z == __int_as_float(0x7f800000) && v < fi) fi = v;
+  }
+  const unsigned long long w = red_max_u64<C>(
+      ((unsigned long long)(uint32_t)(0x7fffffff - fn) << 32) | (uint32_t)(0x7fffffff - fi), sm, slot);
+  const int n = 0x7fffffff - (int)(uint32_t)(w >> 32);
+  if (n != 0x7fffffff) return n;
+  // no NaN anywhere: the largest +inf record wins the low half only if no thread saw NaN
+  const unsigned long long w2 = red_max_u64<C>((unsigned long long)(uint32_t)(0x7fffffff - fi), sm, slot);
+  const int i = 0x7fffffff - (int)(uint32_t)w2;
+  return i == 0x7fffffff ? -1 : i;
+}
+
+// First sorted candidate (largest exact value, lowest id): torch's argmax over
+// an all -inf row returns it.
+template <class C>
+__device__ __noinline__ int top1_smem(const SampleParams& P, const PosCtx& X, const RowRef<C>& R, Smem<C>& sm,
+                                     int& slot) {
+  unsigned long long best = 0ull;
+  const float zlo = __fsub_rn(X.zmax, zmargin(X.zmax));
+  for (int v = threadIdx.x; v < P.V; v += C::NT) {
+    const float z = z2_smem<C>(X, R, v);
+    if (z >= zlo) {
+      const unsigned long long k = cand_key(exact_val<C>(P, X, R, v), v);
+      best = k > best ? k : best;
+    }
+  }
+  const unsigned long long w = red_max_u64<C>(best, sm, slot);
+  const int id = cand_id(w);
+  return (w == 0ull || id < 0 || id >= P.V) ? 0 : id;
+}
+
+// Top-k / top-p (and min-p) selection from the staged rows.
+template <class C>
+__device__ __noinline__ int select_cold(const SampleParams& P, const PosCtx& X, const RowRef<C>& R, ScoreCtx K,
+                                        int topk_raw, bool topk_on, bool topp_on, float top_p, float min_p,
+                                        Smem<C>& sm, int& slot) {
+  const int V = P.V;
+  float H = -kBig, band_lo = kBig;
+  unsigned long long Xcomp = 0ull;
+  int nband = 0;
+  float Sn = X.S;
+  K.r = __fdiv_rn(1.0f, Sn);
+  float Hk = -kBig, cnt_k = (float)V;
+  Band bk{};
+  int k_left = 0;
+  bool done = false;
+  if (topk_on) {
+    float lo, hi;
+    bracket_smem<C>(X, R, V, false, (float)topk_raw, (float)topk_raw, -kBig, (float)V, lo, hi, sm, slot);
+    const float blo = __fsub_rn(lo, zmargin(lo)), bhi = __fadd_rn(hi, zmargin(hi));
+    bk = band_smem<C>(P, X, R, blo, bhi, sm, slot);
+    if (bk.overflow) {
+      float Sk;
+      Xcomp = overflow_resolve<C>(P, X, R, blo, bhi, bk.n_above, bk.m_above, true, topk_raw,
+                                  topp_on && bk.m_above < __fmul_rn(top_p, X.S), top_p, X.S, Sk, sm, slot);
+      Sn = Sk;
+      K.r = __fdiv_rn(1.0f, Sn);
+      if (K.minp_on) K.minp_thr = __fmul_rn(min_p, K.r);
+      H = bhi;
+      band_lo = blo;
+      nband = 0;
+      done = true;
+    } else {
+      k_left = topk_raw - (int)bk.n_above;
+      float part = 0.f;
+      for (int q = threadIdx.x; q < bk.n && q < k_left; q += C::NT) part += sm.cande[q];
+      Sn = __fadd_rn(bk.m_above, block_sum1<C>(part, sm, slot));
+      K.r = __fdiv_rn(1.0f, Sn);
+      Hk = bk.H;
+      cnt_k = bk.n_above;
+    }
+  }
+  if (!done) {
+    const float p0 = (topk_on && bk.n_above == 0.f && bk.n > 0) ? __fmul_rn(sm.cande[0], K.r) : K.r;
+    if (K.minp_on) K.minp_thr = __fmul_rn(min_p, p0);
+    const float tgt = __fmul_rn(top_p, Sn);
+    if (topp_on && !(topk_on && bk.m_above < __fmul_rn(tgt, 1.00001f))) {
+      float lo, hi;
+      bracket_smem<C>(X, R, V, true, __fmul_rn(tgt, 0.99999f), __fmul_rn(tgt, 1.00001f), Hk, cnt_k, lo, hi, sm,
+                      slot);
+      const float blo = fmaxf(__fsub_rn(lo, zmargin(lo)), Hk), bhi = __fadd_rn(hi, zmargin(hi));
+      const Band bp = band_smem<C>(P, X, R, blo, bhi, sm, slot);
+      if (bp.overflow) {
+        float Sk;
+        Xcomp = overflow_resolve<C>(P, X, R, blo, bhi, bp.n_above, bp.m_above, false, 0, true, top_p, Sn, Sk,
+                                    sm, slot);
+        H = bhi;
+        band_lo = blo;
+        nband = 0;
+      } else {
+        band_flags<C>(bp, false, 0, true, top_p, K.r, K.minp_on, K.minp_thr, sm);
+        H = bp.H;
+        nband = bp.n;
+      }
+    } else if (topk_on) {
+      band_flags<C>(bk, true, k_left, topp_on, top_p, K.r, K.minp_on, K.minp_thr, sm);
+      H = bk.H;
+      nband = bk.n;
+    } else {
+      // min-p set too large for one band: min-p as an elementwise condition
+      H = -kBig;
+      nband = 0;
+    }
+  }
+  const Pick bp0 = band_pick<C>(P, K, nband, sm);
+  const int c = argmax_smem<C>(P, X, R, H, band_lo, Xcomp, K, bp0, sm, slot);
+  return c >= 0 ? c : top1_smem<C>(P, X, R, sm, slot);
 }
 
 template <class C>
-__device__ __forceinline__ void process_item(const SampleParams& P, Smem<C>& sm, BlockRed<C::NW>& red,
-                                          int stage, int pos) {
+__device__ __forceinline__ void process_item(const SampleParams& P, Smem<C>& sm, int& slot, int stage, int pos) {
   const int tid = threadIdx.x;
   const int V = P.V;
   const int b = pos / P.L, l = pos - b * P.L;
   const int64_t base = (int64_t)b * P.stride_req + (int64_t)l * P.stride_pos;
-  const RowGeom gc = row_geom<C>(P, base);
-  const unsigned char* sc = sm.stage[stage];
-  const unsigned char* su = sm.stage[stage] + C::ROW_SLOT;
-  const bool cfg = (P.nb == 2);
-
-  // ---- registers: cond and uncond tiles ----
-  Tile<C> tc, tu;
-  const uint32_t edge = load_tile<C>(tc, sc, gc, V);
-  RowGeom gu;
-  if (cfg) {
-    gu = row_geom<C>(P, base + P.stride_branch);
-    if (gu.head == gc.head) load_tile<C>(tu, su, gu, V);
-    else load_tile_rephase<C>(tu, su, gu, gc, V);
-  }
-
-  // ---- sampling parameters ----
-  const float T = param_f(P.temperature, P.temperature_s, b);
+  RowRef<C> R;
+  R.sc = sm.stage[stage];
+  R.su = sm.stage[stage] + C::ROW_SLOT;
+  R.gc = row_geom<C>(P, base);
+  PosCtx X;
+  X.cfg = (P.nb == 2);
+  R.gu = X.cfg ? row_geom<C>(P, base + P.stride_branch) : R.gc;
+  // per-request parameters and the history bitmap: issue the loads first so
+  // their latency hides behind the tile loads and the first passes
+  X.T = param_f(P.temperature, P.temperature_s, b);
   const int topk_raw = param_i(P.top_k, P.top_k_s, b);
   const float top_p = param_f(P.top_p, P.top_p_s, b);
   const float min_p = param_f(P.min_p, P.min_p_s, b);
   const float rep = param_f(P.rep_penalty, P.rep_penalty_s, b);
-  const bool has_hist = P.history_kind != YAPD_HISTORY_NONE && P.history != nullptr;
-  const bool topk_on = topk_raw > 0 && topk_raw < V;
-  const bool topp_on = top_p < 1.0f;
-  const bool minp_on = min_p > 0.0f;
-  const bool pen_on = has_hist && rep != 1.0f;
-  const bool filtered = topk_on || topp_on || minp_on || pen_on;
-  const bool noisy = T > 0.0f || !P.zero_temp_greedy;
-  const bool scale = T > 0.0f;
-  const float rT = scale ? __fdiv_rn(1.0f, T) : 1.0f;
+  const bool pen_on = P.history_kind != YAPD_HISTORY_NONE && P.history != nullptr && rep != 1.0f;
+  const int hwords = (V + 31) >> 5;
+  uint32_t hword = 0u;
+  if (pen_on && tid < hwords) hword = history_word(P, b, tid);
+  X.scale = X.T > 0.0f;
+  X.rT = X.scale ? __fdiv_rn(1.0f, X.T) : 1.0f;
 
-  // ---- P1: row maxima ----
-  float mc_l = kNegInf, mu_l = kNegInf;
+  // ---- registers: cond and uncond tiles ----
+  Tile<C> tc, tu;
+  const uint32_t edge = load_tile<C>(tc, R.sc, R.gc, V);
+  if (X.cfg) {
+    if (R.gu.head == R.gc.head) load_tile<C>(tu, R.su, R.gu, V);
+    else load_tile_rephase<C>(tu, R.su, R.gu, R.gc, V);
+  }
+  const int vbase = tid * C::W - R.gc.head;
+
+  // ---- row maxima ----
+  const float2 ml = tile_max2<C>(tc, tu, X.cfg);
+  const float2 mx = red_max2<C>(ml.x, ml.y, sm, slot);
+  X.mc = mx.x;
+  X.mu = X.cfg ? mx.y : 0.f;
+
+  // ---- sums of exp(x - max) and z2 = log2(e)*guided/T - const ----
+  const float w = P.cfg_w;
+  const float sA = X.scale ? X.rT : 1.0f;
+  X.A2 = X.cfg ? __fmul_rn(__fmul_rn(kLog2e, P.cfg_1pw), sA) : __fmul_rn(kLog2e, sA);
+  X.B2 = X.cfg ? __fmul_rn(__fmul_rn(kLog2e, w), sA) : 0.f;
+  X.K2 = X.cfg ? __fmaf_rn(-X.mc, X.A2, __fmul_rn(X.mu, X.B2)) : __fmul_rn(-X.mc, X.A2);
+  const float mcL = __fmul_rn(X.mc, kLog2e), muL = __fmul_rn(X.mu, kLog2e);
+  float sc_t = 0.f, su_t = 0.f, zm_t = kNegInf;
+  float z2[C::NS];
 #pragma unroll
   for (int k = 0; k < C::NVT; ++k)
 #pragma unroll
     for (int i = 0; i < C::W; ++i) {
-      mc_l = fmaxf(mc_l, tc.get(k, i));
-      if (cfg) mu_l = fmaxf(mu_l, tu.get(k, i));
-    }
-  const float2 mx = red.max2(mc_l, mu_l);
-  const float mc = mx.x, mu = mx.y;
-
-  // ---- P2: sums of exp(x - max) ----
-  float sc_l = 0.f, su_l = 0.f;
-#pragma unroll
-  for (int k = 0; k < C::NVT; ++k)
-#pragma unroll
-    for (int i = 0; i < C::W; ++i) {
-      sc_l += ex2_approx(__fmul_rn(__fsub_rn(tc.get(k, i), mc), kLog2e));
-      if (cfg) su_l += ex2_approx(__fmul_rn(__fsub_rn(tu.get(k, i), mu), kLog2e));
-    }
-  const float2 sm2 = red.sum2(sc_l, su_l);
-  const float Sc = sm2.x, Su = sm2.y;
-  const float lc = logf(Sc), lu = logf(Su);
-
-  // ---- P3: guided / T for every element (exact op order of the reference) ----
-  float key[C::NS];
-#pragma unroll
-  for (int k = 0; k < C::NVT; ++k)
-#pragma unroll
-    for (int i = 0; i < C::W; ++i) {
-      float g;
-      if (cfg) {
-        const float lsc = __fsub_rn(__fsub_rn(tc.get(k, i), mc), lc);
-        const float lsu = __fsub_rn(__fsub_rn(tu.get(k, i), mu), lu);
-        g = __fadd_rn(lsc, __fmul_rn(P.cfg_w, __fsub_rn(lsc, lsu)));
-      } else {
-        g = tc.get(k, i);
+      const float c = tc.get(k, i);
+      sc_t += ex2_approx(__fmaf_rn(c, kLog2e, -mcL));
+      float u = 0.f;
+      if (X.cfg) {
+        u = tu.get(k, i);
+        su_t += ex2_approx(__fmaf_rn(u, kLog2e, -muL));
       }
-      key[k * C::W + i] = scale ? div_rn(g, T, rT) : g;
+      const float z = z2_of(X, c, u);
+      z2[k * C::W + i] = z;
+      zm_t = fmaxf(zm_t, z);
     }
   if (edge) {
 #pragma unroll
     for (int k = 0; k < C::NVT; ++k) {
       if (!((edge >> k) & 1u)) continue;
-      const int v0 = (tid + k * C::NT) * C::W - gc.head;
+      const int v0 = (tid + k * C::NT) * C::W - R.gc.head;
 #pragma unroll
       for (int i = 0; i < C::W; ++i) {
         const int v = v0 + i;
-        if (v < 0 || v >= V) key[k * C::W + i] = kNegInf;
+        if (v < 0 || v >= V) z2[k * C::W + i] = kNegInf;
       }
     }
   }
-  const int vbase = tid * C::W - gc.head;  // element id of slot (k, i) = vbase + k*NT*W + i
+  float s_t = 0.f;
+  if (zm_t > kNegInf) {
+#pragma unroll
+    for (int s = 0; s < C::NS; ++s) s_t += ex2_approx(__fsub_rn(z2[s], zm_t));
+  }
+  if (pen_on && tid < hwords) sm.hist[tid] = hword;
+  if (tid == 0) sm.misc[0] = 0;  // band counter, published by the next barrier
+  block_reduce_sums<C>(sc_t, su_t, zm_t, s_t, sm, slot);
+  X.Sc = sc_t;
+  X.Su = su_t;
+  X.zmax = zm_t;
+  X.S = s_t;
+  X.lc = logf(X.Sc);
+  X.lu = X.cfg ? logf(X.Su) : 0.f;
+  X.Kval = X.cfg ? __fmul_rn(__fsub_rn(__fmul_rn(w, X.lu), __fmul_rn(P.cfg_1pw, X.lc)), sA)
+                 : __fmul_rn(X.mc, sA);
 
-  // torch orders NaN above every number (sort, topk and argmax), so a row with
-  // a NaN value samples its lowest-id NaN token whatever the filters are.
-  bool nan_l = false;
-#pragma unroll
-  for (int s = 0; s < C::NS; ++s) nan_l |= !(key[s] == key[s]);
-  int chosen = 0;
-  if (__syncthreads_or(nan_l)) {
-    int first_nan = 0x7fffffff;
-#pragma unroll
-    for (int s = 0; s < C::NS; ++s) {
-      const int v = vbase + (s / C::W) * C::NT * C::W + (s % C::W);
-      if (v >= 0 && v < V && !(key[s] == key[s]) && v < first_nan) first_nan = v;
-    }
-    const unsigned long long w = red.max_u64((unsigned long long)(uint32_t)(0x7fffffff - first_nan));
-    chosen = 0x7fffffff - (int)(uint32_t)w;
-  } else if (!filtered) {
-    // ---- unfiltered: argmax(guided / T + G) in vocabulary order (engine.py:546-550) ----
-    ArgBest best{kNegInf, 0.f, 0x7fffffff};
-#pragma unroll
-    for (int k = 0; k < C::NVT; ++k)
-#pragma unroll
-      for (int i = 0; i < C::W; ++i) {
-        const int v = vbase + k * C::NT * C::W + i;
-        if (v < 0 || v >= V) continue;
-        float s = key[k * C::W + i];
-        if (noisy) s = __fadd_rn(s, token_noise(P, b, pos, l, v));
-        if (better(s, 0.f, v, best, false)) best = {s, 0.f, v};
-      }
-    // block argmax: largest score, then smallest id; NaN scores lose
-    const uint32_t sk = (best.score == best.score) ? ord_key(best.score) : 0u;
-    const unsigned long long packed =
-        ((unsigned long long)sk << 32) | (uint32_t)(0x7fffffff - (best.v > V ? V : best.v));
-    const unsigned long long win = red.max_u64(packed);
-    chosen = cand_id(win);
-    if (chosen >= V || chosen < 0) chosen = 0;
+  // ---- token choice ----
+  const bool topk_on = topk_raw > 0 && topk_raw < V;
+  const bool topp_on = top_p < 1.0f;
+  const bool minp_on = min_p > 0.0f;
+  ScoreCtx K;
+  K.hist = sm.hist;
+  K.b = b;
+  K.pos = pos;
+  K.l = l;
+  K.pen_on = pen_on;
+  K.noisy = X.T > 0.0f || !P.zero_temp_greedy;
+  K.turbo = topk_on || topp_on || minp_on || K.pen_on;
+  K.minp_on = false;
+  K.rep = rep;
+  K.rrep = K.pen_on ? __fdiv_rn(1.0f, rep) : 1.0f;
+  K.r = __fdiv_rn(1.0f, X.S);
+  K.minp_thr = 0.f;
+
+  int chosen;
+  const Pick none{kNegInf, kNegInf, 0x7fffffff};
+  if (!(X.Sc == X.Sc) || (X.cfg && !(X.Su == X.Su))) {
+    chosen = 0;  // a NaN/+inf logit makes the whole reference row NaN: argmax -> 0
+  } else if (!(X.S == X.S)) {
+    const int f = first_nan_or_inf<C>(X, R, V, sm, slot);
+    chosen = f < 0 ? 0 : f;
   } else if (!topk_on && !topp_on && !minp_on) {
-    // ---- penalty only: every token kept; order ties by (vals desc, id asc) ----
-    const float rrep = __fdiv_rn(1.0f, rep);
-    ArgBest best{kNegInf, kNegInf, 0x7fffffff};
-#pragma unroll
-    for (int k = 0; k < C::NVT; ++k)
-#pragma unroll
-      for (int i = 0; i < C::W; ++i) {
-        const int v = vbase + k * C::NT * C::W + i;
-        if (v < 0 || v >= V) continue;
-        const float kv = key[k * C::W + i];
-        float s = history_has(P, b, v) ? penalize(kv, rep, rrep) : kv;
-        if (noisy) s = __fadd_rn(s, token_noise(P, b, pos, l, v));
-        if (better(s, kv, v, best, true)) best = {s, kv, v};
-      }
-    // two-stage reduction: first the best score, then the order key among equal scores
-    const uint32_t sk = (best.score == best.score) ? ord_key(best.score) : 0u;
-    const unsigned long long w1 = red.max_u64(((unsigned long long)sk << 32) | ord_key(best.tb));
-    const bool tie = ((unsigned long long)sk << 32 | ord_key(best.tb)) == w1;
-    const unsigned long long w2 =
-        red.max_u64(tie ? (unsigned long long)(uint32_t)(0x7fffffff - best.v) : 0ull);
-    chosen = 0x7fffffff - (int)(uint32_t)w2;
-    if (chosen >= V || chosen < 0) chosen = 0;
+    // every token kept: server/engine.py:546-550 (or the penalty-only chain)
+    chosen = argmax_regs<C>(P, X, R, z2, vbase, -kBig, K, none, sm, slot);
+    if (chosen < 0) chosen = 0;
   } else {
-    chosen = filtered_select<C>(P, sm, red, key, vbase, b, pos, l, topk_raw, top_p, min_p, rep,
-                                topk_on, topp_on, minp_on, pen_on, noisy);
+    chosen = -1;
+    if (minp_on && !topk_on) {
+      const float zm = fminf(__fadd_rn(X.zmax, log2f(min_p)), X.zmax);
+      const int n = band_regs<C>(P, X, R, z2, vbase, __fsub_rn(zm, zmargin(zm)), sm);
+      if (n <= 32) {
+        if (tid < 32) {
+          const int c = band_warp_choose<C>(P, X, R, K, n, topp_on, top_p, true, min_p, sm);
+          if (tid == 0) sm.misc[1] = c;
+        }
+        __syncthreads();
+        chosen = sm.misc[1];
+      } else if (n <= C::BAND) {
+        rank_sort<C>(n, sm);
+        Band bd;
+        bd.n = n;
+        bd.H = kBig;
+        bd.n_above = 0.f;
+        bd.m_above = 0.f;
+        bd.overflow = false;
+        const float minp_thr = __fmul_rn(min_p, __fmul_rn(sm.cande[0], K.r));
+        band_flags<C>(bd, false, 0, topp_on, top_p, K.r, true, minp_thr, sm);
+        const Pick bp = band_pick<C>(P, K, bd.n, sm);
+        chosen = block_pick<C>(bp, true, sm, slot);
+        if (chosen < 0) chosen = cand_id(sm.cand[0]);
+      }
+    }
+    if (chosen < 0) {
+      K.minp_on = minp_on;
+      chosen = select_cold<C>(P, X, R, K, topk_raw, topk_on, topp_on, top_p, min_p, sm, slot);
+    }
   }
-
   if (chosen < 0 || chosen >= V) {
     if (tid == 0) atomicOr(P.status, (unsigned)YAPD_STATUS_INTERNAL);
     chosen = 0;
   }
-  // ---- PMI of the chosen token (engine.py:553-558) ----
+  // ---- softmax(c)[s] and softmax(u)[s] of the chosen token (server/engine.py:539-540,
+  // 553, 556); the unmask kernel turns them into the PMI ----
   if (tid == 0) {
     P.sampled[pos] = chosen;
-    if (P.want_pmi) {
-      const float cv = load_elem_smem<C>(sc, gc, chosen);
-      const float rc = __fdiv_rn(1.0f, Sc);
-      const float pc = __fmul_rn(expf(__fsub_rn(cv, mc)), rc);
-      const float lp = __ldg(P.log_prior + chosen);
-      const float lpl = __fmul_rn(P.pmi_lambda, lp);
-      float pmi = __fsub_rn(logf(fmaxf(pc, 1e-8f)), lpl);
-      if (cfg) {
-        const float uv = load_elem_smem<C>(su, gu, chosen);
-        const float ru = __fdiv_rn(1.0f, Su);
-        const float pu = __fmul_rn(expf(__fsub_rn(uv, mu)), ru);
-        const float pmi_u = __fsub_rn(logf(fmaxf(pu, 1e-8f)), lpl);
-        pmi = __fsub_rn(__fmul_rn(P.cfg_1pw, pmi), __fmul_rn(P.cfg_w, pmi_u));
+    if (P.pcu) {
+      const float cv = load_elem_smem<C>(R.sc, R.gc, chosen);
+      const float pc = __fmul_rn(expf(__fsub_rn(cv, X.mc)), __fdiv_rn(1.0f, X.Sc));
+      float pu = 0.f;
+      if (X.cfg) {
+        const float uv = load_elem_smem<C>(R.su, R.gu, chosen);
+        pu = __fmul_rn(expf(__fsub_rn(uv, X.mu)), __fdiv_rn(1.0f, X.Su));
       }
-      P.pmi[pos] = pmi;
+      P.pcu[pos] = make_float2(pc, pu);
     }
   }
 }
@@ -935,7 +1327,7 @@ __global__ void __launch_bounds__(C::NT, C::MINB) sample_kernel(const SamplePara
     for (int s = 0; s < C::NSTAGE && s < n_my; ++s)
       issue_item<C>(P, sm, s, item_pos<C>(P, first + s * stride));
   }
-  BlockRed<C::NW> red{sm.redf, sm.redd, sm.redi, 0};
+  int slot = 0;
   for (int it = 0; it < n_my; ++it) {
     const int stage = it % C::NSTAGE;
     const uint32_t parity = (uint32_t)(it / C::NSTAGE) & 1u;
@@ -951,8 +1343,9 @@ __global__ void __launch_bounds__(C::NT, C::MINB) sample_kernel(const SamplePara
       __syncthreads();
       return;
     }
-    process_item<C>(P, sm, red, stage, item_pos<C>(P, first + it * stride));
-    __syncthreads();
+    process_item<C>(P, sm, slot, stage, item_pos<C>(P, first + it * stride));
+    // Every thread but 0 finished reading this stage before the item's last
+    // barrier; thread 0's own reads precede the refill in program order.
     if (threadIdx.x == 0 && it + C::NSTAGE < n_my) {
       fence_proxy_async_smem();
       issue_item<C>(P, sm, stage, item_pos<C>(P, first + (it + C::NSTAGE) * stride));
@@ -980,6 +1373,10 @@ struct UnmaskParams {
   const int64_t* sched_t;
   const float* q_t;
   const int32_t* sampled;
+  const float2* pcu;
+  const float* log_prior;
+  float pmi_lambda, cfg_w, cfg_1pw;
+  int nb;
   float* pmi;
   const float* gumbel_pos;
   int noise_kind;
@@ -1015,10 +1412,20 @@ __global__ void unmask_kernel(const UnmaskParams U) {
   const int64_t ks = U.k_step[b];
   int kc = (int)(ks < (int64_t)(K - 1) ? ks : (int64_t)(K - 1));
   if (kc < 0) kc = 0;
-  // ranked PMI: position noise on masked positions (engine.py:559-561)
+  // PMI of the sampled token (server/engine.py:553-558, calibration.py:58-60)
+  // and the position noise on masked positions (server/engine.py:559-561)
   float pm = 0.f;
+  const int smp = in ? U.sampled[p] : -1;
+  if (smp >= 0) {
+    const float2 pr = U.pcu[p];
+    const float lpl = __fmul_rn(U.pmi_lambda, __ldg(U.log_prior + smp));
+    pm = __fsub_rn(logf(fmaxf(pr.x, 1e-8f)), lpl);
+    if (U.nb == 2) {
+      const float pmi_u = __fsub_rn(logf(fmaxf(pr.y, 1e-8f)), lpl);
+      pm = __fsub_rn(__fmul_rn(U.cfg_1pw, pm), __fmul_rn(U.cfg_w, pmi_u));
+    }
+  }
   if (is_mask) {
-    pm = U.pmi[p];
     if (U.pos_noise) {
       const float gn = (U.noise_kind == YAPD_NOISE_EXPLICIT)
                            ? U.gumbel_pos[p]
@@ -1073,7 +1480,7 @@ __global__ void unmask_kernel(const UnmaskParams U) {
   if (denoise && do_un) xf = (int64_t)U.sampled[p];
   if (in) {
     U.xt_out[p] = xf;
-    if (is_mask) U.pmi[p] = pm;
+    if (smp >= 0) U.pmi[p] = pm;
   }
   const int n_after = __popc(__ballot_sync(0xffffffffu, in && xf == U.mask_id));
   const bool eos = __any_sync(0xffffffffu, in && xf == U.stop_id);
@@ -1208,7 +1615,8 @@ const char* yapd_status_string(int code) {
 
 size_t yapd_select_workspace_size(int32_t B, int32_t L) {
   if (B <= 0 || L <= 0) return 256;
-  return 256 + align256((size_t)B * (size_t)L * sizeof(int32_t));
+  const size_t n = (size_t)B * (size_t)L;
+  return 256 + align256(n * sizeof(int32_t)) + align256(n * sizeof(float2));
 }
 
 size_t yapd_sample_workspace_size(int32_t R) {
@@ -1270,13 +1678,10 @@ int yapd_select_step(const yapd_select_args* a, void* stream) {
   P.work_count = reinterpret_cast<int32_t*>(ws + 4);
   P.work = reinterpret_cast<int32_t*>(ws + 256);
   P.n_identity = 0;
-  P.log_prior = a->log_prior;
   P.cfg_w = a->cfg_scale;
   P.cfg_1pw = a->cfg_one_plus;
-  P.pmi_lambda = a->pmi_lambda;
-  P.want_pmi = 1;
   P.sampled = a->sampled;
-  P.pmi = a->pmi;
+  P.pcu = reinterpret_cast<float2*>(ws + 256 + align256((size_t)a->B * a->L * sizeof(int32_t)));
 
   cudaStream_t st = (cudaStream_t)stream;
   const int total = a->B * a->L;
@@ -1296,6 +1701,12 @@ int yapd_select_step(const yapd_select_args* a, void* stream) {
   U.sched_t = a->sched_t;
   U.q_t = a->q_t;
   U.sampled = a->sampled;
+  U.pcu = P.pcu;
+  U.log_prior = a->log_prior;
+  U.pmi_lambda = a->pmi_lambda;
+  U.cfg_w = a->cfg_scale;
+  U.cfg_1pw = a->cfg_one_plus;
+  U.nb = a->nb;
   U.pmi = a->pmi;
   U.gumbel_pos = a->noise.gumbel_pos;
   U.noise_kind = a->noise.kind;
@@ -1345,10 +1756,8 @@ int yapd_sample_rows(const yapd_sample_args* a, void* stream) {
   P.work = nullptr;
   P.work_count = nullptr;
   P.n_identity = a->R;
-  P.log_prior = nullptr;
-  P.want_pmi = 0;
   P.sampled = a->sampled;
-  P.pmi = nullptr;
+  P.pcu = nullptr;
   return launch_sample(P, a->logits_dtype, a->R, (cudaStream_t)stream);
 }
 

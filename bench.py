@@ -1,0 +1,481 @@
+#!/usr/bin/env python
+"""Benchmark of the block-diffusion select step: logit rows/sec at V = 8194.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 1|3]
+
+One *step* is one select step (m8than/yapd ``server/engine.py:533-612``) over one
+GPU's batch: configuration 1 by default (64 requests x 2 CFG rows x 32 positions
+x V = 8194 bf16 logits, T 0.8, top-p 0.95, min-p 0.05, repetition penalty 1.2
+over a 256-token history, Philox Gumbel noise), run as 8-step diffusion blocks:
+the block state (masked positions, step counter, commit flag) evolves through
+the kernel's own outputs and is reset at each block start.  A logit row is
+counted when the step must read it (masked position of a non-commit request),
+the metric of the reference's tick.
+
+Under ``torchrun`` each rank runs its own request shard (weak scaling, no
+per-step collective); ranks gather their committed tokens with one NCCL
+all-gather after timing.  Device time is the max over ranks.
+
+Prints one JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from yapd_b200 import select as S  # noqa: E402
+from yapd_b200 import workloads as WL  # noqa: E402
+
+METRIC = "logit rows/sec at V=8194"
+N_BUFFERS = 5  # rotating logits buffers, total well above the 126 MB L2
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=8000)
+    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3])
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=16)
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------- dist
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def dist_init(ws, local):
+    if ws > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        return dist
+    torch.cuda.set_device(local)
+    return None
+
+
+# --------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "50", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], [], set()
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax),
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ------------------------------------------------------------------ workload
+
+def config_name(cfg: int) -> str:
+    return {1: "config1", 2: "config2", 3: "config3"}[cfg]
+
+
+def make_inputs(cfg: int, rank: int, device):
+    """The per-GPU shard: config defaults, Philox noise (production mode)."""
+    inp = WL.make_config(cfg, seed=100 + rank, explicit_noise=False)
+    g = torch.Generator(device=device).manual_seed(7 + 131 * rank)
+    bufs = [inp.logits.to(device)]
+    for _ in range(N_BUFFERS - 1):
+        x = torch.randn(inp.logits.shape, generator=g, device=device) * 2.0
+        idx = torch.randint(0, inp.V, (*inp.logits.shape[:2], 3), generator=g, device=device)
+        x.scatter_add_(2, idx, torch.full(idx.shape, 8.0, device=device))
+        bufs.append(x.to(inp.logits.dtype))
+    return inp, bufs
+
+
+class Runner:
+    """Eight captured graphs, one per diffusion step of a block."""
+
+    def __init__(self, inp, bufs, device):
+        self.inp, self.bufs, self.dev = inp, bufs, device
+        B, L = inp.B, inp.L
+        self.xt0 = torch.full((B, L), inp.mask_id, dtype=torch.int64, device=device)
+        self.k0 = torch.zeros(B, dtype=torch.int64, device=device)
+        self.c0 = torch.zeros(B, dtype=torch.bool, device=device)
+        self.xt = self.xt0.clone()
+        self.k = self.k0.clone()
+        self.c = self.c0.clone()
+        o = S.SelectOutputs.empty(B, L, device)
+        self.out = S.SelectOutputs(xt=self.xt, sampled=o.sampled, pmi=o.pmi, n_unmask=o.n_unmask,
+                                   n_mask_after=o.n_mask_after, hit_eos=o.hit_eos, k_step=self.k,
+                                   is_commit=self.c)
+        self.kw = dict(cfg_scale=inp.cfg_scale, mask_id=inp.mask_id, stop_id=inp.stop_id,
+                       temperature=inp.temperature.to(device), top_k=inp.top_k.to(device),
+                       top_p=inp.top_p.to(device), min_p=inp.min_p.to(device),
+                       rep_penalty=inp.rep_penalty.to(device),
+                       history=inp.history_bitmap().to(device), pmi_lambda=inp.pmi_lambda,
+                       pos_noise=True, use_quantile=True)
+        self.lp = inp.log_prior.to(device)
+        self.sched = inp.sched_t.to(device)
+        self.q = inp.q_t.to(device)
+        self.K = inp.num_steps
+        self.ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(self.K)]
+        for a, b in self.ev:  # torch creates the CUDA events lazily, on first record
+            a.record()
+            b.record()
+        torch.cuda.synchronize()
+        self.graphs = []
+
+    def step(self, k: int, prof: bool = True):
+        if k == 0:
+            self.xt.copy_(self.xt0)
+            self.k.copy_(self.k0)
+            self.c.copy_(self.c0)
+        S.select_step(self.bufs[k % len(self.bufs)], self.xt, self.k, self.c, self.lp, self.sched,
+                      self.q, seed=1234, offset=k, out=self.out,
+                      prof_events=self.ev[k] if prof else None, **self.kw)
+
+    def rows_per_step(self):
+        """Sampled positions per step index, from one eager block."""
+        pos = []
+        for k in range(self.K):
+            if k == 0:
+                masked = self.inp.B * self.inp.L
+            else:
+                masked = int(((self.xt == self.inp.mask_id) & ~self.c[:, None]).sum())
+            self.step(k, prof=False)
+            pos.append(masked)
+        torch.cuda.synchronize()
+        return pos
+
+    def capture(self):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for k in range(self.K):
+                self.step(k)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        for k in range(self.K):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.step(k)
+            self.graphs.append(g)
+        torch.cuda.synchronize()
+
+
+def event_ms(e0, e1) -> float:
+    """Elapsed time between two events recorded by the library (inside a graph,
+    so torch's own bookkeeping does not know them)."""
+    from cuda.bindings import runtime as rt
+    err, ms = rt.cudaEventElapsedTime(rt.cudaEvent_t(e0.cuda_event), rt.cudaEvent_t(e1.cuda_event))
+    if int(err) != 0:
+        raise RuntimeError(f"cudaEventElapsedTime failed: {err}")
+    return float(ms)
+
+
+def algorithmic_bytes(inp, positions: int) -> int:
+    return WL.algorithmic_bytes(inp, 2 * positions, positions, explicit_noise=False)
+
+
+def roofline_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def committed_traffic(cfg: int):
+    """DRAM bytes per sample-kernel launch from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d.get(config_name(cfg))
+    except Exception:
+        return None
+
+
+# ------------------------------------------------------------ CPU baselines
+
+def cpu_sample(cfg: int, seconds: float, B_s: int = 2):
+    """The CPU oracle (the reference algorithm, torch CPU, all host cores) on a
+    bounded sample of the same workload: B_s requests, all positions masked."""
+    from oracle import select_oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    inp = WL.make_config(cfg, seed=999, B=B_s, explicit_noise=False)
+    rows = 2 * inp.B * inp.L
+    O.select_step(inp, noise="philox", seed=1, offset=0)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        O.select_step(inp, noise="philox", seed=1, offset=n)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return {"value": rows * n / el, "unit": "rows/s", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"{config_name(cfg)} shape with B={B_s} requests, all "
+            f"{inp.L} positions masked, {n} steps in {el:.1f} s (torch CPU oracle)"}, el / n, rows
+
+
+# ----------------------------------------------------------------- main arms
+
+def run_reference(args, ws, rank):
+    if ws > 1 and rank != 0:
+        return
+    B_s = 4
+    from oracle import select_oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    inp = WL.make_config(args.config, seed=999, B=B_s, explicit_noise=False)
+    rows = 2 * inp.B * inp.L
+    for i in range(args.warmup):
+        O.select_step(inp, noise="philox", seed=1, offset=i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        O.select_step(inp, noise="philox", seed=1, offset=i)
+    el = time.perf_counter() - t0
+    v = rows * args.steps / el
+    cb = {"value": v, "unit": "rows/s", "cores": torch.get_num_threads(), "kind": "port",
+          "sample": f"{config_name(args.config)} shape with B={B_s} requests per step, all positions "
+                    f"masked (torch CPU oracle of server/engine.py:533-612)"}
+    line = {"metric": METRIC, "value": v, "unit": "rows/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": f"{config_name(args.config)} (CPU sample, B={B_s})",
+                       "parallelism": "host cores"},
+            "cpu_baseline": cb,
+            "e2e": {"value": v, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, ws, rank, local):
+    dist = dist_init(ws, local)
+    dev = torch.device("cuda", local)
+    cfg = args.config
+    inp, bufs = make_inputs(cfg, rank, dev)
+    R = Runner(inp, bufs, dev)
+    positions = R.rows_per_step()
+    R.capture()
+    K = R.K
+    # warm-up
+    for i in range(args.warmup):
+        R.graphs[i % K].replay()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0.record()
+    for i in range(args.steps):
+        R.graphs[(args.warmup + i) % K].replay()
+    e1.record()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    ck = clocks.stop()
+    # sample-kernel time of each step index (last replay of each graph)
+    kern_ms = [event_ms(*R.ev[k]) for k in range(K)]
+    my_rows = sum(2 * positions[(args.warmup + i) % K] for i in range(args.steps))
+    byt = [algorithmic_bytes(inp, positions[k]) for k in range(K)]
+    achieved = sum(byt) / (sum(kern_ms) * 1e-3) / 1e9
+    if dist:
+        t = torch.tensor([ms, float(my_rows)], device=dev, dtype=torch.float64)
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm_ = t.clone()
+        dist.all_reduce(sm_, op=dist.ReduceOp.SUM)
+        ms_max, rows_all = float(mx[0]), float(sm_[1])
+        # final gather of the committed block tokens (the only collective)
+        gathered = [torch.empty_like(R.xt) for _ in range(ws)]
+        dist.all_gather(gathered, R.xt)
+        torch.cuda.synchronize()
+    else:
+        ms_max, rows_all = ms, float(my_rows)
+    value = rows_all / (ms_max * 1e-3)
+
+    # ---- end to end through the public API with host buffers ----
+    e2e = run_e2e(R, inp, dev, args.e2e_steps)
+    if dist:
+        t = torch.tensor([e2e["ms"]], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t[0])
+        e2e_rows = rows_all / args.steps * args.e2e_steps
+    else:
+        e2e_ms, e2e_rows = e2e["ms"], e2e["rows"]
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        cpu, _, _ = cpu_sample(cfg, args.cpu_seconds)
+
+    if rank == 0:
+        peak, peak_kind = roofline_peak()
+        traffic = committed_traffic(cfg)
+        line = {
+            "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16" if inp.logits.dtype == torch.bfloat16 else "f32",
+            "data": "synthetic",
+            "config": {
+                "workload": f"{config_name(cfg)}: {inp.B} requests x 2 CFG rows x {inp.L} positions x "
+                            f"V={inp.V} per GPU, {K}-step diffusion blocks, sparse (masked, non-commit) rows",
+                "global_batch": inp.B * ws, "seq_len": inp.L, "parallelism": f"request-sharded x{ws}",
+                "l2": f"{N_BUFFERS} rotating logits buffers ({N_BUFFERS * inp.logits.numel() * inp.logits.element_size() / 1e6:.0f} MB) > L2",
+                "noise": "in-kernel Philox4x32-10 Gumbel",
+                "rows_per_step_mean": rows_all / args.steps / ws,
+            },
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
+                         "kernel": "sample_kernel", "kernel_ms_per_launch": sum(kern_ms) / K,
+                         "bytes_per_launch": sum(byt) / K},
+            "e2e": {"value": e2e_rows / (e2e_ms * 1e-3), "unit": "rows/s",
+                    "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"]},
+            "gpu_launches": 4 * args.steps,
+            "clocks": ck,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if dist:
+        del R
+        dist.destroy_process_group()
+
+
+def run_e2e(R, inp, dev, steps):
+    """Same metric through select_step with host buffers: every step copies its
+    logits and block state host->device and reads the new state back (the one
+    device->host sync of the engine tick, server/engine.py:635-636)."""
+    K = R.K
+    pin = [b.cpu().pin_memory() for b in R.bufs[:2]]
+    dlog = torch.empty_like(R.bufs[0])
+    hx = R.xt0.cpu().pin_memory()
+    hk = R.k0.cpu().pin_memory()
+    hc = R.c0.cpu().pin_memory()
+    ox = torch.empty_like(hx).pin_memory()
+    ok_ = torch.empty_like(hk).pin_memory()
+    oc = torch.empty_like(hc).pin_memory()
+    on = torch.empty(inp.B, dtype=torch.int32).pin_memory()
+    oe = torch.empty(inp.B, dtype=torch.bool).pin_memory()
+    dx, dk, dc = R.xt0.clone(), R.k0.clone(), R.c0.clone()
+    o = S.SelectOutputs.empty(inp.B, inp.L, dev)
+    out = S.SelectOutputs(xt=dx, sampled=o.sampled, pmi=o.pmi, n_unmask=o.n_unmask,
+                          n_mask_after=o.n_mask_after, hit_eos=o.hit_eos, k_step=dk, is_commit=dc)
+    xt0 = R.xt0.cpu()
+
+    def tick(i):
+        k = i % K
+        if k == 0:
+            hx.copy_(xt0)
+            hk.zero_()
+            hc.zero_()
+        rows = 2 * int(((hx == inp.mask_id) & ~hc[:, None]).sum())
+        dlog.copy_(pin[i % 2], non_blocking=True)
+        dx.copy_(hx, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dc.copy_(hc, non_blocking=True)
+        S.select_step(dlog, dx, dk, dc, R.lp, R.sched, R.q, seed=99, offset=k, out=out, **R.kw)
+        ox.copy_(dx, non_blocking=True)
+        ok_.copy_(dk, non_blocking=True)
+        oc.copy_(dc, non_blocking=True)
+        on.copy_(o.n_mask_after, non_blocking=True)
+        oe.copy_(o.hit_eos, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        hx.copy_(ox)
+        hk.copy_(ok_)
+        hc.copy_(oc)
+        return rows
+
+    for i in range(2):
+        tick(i)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    rows = 0
+    for i in range(steps):
+        rows += tick(i)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    h2d = dlog.numel() * dlog.element_size() + hx.numel() * 8 + hk.numel() * 8 + hc.numel()
+    d2h = ox.numel() * 8 + ok_.numel() * 8 + oc.numel() + on.numel() * 4 + oe.numel()
+    return {"ms": ms, "rows": rows, "h2d": h2d, "d2h": d2h}
+
+
+def main():
+    args = parse()
+    ws, rank, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, ws, rank)
+        return
+    run_ours(args, ws, rank, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -139,6 +139,10 @@ typedef struct yapd_select_args {
   uint8_t* is_commit_out;       /* (B,) may alias is_commit */
   void* workspace;
   size_t workspace_bytes;
+  /* optional cudaEvent_t pair recorded on `stream` around the sampling
+   * kernel (the step's dominant kernel), for roofline timing; NULL = none */
+  void* prof_event_begin;
+  void* prof_event_end;
 } yapd_select_args;
 
 /* Rows for TurboEngine._sample: logits (R, V) with row stride `stride_row`. */

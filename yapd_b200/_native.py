@@ -65,6 +65,7 @@ class SelectArgs(C.Structure):
         ("n_unmask", C.c_void_p), ("n_mask_after", C.c_void_p), ("hit_eos", C.c_void_p),
         ("k_step_out", C.c_void_p), ("is_commit_out", C.c_void_p),
         ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
+        ("prof_event_begin", C.c_void_p), ("prof_event_end", C.c_void_p),
     ]
 
 

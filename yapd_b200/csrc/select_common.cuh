@@ -120,150 +120,6 @@ __device__ __forceinline__ int warp_sum_i(int v) {
   return v;
 }
 
-// Block-wide reductions over NW warps through a two-slot ping-pong scratch,
-// one __syncthreads each.  Every thread receives the result.
-template <int NW>
-struct BlockRed {
-  float* f;    // [2][4][NW]
-  double* d;   // [2][2][NW]
-  int* i;      // [2][4][NW]
-  int slot;
-
-  __device__ __forceinline__ float2 max2(float a, float b) {
-    a = warp_max(a);
-    b = warp_max(b);
-    float* s = f + slot * 4 * NW;
-    slot ^= 1;
-    const int w = threadIdx.x >> 5;
-    if ((threadIdx.x & 31) == 0) {
-      s[w] = a;
-      s[NW + w] = b;
-    }
-    __syncthreads();
-    float ra = s[0], rb = s[NW];
-#pragma unroll
-    for (int k = 1; k < NW; ++k) {
-      ra = fmaxf(ra, s[k]);
-      rb = fmaxf(rb, s[NW + k]);
-    }
-    return make_float2(ra, rb);
-  }
-  __device__ __forceinline__ float2 sum2(float a, float b) {
-    a = warp_sum(a);
-    b = warp_sum(b);
-    float* s = f + slot * 4 * NW;
-    slot ^= 1;
-    const int w = threadIdx.x >> 5;
-    if ((threadIdx.x & 31) == 0) {
-      s[w] = a;
-      s[NW + w] = b;
-    }
-    __syncthreads();
-    float ra = 0.f, rb = 0.f;
-#pragma unroll
-    for (int k = 0; k < NW; ++k) {
-      ra += s[k];
-      rb += s[NW + k];
-    }
-    return make_float2(ra, rb);
-  }
-  // Sum of two doubles and two ints.
-  __device__ __forceinline__ void sum_mixed(double& a, double& b, int& c, int& e) {
-    a = warp_sum_d(a);
-    b = warp_sum_d(b);
-    c = warp_sum_i(c);
-    e = warp_sum_i(e);
-    double* sd = d + slot * 2 * NW;
-    int* si = i + slot * 4 * NW;
-    slot ^= 1;
-    const int w = threadIdx.x >> 5;
-    if ((threadIdx.x & 31) == 0) {
-      sd[w] = a;
-      sd[NW + w] = b;
-      si[w] = c;
-      si[NW + w] = e;
-    }
-    __syncthreads();
-    double ra = 0.0, rb = 0.0;
-    int rc = 0, re = 0;
-#pragma unroll
-    for (int k = 0; k < NW; ++k) {
-      ra += sd[k];
-      rb += sd[NW + k];
-      rc += si[k];
-      re += si[NW + k];
-    }
-    a = ra;
-    b = rb;
-    c = rc;
-    e = re;
-  }
-  // Four int sums.
-  __device__ __forceinline__ int4 sum4i(int4 v) {
-    v.x = warp_sum_i(v.x);
-    v.y = warp_sum_i(v.y);
-    v.z = warp_sum_i(v.z);
-    v.w = warp_sum_i(v.w);
-    int* s = i + slot * 4 * NW;
-    slot ^= 1;
-    const int w = threadIdx.x >> 5;
-    if ((threadIdx.x & 31) == 0) {
-      s[w] = v.x;
-      s[NW + w] = v.y;
-      s[2 * NW + w] = v.z;
-      s[3 * NW + w] = v.w;
-    }
-    __syncthreads();
-    int4 r = make_int4(0, 0, 0, 0);
-#pragma unroll
-    for (int k = 0; k < NW; ++k) {
-      r.x += s[k];
-      r.y += s[NW + k];
-      r.z += s[2 * NW + k];
-      r.w += s[3 * NW + k];
-    }
-    return r;
-  }
-  // Lexicographic max of (hi, lo) 64-bit keys packed as unsigned long long.
-  __device__ __forceinline__ unsigned long long max_u64(unsigned long long v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const unsigned long long x = __shfl_xor_sync(0xffffffffu, v, o);
-      v = x > v ? x : v;
-    }
-    unsigned long long* s = reinterpret_cast<unsigned long long*>(d + slot * 2 * NW);
-    slot ^= 1;
-    const int w = threadIdx.x >> 5;
-    if ((threadIdx.x & 31) == 0) s[w] = v;
-    __syncthreads();
-    unsigned long long r = s[0];
-#pragma unroll
-    for (int k = 1; k < NW; ++k) r = s[k] > r ? s[k] : r;
-    return r;
-  }
-};
-
-// Bitonic sort of n (power of two, n <= 32 * blockDim-limited) u64 keys in
-// shared memory, DESCENDING; all threads of the block take part.
-__device__ __forceinline__ void block_bitonic_desc(unsigned long long* a, int n, int nthreads) {
-  for (int k = 2; k <= n; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int t = threadIdx.x; t < n; t += nthreads) {
-        const int p = t ^ j;
-        if (p > t) {
-          const unsigned long long x = a[t], y = a[p];
-          const bool desc = (t & k) == 0;
-          if (desc ? (x < y) : (x > y)) {
-            a[t] = y;
-            a[p] = x;
-          }
-        }
-      }
-      __syncthreads();
-    }
-  }
-}
-
 // Bitonic sort of one value per lane across a warp, DESCENDING.
 __device__ __forceinline__ unsigned long long warp_bitonic_desc(unsigned long long x) {
   const int lane = threadIdx.x & 31;
@@ -296,6 +152,19 @@ __device__ __forceinline__ float warp_bitonic_asc_f(float x) {
     }
   }
   return x;
+}
+
+}  // namespace yapd
+
+namespace yapd {
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Named barrier `id` over `count` threads (a multiple of the warp size).
+__device__ __forceinline__ void named_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 }  // namespace yapd

@@ -30,7 +30,7 @@ namespace yapd {
 
 template <int NT_, int NVT_, int W_, int ELEM_, int NSTAGE_, int CAP_, int MINB_>
 struct KCfg {
-  static constexpr int NT = NT_;        // threads per CTA
+  static constexpr int NT = NT_;        // compute threads per CTA (plus one producer warp)
   static constexpr int NVT = NVT_;      // 16-byte vectors per thread per row
   static constexpr int W = W_;          // elements per 16-byte vector
   static constexpr int ELEM = ELEM_;    // bytes per logit
@@ -44,8 +44,8 @@ struct KCfg {
   static constexpr bool BF16 = (ELEM == 2);
   static_assert(NT * NVT * 16 >= YAPD_MAX_V * ELEM + 32, "row does not fit the thread tile");
 };
-using CfgBF16 = KCfg<256, 5, 8, 2, 3, 512, 2>;
-using CfgF32 = KCfg<512, 5, 4, 4, 3, 1024, 1>;
+using CfgBF16 = KCfg<224, 5, 8, 2, 3, 0, 2>;
+using CfgF32 = KCfg<480, 5, 4, 4, 3, 0, 1>;
 
 constexpr uint64_t kWaitLimitNs = 500ull * 1000ull * 1000ull;  // 0.5 s per pipeline wait
 constexpr float kMinPMargin = 1e-3f;
@@ -150,18 +150,10 @@ __device__ __forceinline__ int cand_id(unsigned long long c) { return 0x7fffffff
 __device__ __forceinline__ float cand_val(unsigned long long c) { return ord_key_inv((uint32_t)(c >> 32)); }
 
 // Shared memory layout.
+struct StageAux;
+
 template <class C>
-struct Smem {
-  uint64_t full[C::NSTAGE];
-  float red8[2 * 8 * C::NW];
-  unsigned long long redu[2 * C::NW];
-  int misc[8];
-  unsigned long long cand[C::BAND];
-  float cande[C::BAND];
-  unsigned char cflag[C::BAND];
-  uint32_t hist[(YAPD_MAX_V + 31) / 32 + 1];
-  alignas(128) unsigned char stage[C::NSTAGE][C::STAGE_BYTES];
-};
+struct Smem;
 
 // Per-thread register tile of one row: NVT vectors of W elements, kept as
 // raw 16-byte words (bf16 pairs or fp32).
@@ -358,6 +350,27 @@ __device__ __forceinline__ int item_pos(const SampleParams& P, int idx) {
   return P.n_identity > 0 ? idx : P.work[idx];
 }
 
+// Barrier over the compute warps only (the producer/finisher warp never joins).
+template <class C>
+__device__ __forceinline__ void csync() {
+  named_sync(1, C::NT);
+}
+
+// OR of a predicate over the compute warps (one barrier).
+template <class C>
+__device__ __forceinline__ bool csync_or(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "barrier.cta.red.or.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "n"(C::NT)
+      : "memory");
+  return r != 0;
+}
+
 // ------------------------------------------------------------ per-position core
 //
 // Hot path (registers, fully unrolled): row maxima, the sums of exp(x - max),
@@ -433,7 +446,7 @@ __device__ __forceinline__ float2 red_max2(float a, float c, Smem<C>& sm, int& s
     s[threadIdx.x >> 5] = a;
     s[C::NW + (threadIdx.x >> 5)] = c;
   }
-  __syncthreads();
+  csync<C>();
   float ra = s[0], rc = s[C::NW];
 #pragma unroll
   for (int q = 1; q < C::NW; ++q) {
@@ -458,7 +471,7 @@ __device__ __forceinline__ unsigned long long red_max_u64(unsigned long long v, 
   unsigned long long* s = sm.redu + slot * C::NW;
   slot ^= 1;
   if ((threadIdx.x & 31) == 0) s[threadIdx.x >> 5] = v;
-  __syncthreads();
+  csync<C>();
   unsigned long long r = s[0];
 #pragma unroll
   for (int q = 1; q < C::NW; ++q) r = s[q] > r ? s[q] : r;
@@ -477,7 +490,7 @@ __device__ __forceinline__ void block_sum8(float (&v)[8], Smem<C>& sm, int& slot
 #pragma unroll
     for (int j = 0; j < 8; ++j) s[j * C::NW + w] = v[j];
   }
-  __syncthreads();
+  csync<C>();
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     float a = 0.f;
@@ -505,17 +518,20 @@ __device__ __forceinline__ void lse2_merge(float& m, float& s, float m2, float s
   m = M;
 }
 
-// Block reduction of the (Sc, Su) sums and the (zmax, S) log-sum-exp pair.
+// Block reduction of the (Sc, Su) sums and the (zmax, S) log-sum-exp pair:
+// S is carried relative to each thread's own maximum and rescaled once per
+// level (warp, block).
 template <class C>
 __device__ __forceinline__ void block_reduce_sums(float& sc, float& su, float& zm, float& s, Smem<C>& sm,
                                                   int& slot) {
+  const float zw = warp_max(zm);
+  // threads without a finite element carry s = 0 (or NaN) unscaled
+  float sw = (zm > kNegInf) ? __fmul_rn(s, ex2_approx(__fsub_rn(zm, zw))) : s;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     sc += __shfl_xor_sync(0xffffffffu, sc, o);
     su += __shfl_xor_sync(0xffffffffu, su, o);
-    const float m2 = __shfl_xor_sync(0xffffffffu, zm, o);
-    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
-    lse2_merge(zm, s, m2, s2);
+    sw += __shfl_xor_sync(0xffffffffu, sw, o);
   }
   float* b = sm.red8 + slot * 8 * C::NW;
   slot ^= 1;
@@ -523,19 +539,25 @@ __device__ __forceinline__ void block_reduce_sums(float& sc, float& su, float& z
   if ((threadIdx.x & 31) == 0) {
     b[w] = sc;
     b[C::NW + w] = su;
-    b[2 * C::NW + w] = zm;
-    b[3 * C::NW + w] = s;
+    b[2 * C::NW + w] = zw;
+    b[3 * C::NW + w] = sw;
   }
-  __syncthreads();
+  csync<C>();
   sc = 0.f;
   su = 0.f;
   zm = kNegInf;
-  s = 0.f;
 #pragma unroll
   for (int q = 0; q < C::NW; ++q) {
     sc += b[q];
     su += b[C::NW + q];
-    lse2_merge(zm, s, b[2 * C::NW + q], b[3 * C::NW + q]);
+    zm = fmaxf(zm, b[2 * C::NW + q]);
+  }
+  s = 0.f;
+#pragma unroll
+  for (int q = 0; q < C::NW; ++q) {
+    const float zq = b[2 * C::NW + q];
+    const float sq = b[3 * C::NW + q];
+    s += (zq > kNegInf) ? __fmul_rn(sq, ex2_approx(__fsub_rn(zq, zm))) : sq;
   }
 }
 
@@ -605,30 +627,29 @@ __device__ __forceinline__ int block_pick(const Pick& bp, bool turbo, Smem<C>& s
 
 // Hot argmax over the register tile: every valid element with z2 >= H kept
 // (and the min-p test), scored approximately, the near-best rescored exactly.
-template <class C>
-__device__ __forceinline__ int argmax_regs(const SampleParams& P, const PosCtx& X, const RowRef<C>& R,
-                                           const float (&z2)[C::NS], int vbase, float H, const ScoreCtx& K,
-                                           Pick bp, Smem<C>& sm, int& slot) {
+// zat(s) recomputes slot s's z2 from the tiles (-inf for invalid slots).
+template <class C, class ZF>
+__device__ __forceinline__ int argmax_regs(const SampleParams& P, const PosCtx& X, const RowRef<C>& R, ZF zat,
+                                           int vbase, float H, const ScoreCtx& K, Pick bp, Smem<C>& sm,
+                                           int& slot) {
   const int V = P.V;
-  float sa[C::NS];
+  // approximate score of slot s, -inf when not kept (recomputed on the second pass)
+  auto score_at = [&](int s) -> float {
+    const int v = vbase + (s / C::W) * C::NT * C::W + (s % C::W);
+    const float z = zat(s);
+    bool keep = v >= 0 && v < V && z >= H;
+    if (keep && K.minp_on) keep = __fmul_rn(ex2_approx(__fsub_rn(z, X.zmax)), K.r) >= K.minp_thr;
+    return keep ? approx_score<C>(P, X, K, v, z) : kNegInf;
+  };
   float best = kNegInf;
 #pragma unroll
-  for (int s = 0; s < C::NS; ++s) {
-    const int v = vbase + (s / C::W) * C::NT * C::W + (s % C::W);
-    float sc = kNegInf;
-    bool keep = v >= 0 && v < V && z2[s] >= H;
-    if (keep && K.minp_on)
-      keep = __fmul_rn(ex2_approx(__fsub_rn(z2[s], X.zmax)), K.r) >= K.minp_thr;
-    if (keep) sc = approx_score<C>(P, X, K, v, z2[s]);
-    sa[s] = sc;
-    best = fmaxf(best, sc);
-  }
+  for (int s = 0; s < C::NS; ++s) best = fmaxf(best, score_at(s));
   const float gbest = red_max1<C>(best, sm, slot);
   if (gbest > kNegInf) {
     const float thr = gbest - score_margin(gbest);
 #pragma unroll
     for (int s = 0; s < C::NS; ++s) {
-      if (sa[s] >= thr) {
+      if (score_at(s) >= thr) {
         const int v = vbase + (s / C::W) * C::NT * C::W + (s % C::W);
         const float vals = exact_val<C>(P, X, R, v);
         const float es = exact_score<C>(P, K, v, vals);
@@ -644,9 +665,10 @@ __device__ __forceinline__ int argmax_regs(const SampleParams& P, const PosCtx& 
 // kept (min-p test included); elements with band_lo <= z2 < H are kept iff
 // their composite (exact value, -id) key is >= Xcomp.
 template <class C>
-__device__ __noinline__ int argmax_smem(const SampleParams& P, const PosCtx& X, const RowRef<C>& R, float H,
-                                        float band_lo, unsigned long long Xcomp, const ScoreCtx& K, Pick bp,
-                                        Smem<C>& sm, int& slot) {
+__device__ __noinline__ int argmax_smem(const SampleParams& P, const PosCtx X, const RowRef<C> R, float H,
+                                        float band_lo, unsigned long long Xcomp, const ScoreCtx& K, Pick bp, Smem<C>& sm) {
+  csync<C>();  // out-of-line reductions use scratch slots 2/3
+  int slot = 2;
   const int V = P.V;
   float best = kNegInf;
   for (int v = threadIdx.x; v < V; v += C::NT) {
@@ -716,12 +738,12 @@ __device__ __forceinline__ void rank_sort(int n, Smem<C>& sm) {
     ev = sm.cande[tid];
     for (int j = 0; j < n; ++j) rank += (sm.cand[j] > key) ? 1 : 0;
   }
-  __syncthreads();
+  csync<C>();
   if (tid < n) {
     sm.cand[rank] = key;
     sm.cande[rank] = ev;
   }
-  __syncthreads();
+  csync<C>();
 }
 
 __device__ __forceinline__ void band_push(unsigned long long* cand, float* cande, int* counter, bool in,
@@ -743,13 +765,14 @@ __device__ __forceinline__ void band_push(unsigned long long* cand, float* cande
 }
 
 // Hot band from registers: {z2 >= lo_z} (nothing above it), unsorted in
-// sm.cand / sm.cande.  sm.misc[0] must be zero on entry (and a barrier passed).
-template <class C>
-__device__ __forceinline__ int band_regs(const SampleParams& P, const PosCtx& X, const RowRef<C>& R,
-                                         const float (&z2)[C::NS], int vbase, float lo_z, Smem<C>& sm) {
+// sm.cand (exact value, id) and sm.cande (2^(z2 - zmax)).  sm.misc[0] must be
+// zero on entry.  zat(s) recomputes slot s's z2 from the tiles.
+template <class C, class ZF>
+__device__ __forceinline__ int band_regs(const SampleParams& P, const PosCtx& X, const RowRef<C>& R, ZF zat,
+                                         int vbase, float lo_z, Smem<C>& sm) {
   uint64_t cm = 0ull;
 #pragma unroll
-  for (int s = 0; s < C::NS; ++s) cm |= (z2[s] >= lo_z) ? (1ull << s) : 0ull;
+  for (int s = 0; s < C::NS; ++s) cm |= (zat(s) >= lo_z) ? (1ull << s) : 0ull;
   const int lane = threadIdx.x & 31;
   const int cnt = __popcll(cm);
   int incl = cnt;
@@ -772,58 +795,20 @@ __device__ __forceinline__ int band_regs(const SampleParams& P, const PosCtx& X,
     }
     ++base;
   }
-  __syncthreads();
+  csync<C>();
   return sm.misc[0];
-}
-
-// Resolve a band of at most 32 candidates inside warp 0: sort, top-p / min-p
-// flags from the prefix sums, exact scores, argmax.  Returns the chosen id
-// (valid in warp 0 only).
-template <class C>
-__device__ __forceinline__ int band_warp_choose(const SampleParams& P, const PosCtx& X, const RowRef<C>& R,
-                                                const ScoreCtx& K, int n, bool topp_on, float top_p,
-                                                bool minp_on, float min_p, Smem<C>& sm) {
-  const int lane = threadIdx.x & 31;
-  unsigned long long key = lane < n ? sm.cand[lane] : 0ull;
-  key = warp_bitonic_desc(key);
-  const bool live = lane < n;
-  const int v = cand_id(key);
-  const float vals = cand_val(key);
-  const float e = live ? ex2_approx(__fsub_rn(z2_smem<C>(X, R, v), X.zmax)) : 0.f;
-  const float p = __fmul_rn(e, K.r);
-  double incl = (double)p;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const double t = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += t;
-  }
-  const float p0 = __shfl_sync(0xffffffffu, p, 0);
-  bool keep = live;
-  if (topp_on) keep = keep && (__fsub_rn((float)incl, p) < top_p);
-  if (minp_on) keep = keep && (p >= __fmul_rn(min_p, p0));
-  float sc = kNegInf;
-  if (keep) sc = exact_score<C>(P, K, v, vals);
-  if (!(sc == sc)) sc = kNegInf;
-  // argmax: score desc, then sorted position (lane) asc
-  const uint32_t ks = sc > kNegInf ? ord_key(sc) : 0u;
-  unsigned long long rec = ks ? (((unsigned long long)ks << 32) | (uint32_t)(31 - lane)) : 0ull;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const unsigned long long x = __shfl_xor_sync(0xffffffffu, rec, o);
-    rec = x > rec ? x : rec;
-  }
-  const int win_lane = rec ? 31 - (int)(uint32_t)(rec & 0xffffffffu) : 0;
-  return __shfl_sync(0xffffffffu, v, win_lane);
 }
 
 // Cold band from the staged rows: {lo_z <= z2 < hi_z}, with count and mass above hi_z.
 template <class C>
-__device__ __noinline__ Band band_smem(const SampleParams& P, const PosCtx& X, const RowRef<C>& R, float lo_z,
-                                       float hi_z, Smem<C>& sm, int& slot) {
+__device__ __noinline__ Band band_smem(const SampleParams& P, const PosCtx X, const RowRef<C> R, float lo_z,
+                                       float hi_z, Smem<C>& sm) {
+  csync<C>();  // out-of-line reductions use scratch slots 2/3
+  int slot = 2;
   const int V = P.V;
-  __syncthreads();
+  csync<C>();
   if (threadIdx.x == 0) sm.misc[0] = 0;
-  __syncthreads();
+  csync<C>();
   float na = 0.f, ma = 0.f;
   for (int v0 = 0; v0 < V; v0 += C::NT) {
     const int v = v0 + threadIdx.x;
@@ -883,7 +868,7 @@ __device__ __forceinline__ void band_flags(const Band& bd, bool use_k, int k_lef
       run = __shfl_sync(0xffffffffu, incl, 31);
     }
   }
-  __syncthreads();
+  csync<C>();
 }
 
 // Counts and masses of {z2 >= t[j]} over the staged rows.
@@ -913,9 +898,10 @@ __device__ __forceinline__ void stats4_smem(const PosCtx& X, const RowRef<C>& R,
 // on return stat(hi) < tgt_lo and stat(lo) >= tgt_hi, with few elements
 // between them unless the values are (near) ties.
 template <class C>
-__device__ __noinline__ void bracket_smem(const PosCtx& X, const RowRef<C>& R, int V, bool by_mass, float tgt_lo,
-                                          float tgt_hi, float floor_t, float cnt_floor, float& lo, float& hi,
-                                          Smem<C>& sm, int& slot) {
+__device__ __noinline__ void bracket_smem(const PosCtx X, const RowRef<C> R, int V, bool by_mass, float tgt_lo,
+                                          float tgt_hi, float floor_t, float cnt_floor, float& lo, float& hi, Smem<C>& sm) {
+  csync<C>();  // out-of-line reductions use scratch slots 2/3
+  int slot = 2;
   lo = floor_t;
   float cnt_lo = cnt_floor;
   hi = X.zmax + 1.0f;
@@ -955,11 +941,12 @@ __device__ __noinline__ void bracket_smem(const PosCtx& X, const RowRef<C>& R, i
 // (exact value, -id) thresholds by bisection (top-k by count, top-p by the
 // exclusive prefix mass).  Band elements with composite >= the result are kept.
 template <class C>
-__device__ __noinline__ unsigned long long overflow_resolve(const SampleParams& P, const PosCtx& X,
-                                                            const RowRef<C>& R, float lo_z, float hi_z,
+__device__ __noinline__ unsigned long long overflow_resolve(const SampleParams& P, const PosCtx X,
+                                                            const RowRef<C> R, float lo_z, float hi_z,
                                                             float n_above, float m_above, bool topk_on, int kk,
-                                                            bool topp_on, float top_p, float S_all, float& Sk_out,
-                                                            Smem<C>& sm, int& slot) {
+                                                            bool topp_on, float top_p, float S_all, float& Sk_out, Smem<C>& sm) {
+  csync<C>();  // out-of-line reductions use scratch slots 2/3
+  int slot = 2;
   const int V = P.V;
   unsigned long long Xk = 0ull;
   float Sn = S_all;
@@ -1014,7 +1001,9 @@ __device__ __noinline__ unsigned long long overflow_resolve(const SampleParams& 
 
 // Lowest id whose z2 is NaN, else +inf, else -1 (torch orders NaN first).
 template <class C>
-__device__ __noinline__ int first_nan_or_inf(const PosCtx& X, const RowRef<C>& R, int V, Smem<C>& sm, int& slot) {
+__device__ __noinline__ int first_nan_or_inf(const PosCtx X, const RowRef<C> R, int V, Smem<C>& sm) {
+  csync<C>();  // out-of-line reductions use scratch slots 2/3
+  int slot = 2;
   int fn = 0x7fffffff, fi = 0x7fffffff;
   for (int v = threadIdx.x; v < V; v += C::NT) {
     const float z = z2_smem<C>(X, R, v);
@@ -1034,8 +1023,9 @@ __device__ __noinline__ int first_nan_or_inf(const PosCtx& X, const RowRef<C>& R
 // First sorted candidate (largest exact value, lowest id): torch's argmax over
 // an all -inf row returns it.
 template <class C>
-__device__ __noinline__ int top1_smem(const SampleParams& P, const PosCtx& X, const RowRef<C>& R, Smem<C>& sm,
-                                     int& slot) {
+__device__ __noinline__ int top1_smem(const SampleParams& P, const PosCtx X, const RowRef<C> R, Smem<C>& sm) {
+  csync<C>();  // out-of-line reductions use scratch slots 2/3
+  int slot = 2;
   unsigned long long best = 0ull;
   const float zlo = __fsub_rn(X.zmax, zmargin(X.zmax));
   for (int v = threadIdx.x; v < P.V; v += C::NT) {
@@ -1052,9 +1042,10 @@ __device__ __noinline__ int top1_smem(const SampleParams& P, const PosCtx& X, co
 
 // Top-k / top-p (and min-p) selection from the staged rows.
 template <class C>
-__device__ __noinline__ int select_cold(const SampleParams& P, const PosCtx& X, const RowRef<C>& R, ScoreCtx K,
-                                        int topk_raw, bool topk_on, bool topp_on, float top_p, float min_p,
-                                        Smem<C>& sm, int& slot) {
+__device__ __noinline__ int select_cold(const SampleParams& P, const PosCtx X, const RowRef<C> R, ScoreCtx K,
+                                        int topk_raw, bool topk_on, bool topp_on, float top_p, float min_p, Smem<C>& sm) {
+  csync<C>();  // out-of-line reductions use scratch slots 2/3
+  int slot = 2;
   const int V = P.V;
   float H = -kBig, band_lo = kBig;
   unsigned long long Xcomp = 0ull;
@@ -1067,13 +1058,16 @@ __device__ __noinline__ int select_cold(const SampleParams& P, const PosCtx& X, 
   bool done = false;
   if (topk_on) {
     float lo, hi;
-    bracket_smem<C>(X, R, V, false, (float)topk_raw, (float)topk_raw, -kBig, (float)V, lo, hi, sm, slot);
+    bracket_smem<C>(X, R, V, false, (float)topk_raw, (float)topk_raw, -kBig, (float)V, lo, hi, sm);
+    csync<C>();
     const float blo = __fsub_rn(lo, zmargin(lo)), bhi = __fadd_rn(hi, zmargin(hi));
-    bk = band_smem<C>(P, X, R, blo, bhi, sm, slot);
+    bk = band_smem<C>(P, X, R, blo, bhi, sm);
+    csync<C>();
     if (bk.overflow) {
       float Sk;
       Xcomp = overflow_resolve<C>(P, X, R, blo, bhi, bk.n_above, bk.m_above, true, topk_raw,
-                                  topp_on && bk.m_above < __fmul_rn(top_p, X.S), top_p, X.S, Sk, sm, slot);
+                                  topp_on && bk.m_above < __fmul_rn(top_p, X.S), top_p, X.S, Sk, sm);
+      csync<C>();
       Sn = Sk;
       K.r = __fdiv_rn(1.0f, Sn);
       if (K.minp_on) K.minp_thr = __fmul_rn(min_p, K.r);
@@ -1097,14 +1091,15 @@ __device__ __noinline__ int select_cold(const SampleParams& P, const PosCtx& X, 
     const float tgt = __fmul_rn(top_p, Sn);
     if (topp_on && !(topk_on && bk.m_above < __fmul_rn(tgt, 1.00001f))) {
       float lo, hi;
-      bracket_smem<C>(X, R, V, true, __fmul_rn(tgt, 0.99999f), __fmul_rn(tgt, 1.00001f), Hk, cnt_k, lo, hi, sm,
-                      slot);
+      bracket_smem<C>(X, R, V, true, __fmul_rn(tgt, 0.99999f), __fmul_rn(tgt, 1.00001f), Hk, cnt_k, lo, hi, sm);
+    csync<C>();
       const float blo = fmaxf(__fsub_rn(lo, zmargin(lo)), Hk), bhi = __fadd_rn(hi, zmargin(hi));
-      const Band bp = band_smem<C>(P, X, R, blo, bhi, sm, slot);
+      const Band bp = band_smem<C>(P, X, R, blo, bhi, sm);
+    csync<C>();
       if (bp.overflow) {
         float Sk;
-        Xcomp = overflow_resolve<C>(P, X, R, blo, bhi, bp.n_above, bp.m_above, false, 0, true, top_p, Sn, Sk,
-                                    sm, slot);
+        Xcomp = overflow_resolve<C>(P, X, R, blo, bhi, bp.n_above, bp.m_above, false, 0, true, top_p, Sn, Sk, sm);
+      csync<C>();
         H = bhi;
         band_lo = blo;
         nband = 0;
@@ -1124,61 +1119,125 @@ __device__ __noinline__ int select_cold(const SampleParams& P, const PosCtx& X, 
     }
   }
   const Pick bp0 = band_pick<C>(P, K, nband, sm);
-  const int c = argmax_smem<C>(P, X, R, H, band_lo, Xcomp, K, bp0, sm, slot);
-  return c >= 0 ? c : top1_smem<C>(P, X, R, sm, slot);
+  const int c = argmax_smem<C>(P, X, R, H, band_lo, Xcomp, K, bp0, sm);
+  csync<C>();
+  return c >= 0 ? c : top1_smem<C>(P, X, R, sm);
 }
 
+// Per-stage side data: request parameters and history (filled by the
+// producer warp when it issues the stage), and the hand-off record from the
+// compute warps to the finisher.
+struct StageAux {
+  int item;  // flat position b*L + l of the staged item
+  float T, top_p, min_p, rep;
+  int top_k;
+  int hist_ok;
+  int kind;  // 0: outputs written by the compute warps; 1: band for the finisher
+  int pos, b, l;
+  int topp_on, pen_on, noisy;
+  float r, rrep;
+  float mc, Sc, mu, Su;
+  uint32_t hist[(YAPD_MAX_V + 31) / 32 + 3];
+};
+
 template <class C>
-__device__ __forceinline__ void process_item(const SampleParams& P, Smem<C>& sm, int& slot, int stage, int pos) {
-  const int tid = threadIdx.x;
-  const int V = P.V;
+struct Smem {
+  uint64_t full[C::NSTAGE];  // rows + parameters landed
+  uint64_t hand[C::NSTAGE];  // compute warps done with the stage
+  uint64_t candfree;         // finisher done with the candidate band
+  float red8[4 * 8 * C::NW];  // slots 0/1: hot path, 2/3: out-of-line paths
+  unsigned long long redu[4 * C::NW];
+  int misc[8];
+  unsigned long long cand[C::BAND];
+  float cande[C::BAND];
+  unsigned char cflag[C::BAND];
+  StageAux aux[C::NSTAGE];
+  alignas(128) unsigned char stage[C::NSTAGE][C::STAGE_BYTES];
+};
+
+// Write the sampled id and the PMI inputs softmax(c)[s], softmax(u)[s]
+// (server/engine.py:539-540, 553, 556); the unmask kernel forms the PMI.
+template <class C, bool CFG>
+__device__ __forceinline__ void write_choice(const SampleParams& P, const RowRef<C>& R, int pos, int chosen,
+                                             float mc, float Sc, float mu, float Su) {
+  P.sampled[pos] = chosen;
+  if (P.pcu) {
+    const float cv = load_elem_smem<C>(R.sc, R.gc, chosen);
+    const float pc = __fmul_rn(expf(__fsub_rn(cv, mc)), __fdiv_rn(1.0f, Sc));
+    float pu = 0.f;
+    if (CFG) {
+      const float uv = load_elem_smem<C>(R.su, R.gu, chosen);
+      pu = __fmul_rn(expf(__fsub_rn(uv, mu)), __fdiv_rn(1.0f, Su));
+    }
+    P.pcu[pos] = make_float2(pc, pu);
+  }
+}
+
+template <class C, bool CFG>
+__device__ __forceinline__ RowRef<C> row_ref(const SampleParams& P, Smem<C>& sm, int stage, int pos) {
   const int b = pos / P.L, l = pos - b * P.L;
   const int64_t base = (int64_t)b * P.stride_req + (int64_t)l * P.stride_pos;
   RowRef<C> R;
   R.sc = sm.stage[stage];
   R.su = sm.stage[stage] + C::ROW_SLOT;
   R.gc = row_geom<C>(P, base);
+  R.gu = CFG ? row_geom<C>(P, base + P.stride_branch) : R.gc;
+  return R;
+}
+
+// Compute warps: one position.
+template <class C, bool CFG>
+__device__ __forceinline__ void compute_item(const SampleParams& P, Smem<C>& sm, int& slot, int stage, int pos,
+                                             int it) {
+  const int tid = threadIdx.x;
+  const int V = P.V;
+  const int b = pos / P.L, l = pos - b * P.L;
+  const RowRef<C> R = row_ref<C, CFG>(P, sm, stage, pos);
+  StageAux& A = sm.aux[stage];
   PosCtx X;
-  X.cfg = (P.nb == 2);
-  R.gu = X.cfg ? row_geom<C>(P, base + P.stride_branch) : R.gc;
-  // per-request parameters and the history bitmap: issue the loads first so
-  // their latency hides behind the tile loads and the first passes
-  X.T = param_f(P.temperature, P.temperature_s, b);
-  const int topk_raw = param_i(P.top_k, P.top_k_s, b);
-  const float top_p = param_f(P.top_p, P.top_p_s, b);
-  const float min_p = param_f(P.min_p, P.min_p_s, b);
-  const float rep = param_f(P.rep_penalty, P.rep_penalty_s, b);
-  const bool pen_on = P.history_kind != YAPD_HISTORY_NONE && P.history != nullptr && rep != 1.0f;
-  const int hwords = (V + 31) >> 5;
-  uint32_t hword = 0u;
-  if (pen_on && tid < hwords) hword = history_word(P, b, tid);
+  X.cfg = CFG;
+  X.T = A.T;
+  const int topk_raw = A.top_k;
+  const float top_p = A.top_p;
+  const float min_p = A.min_p;
+  const float rep = A.rep;
+  const bool pen_on = A.hist_ok && rep != 1.0f;
   X.scale = X.T > 0.0f;
   X.rT = X.scale ? __fdiv_rn(1.0f, X.T) : 1.0f;
 
   // ---- registers: cond and uncond tiles ----
   Tile<C> tc, tu;
   const uint32_t edge = load_tile<C>(tc, R.sc, R.gc, V);
-  if (X.cfg) {
+  if (CFG) {
     if (R.gu.head == R.gc.head) load_tile<C>(tu, R.su, R.gu, V);
     else load_tile_rephase<C>(tu, R.su, R.gu, R.gc, V);
   }
   const int vbase = tid * C::W - R.gc.head;
 
   // ---- row maxima ----
-  const float2 ml = tile_max2<C>(tc, tu, X.cfg);
+  const float2 ml = tile_max2<C>(tc, tu, CFG);
   const float2 mx = red_max2<C>(ml.x, ml.y, sm, slot);
   X.mc = mx.x;
-  X.mu = X.cfg ? mx.y : 0.f;
+  X.mu = CFG ? mx.y : 0.f;
 
   // ---- sums of exp(x - max) and z2 = log2(e)*guided/T - const ----
   const float w = P.cfg_w;
   const float sA = X.scale ? X.rT : 1.0f;
-  X.A2 = X.cfg ? __fmul_rn(__fmul_rn(kLog2e, P.cfg_1pw), sA) : __fmul_rn(kLog2e, sA);
-  X.B2 = X.cfg ? __fmul_rn(__fmul_rn(kLog2e, w), sA) : 0.f;
-  X.K2 = X.cfg ? __fmaf_rn(-X.mc, X.A2, __fmul_rn(X.mu, X.B2)) : __fmul_rn(-X.mc, X.A2);
+  X.A2 = CFG ? __fmul_rn(__fmul_rn(kLog2e, P.cfg_1pw), sA) : __fmul_rn(kLog2e, sA);
+  X.B2 = CFG ? __fmul_rn(__fmul_rn(kLog2e, w), sA) : 0.f;
+  X.K2 = CFG ? __fmaf_rn(-X.mc, X.A2, __fmul_rn(X.mu, X.B2)) : __fmul_rn(-X.mc, X.A2);
   const float mcL = __fmul_rn(X.mc, kLog2e), muL = __fmul_rn(X.mu, kLog2e);
   float sc_t = 0.f, su_t = 0.f, zm_t = kNegInf;
-  float z2[C::NS];
+  // z2 of slot (k, i), -inf outside the row (recomputed where needed: two FMAs)
+  auto zat = [&](int s) -> float {
+    const int k = s / C::W, i = s % C::W;
+    float z = z2_of(X, tc.get(k, i), CFG ? tu.get(k, i) : 0.f);
+    if ((edge >> k) & 1u) {
+      const int v = (tid + k * C::NT) * C::W - R.gc.head + i;
+      if (v < 0 || v >= V) z = kNegInf;
+    }
+    return z;
+  };
 #pragma unroll
   for (int k = 0; k < C::NVT; ++k)
 #pragma unroll
@@ -1186,49 +1245,42 @@ __device__ __forceinline__ void process_item(const SampleParams& P, Smem<C>& sm,
       const float c = tc.get(k, i);
       sc_t += ex2_approx(__fmaf_rn(c, kLog2e, -mcL));
       float u = 0.f;
-      if (X.cfg) {
+      if (CFG) {
         u = tu.get(k, i);
         su_t += ex2_approx(__fmaf_rn(u, kLog2e, -muL));
       }
-      const float z = z2_of(X, c, u);
-      z2[k * C::W + i] = z;
-      zm_t = fmaxf(zm_t, z);
+      zm_t = fmaxf(zm_t, z2_of(X, c, u));  // invalid slots give NaN or -inf: ignored
     }
-  if (edge) {
-#pragma unroll
-    for (int k = 0; k < C::NVT; ++k) {
-      if (!((edge >> k) & 1u)) continue;
-      const int v0 = (tid + k * C::NT) * C::W - R.gc.head;
-#pragma unroll
-      for (int i = 0; i < C::W; ++i) {
-        const int v = v0 + i;
-        if (v < 0 || v >= V) z2[k * C::W + i] = kNegInf;
-      }
-    }
-  }
   float s_t = 0.f;
-  if (zm_t > kNegInf) {
+  {
+    // relative to this thread's maximum (0 when it has no finite element, so
+    // that a NaN still propagates)
+    const float zr = zm_t > kNegInf ? zm_t : 0.f;
 #pragma unroll
-    for (int s = 0; s < C::NS; ++s) s_t += ex2_approx(__fsub_rn(z2[s], zm_t));
+    for (int s = 0; s < C::NS; ++s) s_t += ex2_approx(__fsub_rn(zat(s), zr));
   }
-  if (pen_on && tid < hwords) sm.hist[tid] = hword;
-  if (tid == 0) sm.misc[0] = 0;  // band counter, published by the next barrier
+  if (tid == 0) {
+    // the finisher must be done with the previous band before it is reused
+    if (it > 0 && !mbar_wait_bounded(&sm.candfree, (uint32_t)(it - 1) & 1u, kWaitLimitNs))
+      atomicOr(P.status, (unsigned)YAPD_STATUS_WAIT_TIMEOUT);
+    sm.misc[0] = 0;
+  }
   block_reduce_sums<C>(sc_t, su_t, zm_t, s_t, sm, slot);
   X.Sc = sc_t;
   X.Su = su_t;
   X.zmax = zm_t;
   X.S = s_t;
   X.lc = logf(X.Sc);
-  X.lu = X.cfg ? logf(X.Su) : 0.f;
-  X.Kval = X.cfg ? __fmul_rn(__fsub_rn(__fmul_rn(w, X.lu), __fmul_rn(P.cfg_1pw, X.lc)), sA)
-                 : __fmul_rn(X.mc, sA);
+  X.lu = CFG ? logf(X.Su) : 0.f;
+  X.Kval = CFG ? __fmul_rn(__fsub_rn(__fmul_rn(w, X.lu), __fmul_rn(P.cfg_1pw, X.lc)), sA)
+               : __fmul_rn(X.mc, sA);
 
   // ---- token choice ----
   const bool topk_on = topk_raw > 0 && topk_raw < V;
   const bool topp_on = top_p < 1.0f;
   const bool minp_on = min_p > 0.0f;
   ScoreCtx K;
-  K.hist = sm.hist;
+  K.hist = A.hist;
   K.b = b;
   K.pos = pos;
   K.l = l;
@@ -1241,29 +1293,40 @@ __device__ __forceinline__ void process_item(const SampleParams& P, Smem<C>& sm,
   K.r = __fdiv_rn(1.0f, X.S);
   K.minp_thr = 0.f;
 
-  int chosen;
+  int chosen = -1;
+  bool handed = false;
   const Pick none{kNegInf, kNegInf, 0x7fffffff};
-  if (!(X.Sc == X.Sc) || (X.cfg && !(X.Su == X.Su))) {
+  if (!(X.Sc == X.Sc) || (CFG && !(X.Su == X.Su))) {
     chosen = 0;  // a NaN/+inf logit makes the whole reference row NaN: argmax -> 0
   } else if (!(X.S == X.S)) {
-    const int f = first_nan_or_inf<C>(X, R, V, sm, slot);
+    const int f = first_nan_or_inf<C>(X, R, V, sm);
     chosen = f < 0 ? 0 : f;
   } else if (!topk_on && !topp_on && !minp_on) {
     // every token kept: server/engine.py:546-550 (or the penalty-only chain)
-    chosen = argmax_regs<C>(P, X, R, z2, vbase, -kBig, K, none, sm, slot);
+    chosen = argmax_regs<C>(P, X, R, zat, vbase, -kBig, K, none, sm, slot);
     if (chosen < 0) chosen = 0;
   } else {
-    chosen = -1;
     if (minp_on && !topk_on) {
       const float zm = fminf(__fadd_rn(X.zmax, log2f(min_p)), X.zmax);
-      const int n = band_regs<C>(P, X, R, z2, vbase, __fsub_rn(zm, zmargin(zm)), sm);
+      const int n = band_regs<C>(P, X, R, zat, vbase, __fsub_rn(zm, zmargin(zm)), sm);
       if (n <= 32) {
-        if (tid < 32) {
-          const int c = band_warp_choose<C>(P, X, R, K, n, topp_on, top_p, true, min_p, sm);
-          if (tid == 0) sm.misc[1] = c;
+        // hand the short band to the finisher warp
+        if (tid == 0) {
+          A.kind = 1;
+          A.pos = pos;
+          A.b = b;
+          A.l = l;
+          A.topp_on = topp_on;
+          A.pen_on = K.pen_on;
+          A.noisy = K.noisy;
+          A.r = K.r;
+          A.rrep = K.rrep;
+          A.mc = X.mc;
+          A.Sc = X.Sc;
+          A.mu = X.mu;
+          A.Su = X.Su;
         }
-        __syncthreads();
-        chosen = sm.misc[1];
+        handed = true;
       } else if (n <= C::BAND) {
         rank_sort<C>(n, sm);
         Band bd;
@@ -1279,38 +1342,124 @@ __device__ __forceinline__ void process_item(const SampleParams& P, Smem<C>& sm,
         if (chosen < 0) chosen = cand_id(sm.cand[0]);
       }
     }
-    if (chosen < 0) {
+    if (!handed && chosen < 0) {
       K.minp_on = minp_on;
-      chosen = select_cold<C>(P, X, R, K, topk_raw, topk_on, topp_on, top_p, min_p, sm, slot);
+      chosen = select_cold<C>(P, X, R, K, topk_raw, topk_on, topp_on, top_p, min_p, sm);
     }
   }
-  if (chosen < 0 || chosen >= V) {
-    if (tid == 0) atomicOr(P.status, (unsigned)YAPD_STATUS_INTERNAL);
-    chosen = 0;
-  }
-  // ---- softmax(c)[s] and softmax(u)[s] of the chosen token (server/engine.py:539-540,
-  // 553, 556); the unmask kernel turns them into the PMI ----
-  if (tid == 0) {
-    P.sampled[pos] = chosen;
-    if (P.pcu) {
-      const float cv = load_elem_smem<C>(R.sc, R.gc, chosen);
-      const float pc = __fmul_rn(expf(__fsub_rn(cv, X.mc)), __fdiv_rn(1.0f, X.Sc));
-      float pu = 0.f;
-      if (X.cfg) {
-        const float uv = load_elem_smem<C>(R.su, R.gu, chosen);
-        pu = __fmul_rn(expf(__fsub_rn(uv, X.mu)), __fdiv_rn(1.0f, X.Su));
-      }
-      P.pcu[pos] = make_float2(pc, pu);
+  if (!handed && tid == 0) {
+    if (chosen < 0 || chosen >= V) {
+      atomicOr(P.status, (unsigned)YAPD_STATUS_INTERNAL);
+      chosen = 0;
     }
+    A.kind = 0;
+    write_choice<C, CFG>(P, R, pos, chosen, X.mc, X.Sc, X.mu, X.Su);
   }
 }
 
-}  // namespace yapd
+// Finisher: resolve a band of at most 32 candidates: top-p / min-p flags from
+// prefix sums over the exactly sorted band, exact scores (penalty + noise),
+// argmax, and the PMI inputs of the winner.
+template <class C, bool CFG>
+__device__ __forceinline__ void finish_band(const SampleParams& P, Smem<C>& sm, const StageAux& A,
+                                            const RowRef<C>& R) {
+  const int lane = threadIdx.x & 31;
+  const int n = sm.misc[0];
+  unsigned long long key = lane < n ? sm.cand[lane] : 0ull;
+  int q = lane;
+#pragma unroll
+  for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const unsigned long long y = __shfl_xor_sync(0xffffffffu, key, j);
+      const int qy = __shfl_xor_sync(0xffffffffu, q, j);
+      const bool up = ((lane & k) == 0);
+      const bool lower = ((lane & j) == 0);
+      const bool take_max = (up == lower);
+      if (take_max ? (y > key) : (y < key)) {
+        key = y;
+        q = qy;
+      }
+    }
+  }
+  const bool live = lane < n;
+  const int v = cand_id(key);
+  const float vals = cand_val(key);
+  const float e = live ? sm.cande[q] : 0.f;
+  const float p = __fmul_rn(e, A.r);
+  double incl = (double)p;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  const float p0 = __shfl_sync(0xffffffffu, p, 0);
+  bool keep = live;
+  if (A.topp_on) keep = keep && (__fsub_rn((float)incl, p) < A.top_p);
+  keep = keep && (p >= __fmul_rn(A.min_p, p0));
+  float sc = kNegInf;
+  if (keep) {
+    sc = vals;
+    if (A.pen_on && ((A.hist[v >> 5] >> (v & 31)) & 1u)) sc = penalize(vals, A.rep, A.rrep);
+    if (A.noisy) sc = __fadd_rn(sc, noise_at(P, A.b, A.pos, A.l, v));
+  }
+  if (!(sc == sc)) sc = kNegInf;
+  const uint32_t ks = sc > kNegInf ? ord_key(sc) : 0u;
+  unsigned long long rec = ks ? (((unsigned long long)ks << 32) | (uint32_t)(31 - lane)) : 0ull;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long x = __shfl_xor_sync(0xffffffffu, rec, o);
+    rec = x > rec ? x : rec;
+  }
+  const int win_lane = rec ? 31 - (int)(uint32_t)(rec & 0xffffffffu) : 0;
+  if (lane == win_lane) {
+    int chosen = v;
+    if (!live || chosen < 0 || chosen >= P.V) {
+      atomicOr(P.status, (unsigned)YAPD_STATUS_INTERNAL);
+      chosen = 0;
+    }
+    write_choice<C, CFG>(P, R, A.pos, chosen, A.mc, A.Sc, A.mu, A.Su);
+  }
+}
 
-namespace yapd {
+// Producer: bulk copies of the position's rows plus its parameters and history.
+template <class C, bool CFG>
+__device__ __forceinline__ void produce_item(const SampleParams& P, Smem<C>& sm, int stage, int pos) {
+  const int lane = threadIdx.x & 31;
+  if (lane == 0) issue_item<C>(P, sm, stage, pos);
+  const int b = pos / P.L;
+  StageAux& A = sm.aux[stage];
+  if (lane == 0) {
+    A.item = pos;
+    A.T = param_f(P.temperature, P.temperature_s, b);
+    A.top_k = param_i(P.top_k, P.top_k_s, b);
+    A.top_p = param_f(P.top_p, P.top_p_s, b);
+    A.min_p = param_f(P.min_p, P.min_p_s, b);
+    A.rep = param_f(P.rep_penalty, P.rep_penalty_s, b);
+    A.hist_ok = (P.history_kind != YAPD_HISTORY_NONE && P.history != nullptr) ? 1 : 0;
+  }
+  const float rep = param_f(P.rep_penalty, P.rep_penalty_s, b);
+  if (P.history_kind != YAPD_HISTORY_NONE && P.history != nullptr && rep != 1.0f) {
+    const int hwords = (P.V + 31) >> 5;
+    constexpr int kPer = ((YAPD_MAX_V + 31) / 32 + 31) / 32;
+    uint32_t hw[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int wd = lane + 32 * j;
+      hw[j] = wd < hwords ? history_word(P, b, wd) : 0u;
+    }
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int wd = lane + 32 * j;
+      if (wd < hwords) A.hist[wd] = hw[j];
+    }
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&sm.full[stage]);
+}
 
-template <class C>
-__global__ void __launch_bounds__(C::NT, C::MINB) sample_kernel(const SampleParams P) {
+template <class C, bool CFG>
+__global__ void __launch_bounds__(C::NT + 32, C::MINB) sample_kernel(const SampleParams P) {
   extern __shared__ unsigned char smem_raw[];
   Smem<C>& sm = *reinterpret_cast<Smem<C>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
@@ -1318,38 +1467,57 @@ __global__ void __launch_bounds__(C::NT, C::MINB) sample_kernel(const SamplePara
   const int first = blockIdx.x, stride = gridDim.x;
   if (first >= n_items) return;
   const int n_my = (n_items - first + stride - 1) / stride;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < C::NSTAGE; ++s) mbar_init(&sm.full[s], 1);
+  const bool finisher = threadIdx.x >= C::NT;
+  if (threadIdx.x == C::NT) {
+    for (int s = 0; s < C::NSTAGE; ++s) {
+      mbar_init(&sm.full[s], 2);        // expect_tx arrive + parameters arrive
+      mbar_init(&sm.hand[s], C::NW);    // one arrive per compute warp
+    }
+    mbar_init(&sm.candfree, 1);
     fence_mbar_init();
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (finisher) {
     for (int s = 0; s < C::NSTAGE && s < n_my; ++s)
-      issue_item<C>(P, sm, s, item_pos<C>(P, first + s * stride));
+      produce_item<C, CFG>(P, sm, s, item_pos<C>(P, first + s * stride));
+    for (int it = 0; it < n_my; ++it) {
+      const int stage = it % C::NSTAGE;
+      const uint32_t parity = (uint32_t)(it / C::NSTAGE) & 1u;
+      if (!mbar_wait_bounded(&sm.hand[stage], parity, kWaitLimitNs)) {
+        // the compute warps stopped: record it and give the copies still in
+        // flight (items it .. it+NSTAGE-1) a bounded chance to land
+        if ((threadIdx.x & 31) == 0) {
+          atomicOr(P.status, (unsigned)YAPD_STATUS_WAIT_TIMEOUT);
+          for (int q = it; q < n_my && q < it + C::NSTAGE; ++q)
+            (void)mbar_wait_bounded(&sm.full[q % C::NSTAGE], (uint32_t)(q / C::NSTAGE) & 1u, kWaitLimitNs);
+        }
+        break;
+      }
+      const StageAux& A = sm.aux[stage];
+      if (A.kind == 1) {
+        const RowRef<C> R = row_ref<C, CFG>(P, sm, stage, A.pos);
+        finish_band<C, CFG>(P, sm, A, R);
+      }
+      __syncwarp();
+      if ((threadIdx.x & 31) == 0) mbar_arrive(&sm.candfree);
+      if (it + C::NSTAGE < n_my) {
+        if ((threadIdx.x & 31) == 0) fence_proxy_async_smem();
+        __syncwarp();
+        produce_item<C, CFG>(P, sm, stage, item_pos<C>(P, first + (it + C::NSTAGE) * stride));
+      }
+    }
+    return;
   }
   int slot = 0;
   for (int it = 0; it < n_my; ++it) {
     const int stage = it % C::NSTAGE;
     const uint32_t parity = (uint32_t)(it / C::NSTAGE) & 1u;
     const bool ok = mbar_wait_bounded(&sm.full[stage], parity, kWaitLimitNs);
-    if (__syncthreads_or(!ok)) {
-      // A copy did not land in time: record it, give the copies still in
-      // flight a bounded chance to finish, and leave without touching them.
-      if (threadIdx.x == 0) {
-        atomicOr(P.status, (unsigned)YAPD_STATUS_WAIT_TIMEOUT);
-        for (int q = it; q < n_my && q < it + C::NSTAGE; ++q)
-          (void)mbar_wait_bounded(&sm.full[q % C::NSTAGE], (uint32_t)(q / C::NSTAGE) & 1u, kWaitLimitNs);
-      }
-      __syncthreads();
-      return;
-    }
-    process_item<C>(P, sm, slot, stage, item_pos<C>(P, first + it * stride));
-    // Every thread but 0 finished reading this stage before the item's last
-    // barrier; thread 0's own reads precede the refill in program order.
-    if (threadIdx.x == 0 && it + C::NSTAGE < n_my) {
-      fence_proxy_async_smem();
-      issue_item<C>(P, sm, stage, item_pos<C>(P, first + (it + C::NSTAGE) * stride));
-    }
+    if (!ok) atomicOr(P.status, (unsigned)YAPD_STATUS_WAIT_TIMEOUT);
+    if (csync_or<C>(!ok)) return;
+    compute_item<C, CFG>(P, sm, slot, stage, sm.aux[stage].item, it);
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&sm.hand[stage]);
   }
 }
 
@@ -1505,12 +1673,22 @@ constexpr size_t smem_bytes() {
 
 struct DevInfo {
   int sms = 0;
-  int occ_bf16 = 0;
-  int occ_f32 = 0;
+  int occ[2][2] = {{0, 0}, {0, 0}};  // [bf16][cfg]
   bool init = false;
 };
 
 static DevInfo g_dev[64];
+
+template <class C, bool CFG>
+static int prepare_kernel(int* occ) {
+  if (cudaFuncSetAttribute(sample_kernel<C, CFG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem_bytes<C>()) != cudaSuccess)
+    return YAPD_ERR_LAUNCH;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(occ, sample_kernel<C, CFG>, C::NT + 32, smem_bytes<C>()) !=
+      cudaSuccess)
+    return YAPD_ERR_LAUNCH;
+  return *occ >= 1 ? YAPD_OK : YAPD_ERR_LAUNCH;
+}
 
 static int device_info(DevInfo** out) {
   int dev = 0;
@@ -1519,19 +1697,11 @@ static int device_info(DevInfo** out) {
   if (!d.init) {
     if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       return YAPD_ERR_NO_DEVICE;
-    if (cudaFuncSetAttribute(sample_kernel<CfgBF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem_bytes<CfgBF16>()) != cudaSuccess)
-      return YAPD_ERR_LAUNCH;
-    if (cudaFuncSetAttribute(sample_kernel<CfgF32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem_bytes<CfgF32>()) != cudaSuccess)
-      return YAPD_ERR_LAUNCH;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.occ_bf16, sample_kernel<CfgBF16>, CfgBF16::NT,
-                                                      smem_bytes<CfgBF16>()) != cudaSuccess)
-      return YAPD_ERR_LAUNCH;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.occ_f32, sample_kernel<CfgF32>, CfgF32::NT,
-                                                      smem_bytes<CfgF32>()) != cudaSuccess)
-      return YAPD_ERR_LAUNCH;
-    if (d.occ_bf16 < 1 || d.occ_f32 < 1) return YAPD_ERR_LAUNCH;
+    int rc = prepare_kernel<CfgBF16, true>(&d.occ[1][1]);
+    if (rc == YAPD_OK) rc = prepare_kernel<CfgBF16, false>(&d.occ[1][0]);
+    if (rc == YAPD_OK) rc = prepare_kernel<CfgF32, true>(&d.occ[0][1]);
+    if (rc == YAPD_OK) rc = prepare_kernel<CfgF32, false>(&d.occ[0][0]);
+    if (rc != YAPD_OK) return rc;
     d.init = true;
   }
   *out = &d;
@@ -1569,20 +1739,27 @@ static int fill_sampling(SampleParams& P, const yapd_sampling& s, const yapd_noi
   return YAPD_OK;
 }
 
+template <class C, bool CFG>
+static void launch_one(const SampleParams& P, int occ, int sms, int max_items, cudaStream_t st) {
+  int grid = sms * occ;
+  if (grid > max_items) grid = max_items;
+  if (grid < 1) grid = 1;
+  sample_kernel<C, CFG><<<grid, C::NT + 32, smem_bytes<C>(), st>>>(P);
+}
+
 static int launch_sample(const SampleParams& P, int dtype, int max_items, cudaStream_t st) {
   DevInfo* d = nullptr;
   int rc = device_info(&d);
   if (rc != YAPD_OK) return rc;
-  if (dtype == YAPD_DTYPE_BF16) {
-    int grid = d->sms * d->occ_bf16;
-    if (grid > max_items) grid = max_items;
-    if (grid < 1) grid = 1;
-    sample_kernel<CfgBF16><<<grid, CfgBF16::NT, smem_bytes<CfgBF16>(), st>>>(P);
+  const bool bf = dtype == YAPD_DTYPE_BF16;
+  const bool cfg = P.nb == 2;
+  const int occ = d->occ[bf ? 1 : 0][cfg ? 1 : 0];
+  if (bf) {
+    if (cfg) launch_one<CfgBF16, true>(P, occ, d->sms, max_items, st);
+    else launch_one<CfgBF16, false>(P, occ, d->sms, max_items, st);
   } else {
-    int grid = d->sms * d->occ_f32;
-    if (grid > max_items) grid = max_items;
-    if (grid < 1) grid = 1;
-    sample_kernel<CfgF32><<<grid, CfgF32::NT, smem_bytes<CfgF32>(), st>>>(P);
+    if (cfg) launch_one<CfgF32, true>(P, occ, d->sms, max_items, st);
+    else launch_one<CfgF32, false>(P, occ, d->sms, max_items, st);
   }
   return cudaGetLastError() == cudaSuccess ? YAPD_OK : YAPD_ERR_LAUNCH;
 }
@@ -1691,8 +1868,16 @@ int yapd_select_step(const yapd_select_args* a, void* stream) {
   init_outputs_kernel<<<(total + 255) / 256, 256, 0, st>>>(a->xt, a->is_commit, a->B, a->L, a->mask_id,
                                                            a->dense, a->sampled, a->pmi);
   if (cudaGetLastError() != cudaSuccess) return YAPD_ERR_LAUNCH;
+  // profiling events: inside a stream capture they must be external event
+  // nodes so that graph replays record timestamps
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (a->prof_event_begin || a->prof_event_end) cudaStreamIsCapturing(st, &cap);
+  const unsigned ev_flags = cap == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : 0u;
+  if (a->prof_event_begin)
+    cudaEventRecordWithFlags(static_cast<cudaEvent_t>(a->prof_event_begin), st, ev_flags);
   rc = launch_sample(P, a->logits_dtype, total, st);
   if (rc != YAPD_OK) return rc;
+  if (a->prof_event_end) cudaEventRecordWithFlags(static_cast<cudaEvent_t>(a->prof_event_end), st, ev_flags);
 
   UnmaskParams U{};
   U.xt = a->xt;

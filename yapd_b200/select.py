@@ -134,7 +134,8 @@ def select_step(logits: torch.Tensor, xt: torch.Tensor, k_step: torch.Tensor,
                 use_quantile: bool = True, gumbel_tok: torch.Tensor | None = None,
                 gumbel_pos: torch.Tensor | None = None, seed: int = 0, offset: int = 0,
                 zero_temp_greedy: bool = True, dense: bool = False,
-                out: SelectOutputs | None = None) -> SelectOutputs:
+                out: SelectOutputs | None = None,
+                prof_events: tuple | None = None) -> SelectOutputs:
     """One block-diffusion select step (``server/engine.py:533-612``).
 
     ``nb`` is 2 when ``cfg_scale > 0`` (conditional + unconditional rows) and 1
@@ -204,6 +205,8 @@ def select_step(logits: torch.Tensor, xt: torch.Tensor, k_step: torch.Tensor,
     a.n_unmask, a.n_mask_after = out.n_unmask.data_ptr(), out.n_mask_after.data_ptr()
     a.hit_eos, a.k_step_out = out.hit_eos.data_ptr(), out.k_step.data_ptr()
     a.is_commit_out = out.is_commit.data_ptr()
+    if prof_events is not None:
+        a.prof_event_begin, a.prof_event_end = prof_events[0].cuda_event, prof_events[1].cuda_event
     need = N.lib().yapd_select_workspace_size(B, L)
     ws = workspace(need, dev)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()

@@ -353,8 +353,8 @@ def run_ours(args, ws, rank, local):
         dist.all_reduce(sm_, op=dist.ReduceOp.SUM)
         ms_max, rows_all = float(mx[0]), float(sm_[1])
         # final gather of the committed block tokens (the only collective)
-        gathered = [torch.empty_like(R.xt) for _ in range(ws)]
-        dist.all_gather(gathered, R.xt)
+        from yapd_b200.shard import gather_committed
+        gather_committed(R.xt, R.xt.shape[0] * ws, dist)
         torch.cuda.synchronize()
     else:
         ms_max, rows_all = ms, float(my_rows)

@@ -93,3 +93,15 @@ def test_penalty_sign_rule():
     s = O.sample_tokens(g2, one, torch.zeros(1, dtype=torch.int32), one, torch.zeros(1),
                         torch.tensor([1.2]), torch.tensor([[True, False, False]]), torch.zeros(1, 3))
     assert s.item() == 1
+
+
+def test_philox_known_answers():
+    """Random123's published Philox4x32-10 known-answer vectors."""
+    from oracle.philox import philox4x32_10
+    cases = [((0, 0, 0, 0), (0, 0), (0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8)),
+             ((0xFFFFFFFF,) * 4, (0xFFFFFFFF, 0xFFFFFFFF), (0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD)),
+             ((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344), (0xA4093822, 0x299F31D0),
+              (0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1))]
+    for ctr, key, want in cases:
+        out = philox4x32_10(np.array([ctr], dtype=np.uint32), key)
+        assert tuple(int(x) for x in out[0]) == want

@@ -190,6 +190,24 @@ int yapd_select_step(const yapd_select_args* args, void* stream);
  */
 int yapd_sample_rows(const yapd_sample_args* args, void* stream);
 
+/* Positions (B * L) the no-allocation entry point accepts. */
+#define YAPD_NOALLOC_MAX_POSITIONS 16384
+
+/*
+ * yapd_select_step without a caller workspace, for callers that cannot
+ * allocate device memory (no cudaMalloc in their process: a foreign memory
+ * pool, an allocation-free serving loop, a sandbox with pre-registered
+ * buffers).  It has no counterpart in the reference.  Scratch comes from one
+ * fixed array in the library's device memory (about 192 KB per device, held
+ * until exit); args->workspace and args->workspace_bytes are ignored.
+ * B * L above YAPD_NOALLOC_MAX_POSITIONS returns YAPD_ERR_WORKSPACE.
+ * The first call on a device looks up that array's device address, so make
+ * it before any stream capture.  All calls share the array: calls whose
+ * kernels overlap on the GPU race.  The status word is cleared per call and
+ * is not readable through yapd_read_status.
+ */
+int yapd_select_step_noalloc(const yapd_select_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -26,8 +26,9 @@ YAPD_STATUS_INTERNAL = 2
 EXPORTED = [
     "yapd_abi_version", "yapd_status_string", "yapd_select_workspace_size",
     "yapd_sample_workspace_size", "yapd_clear_status", "yapd_read_status",
-    "yapd_select_step", "yapd_sample_rows",
+    "yapd_select_step", "yapd_sample_rows", "yapd_select_step_noalloc",
 ]
+YAPD_NOALLOC_MAX_POSITIONS = 16384
 
 
 class Sampling(C.Structure):
@@ -106,6 +107,8 @@ def lib():
     h.yapd_select_step.argtypes = [C.POINTER(SelectArgs), C.c_void_p]
     h.yapd_sample_rows.restype = C.c_int
     h.yapd_sample_rows.argtypes = [C.POINTER(SampleArgs), C.c_void_p]
+    h.yapd_select_step_noalloc.restype = C.c_int
+    h.yapd_select_step_noalloc.argtypes = [C.POINTER(SelectArgs), C.c_void_p]
     if h.yapd_abi_version() != 1:
         raise RuntimeError("yapd_select ABI version mismatch")
     _lib = h

@@ -1947,3 +1947,63 @@ int yapd_sample_rows(const yapd_sample_args* a, void* stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Select step for callers that cannot allocate device memory.
+//
+// Some hosts of this library cannot call cudaMalloc at all: a caller running
+// inside a memory pool or allocator it does not own, a real-time serving
+// loop that forbids allocation after start-up, or a sandbox that only hands
+// out pre-registered buffers.  For them, yapd_select_step_noalloc takes its
+// scratch (status word, work list and PMI inputs) from one fixed array in
+// the library's own device memory instead of a caller workspace.
+//
+// The array is sized for YAPD_NOALLOC_MAX_POSITIONS positions (B * L); every
+// GPU that loads the library holds it until the process exits.  All calls on
+// a device share it, and it keeps the previous call's contents: the status
+// word is cleared at the start of each call (the rest is fully rewritten
+// before it is read), and two calls whose kernels overlap on the GPU (on
+// different streams) race on it.
+// ---------------------------------------------------------------------------
+
+namespace yapd {
+
+constexpr size_t kNoAllocBytes =
+    256 + ((YAPD_NOALLOC_MAX_POSITIONS * sizeof(int32_t) + 255) & ~(size_t)255) +
+    ((YAPD_NOALLOC_MAX_POSITIONS * sizeof(float2) + 255) & ~(size_t)255);
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+// Device address of g_noalloc_scratch per device.  In host code the symbol
+// name is only a stand-in: the kernels need the address that
+// cudaGetSymbolAddress returns with the device current.
+static void* g_noalloc_ptr[64];
+
+static int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return YAPD_ERR_NO_DEVICE;
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return YAPD_ERR_LAUNCH;
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return YAPD_OK;
+}
+
+}  // namespace yapd
+
+extern "C" int yapd_select_step_noalloc(const yapd_select_args* args, void* stream) {
+  if (!args) return YAPD_ERR_NULL_POINTER;
+  if (args->B <= 0 || args->L <= 0) return YAPD_ERR_BAD_SHAPE;
+  if ((int64_t)args->B * (int64_t)args->L > (int64_t)YAPD_NOALLOC_MAX_POSITIONS) return YAPD_ERR_WORKSPACE;
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != YAPD_OK) return rc;
+  if (yapd_select_workspace_size(args->B, args->L) > kNoAllocBytes) return YAPD_ERR_WORKSPACE;
+  if (cudaMemsetAsync(scratch, 0, sizeof(uint32_t), (cudaStream_t)stream) != cudaSuccess) return YAPD_ERR_LAUNCH;
+  yapd_select_args a = *args;
+  a.workspace = scratch;
+  a.workspace_bytes = kNoAllocBytes;
+  return yapd_select_step(&a, stream);
+}

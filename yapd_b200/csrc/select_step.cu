@@ -19,6 +19,7 @@
 #include <math.h>
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "yapd_select.h"
 #include "philox.cuh"
@@ -28,27 +29,33 @@ namespace yapd {
 
 // ----------------------------------------------------------------- config
 
-template <int NT_, int NVT_, int W_, int ELEM_, int NSTAGE_, int CAP_, int MINB_>
+template <int NT_, int NG_, int W_, int ELEM_, int NSTAGE_>
 struct KCfg {
-  static constexpr int NT = NT_;        // compute threads per CTA (plus one producer warp)
-  static constexpr int NVT = NVT_;      // 16-byte vectors per thread per row
+  static constexpr int NT = NT_;        // compute threads per group (one position at a time)
+  static constexpr int NG = NG_;        // groups per CTA
   static constexpr int W = W_;          // elements per 16-byte vector
   static constexpr int ELEM = ELEM_;    // bytes per logit
   static constexpr int NSTAGE = NSTAGE_;
   static constexpr int BAND = NT_;      // candidate band capacity (one thread per element)
-  static constexpr int MINB = MINB_;    // CTAs per SM the launch bounds target
-  static constexpr int NS = NVT * W;    // element slots per thread per row
-  static constexpr int NW = NT / 32;
+  static constexpr int NW = NT / 32;    // warps per group
+  static constexpr int NTHREADS = NG * NT;
   static constexpr int ROW_SLOT = ((YAPD_MAX_V * ELEM + 32 + 127) / 128) * 128;
   static constexpr int STAGE_BYTES = 2 * ROW_SLOT;
   static constexpr bool BF16 = (ELEM == 2);
-  static_assert(NT * NVT * 16 >= YAPD_MAX_V * ELEM + 32, "row does not fit the thread tile");
+  static constexpr int KV = ((YAPD_MAX_V + 2 * W) / W + NT - 1) / NT;  // vectors per thread per row (max)
+  static_assert(NT % 32 == 0 && NT >= 64, "groups are whole warps");
+  static_assert(NSTAGE >= NG, "every group needs a stage");
 };
-using CfgBF16 = KCfg<224, 5, 8, 2, 3, 0, 2>;
-using CfgF32 = KCfg<480, 5, 4, 4, 3, 0, 1>;
+using CfgBF16 = KCfg<96, 4, 8, 2, 6>;
+using CfgF32 = KCfg<192, 2, 4, 4, 3>;
+
+// Thread index within its group, and the group index.
+template <class C>
+__device__ __forceinline__ int gtid() { return (int)(threadIdx.x % C::NT); }
+template <class C>
+__device__ __forceinline__ int gidx() { return threadIdx.x / C::NT; }
 
 constexpr uint64_t kWaitLimitNs = 500ull * 1000ull * 1000ull;  // 0.5 s per pipeline wait
-constexpr float kMinPMargin = 1e-3f;
 
 // Kernel parameters (flattened from the C ABI structs on the host).
 struct SampleParams {
@@ -116,27 +123,6 @@ __device__ __forceinline__ RowGeom row_geom(const SampleParams& P, int64_t elem_
 __device__ __forceinline__ float param_f(const float* a, float s, int b) { return a ? a[b] : s; }
 __device__ __forceinline__ int param_i(const int32_t* a, int s, int b) { return a ? a[b] : s; }
 
-// Word w of request b's history as a bitmap (bit v&31 of word v>>5).
-__device__ __forceinline__ uint32_t history_word(const SampleParams& P, int b, int w) {
-  if (P.history_kind == YAPD_HISTORY_BITMAP) {
-    const uint32_t* h = reinterpret_cast<const uint32_t*>(P.history) + (int64_t)b * P.history_stride;
-    return __ldg(h + w);
-  }
-  // one byte (bool) per token: pack 32 of them
-  const uint8_t* h = reinterpret_cast<const uint8_t*>(P.history) + (int64_t)b * P.history_stride;
-  uint32_t word = 0;
-  const int v0 = w * 32;
-  for (int j = 0; j < 32 && v0 + j < P.V; ++j) word |= (__ldg(h + v0 + j) != 0 ? 1u : 0u) << j;
-  return word;
-}
-
-__device__ __forceinline__ float token_noise(const SampleParams& P, int b, int pos_flat, int l, int v) {
-  if (P.noise_kind == YAPD_NOISE_EXPLICIT) {
-    return __ldg(P.gumbel_tok + (int64_t)b * P.gt_stride_req + (int64_t)l * P.gt_stride_pos + v);
-  }
-  return philox_token_gumbel(P.seed, P.offset, (uint32_t)pos_flat, (uint32_t)v);
-}
-
 // Repetition penalty of server/engine_ar.py:240: v>0 ? v/r : v*r.
 __device__ __forceinline__ float penalize(float v, float rep, float rrep) {
   return v > 0.0f ? div_rn(v, rep, rrep) : __fmul_rn(v, rep);
@@ -150,77 +136,10 @@ __device__ __forceinline__ int cand_id(unsigned long long c) { return 0x7fffffff
 __device__ __forceinline__ float cand_val(unsigned long long c) { return ord_key_inv((uint32_t)(c >> 32)); }
 
 // Shared memory layout.
-struct StageAux;
-
 template <class C>
 struct Smem;
-
-// Per-thread register tile of one row: NVT vectors of W elements, kept as
-// raw 16-byte words (bf16 pairs or fp32).
 template <class C>
-struct Tile {
-  uint4 v[C::NVT];
-  __device__ __forceinline__ float get(int k, int i) const {
-    const uint32_t* w = reinterpret_cast<const uint32_t*>(&v[k]);
-    if constexpr (C::BF16) {
-      return (i & 1) ? bf16hi(w[i >> 1]) : bf16lo(w[i >> 1]);
-    } else {
-      return __uint_as_float(w[i]);
-    }
-  }
-  __device__ __forceinline__ void set_neg_inf(int k, int i) {
-    uint32_t* w = reinterpret_cast<uint32_t*>(&v[k]);
-    if constexpr (C::BF16) {
-      if (i & 1) w[i >> 1] = (w[i >> 1] & 0x0000ffffu) | 0xff800000u;
-      else w[i >> 1] = (w[i >> 1] & 0xffff0000u) | 0x0000ff80u;
-    } else {
-      w[i] = 0xff800000u;
-    }
-  }
-  __device__ __forceinline__ void set(int k, int i, float f) {
-    uint32_t* w = reinterpret_cast<uint32_t*>(&v[k]);
-    if constexpr (C::BF16) {
-      const uint32_t h = __float_as_uint(f) >> 16;  // exact: f came from bf16
-      if (i & 1) w[i >> 1] = (w[i >> 1] & 0x0000ffffu) | (h << 16);
-      else w[i >> 1] = (w[i >> 1] & 0xffff0000u) | h;
-    } else {
-      w[i] = __float_as_uint(f);
-    }
-  }
-};
-
-// Per-thread maxima of the cond and uncond tiles (bf16 pairs compared packed).
-template <class C>
-__device__ __forceinline__ float2 tile_max2(const Tile<C>& tc, const Tile<C>& tu, bool cfg) {
-  if constexpr (C::BF16) {
-    const uint32_t ninf2 = 0xff80ff80u;
-    __nv_bfloat162 mc2 = *reinterpret_cast<const __nv_bfloat162*>(&ninf2);
-    __nv_bfloat162 mu2 = mc2;
-#pragma unroll
-    for (int k = 0; k < C::NVT; ++k) {
-      const uint32_t* a = reinterpret_cast<const uint32_t*>(&tc.v[k]);
-      const uint32_t* u = reinterpret_cast<const uint32_t*>(&tu.v[k]);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        mc2 = __hmax2(mc2, *reinterpret_cast<const __nv_bfloat162*>(&a[j]));
-        if (cfg) mu2 = __hmax2(mu2, *reinterpret_cast<const __nv_bfloat162*>(&u[j]));
-      }
-    }
-    const float mc = fmaxf(__bfloat162float(__low2bfloat16(mc2)), __bfloat162float(__high2bfloat16(mc2)));
-    const float mu = fmaxf(__bfloat162float(__low2bfloat16(mu2)), __bfloat162float(__high2bfloat16(mu2)));
-    return make_float2(mc, cfg ? mu : kNegInf);
-  } else {
-    float mc = kNegInf, mu = kNegInf;
-#pragma unroll
-    for (int k = 0; k < C::NVT; ++k)
-#pragma unroll
-      for (int i = 0; i < C::W; ++i) {
-        mc = fmaxf(mc, tc.get(k, i));
-        if (cfg) mu = fmaxf(mu, tu.get(k, i));
-      }
-    return make_float2(mc, mu);
-  }
-}
+struct KSmem;
 
 template <class C>
 __device__ __forceinline__ float load_elem_global(const char* row, int v) {
@@ -243,52 +162,53 @@ __device__ __forceinline__ float load_elem_smem(const unsigned char* s, const Ro
   }
 }
 
-// Load this thread's vectors of a row from the staged copy.  Element v of
-// vector k is j*W + i - head with j = tid + k*NT; invalid elements read -inf.
-// Returns a bitmask of vectors that contain any invalid or out-of-copy element.
+// ------------------------------------------------------------ streaming geometry
+//
+// The staged copy of a row starts `head` elements before element 0.  Vectors
+// (16 bytes) j in [j0, j1) lie wholly inside [0, avail) of both rows (the cond
+// and uncond copies share their head); the remaining elements, at most a few
+// per row end, are "scalar" elements e in [0, nscal) with id scalar_v(e).
+// When the two rows have different heads every element is scalar.
+struct Span {
+  int j0, j1;  // interior vectors
+  int head;    // elements before element 0 in vector 0
+  int nlo;     // scalar elements [0, nlo) ...
+  int hi0;     // ... and [hi0, V)
+  int nscal;
+};
+
+__device__ __forceinline__ int scalar_v(const Span& S, int e) { return e < S.nlo ? e : S.hi0 + (e - S.nlo); }
+
+// Element i of a 16-byte vector.
 template <class C>
-__device__ __forceinline__ uint32_t load_tile(Tile<C>& t, const unsigned char* s, const RowGeom& g, int V) {
-  uint32_t edge = 0;
-  const int tid = threadIdx.x;
-#pragma unroll
-  for (int k = 0; k < C::NVT; ++k) {
-    const int j = tid + k * C::NT;
-    const int v0 = j * C::W - g.head;
-    if ((uint32_t)(j * 16) < g.bytes) {
-      t.v[k] = *reinterpret_cast<const uint4*>(s + j * 16);
-    } else {
-      t.v[k] = make_uint4(0, 0, 0, 0);
-    }
-    const bool interior = v0 >= 0 && v0 + C::W <= g.avail;
-    if (!interior) {
-      edge |= 1u << k;
-#pragma unroll
-      for (int i = 0; i < C::W; ++i) {
-        const int v = v0 + i;
-        if (v < 0 || v >= V) t.set_neg_inf(k, i);
-        else if (v >= g.avail) t.set(k, i, load_elem_global<C>(g.row, v));
-      }
-    }
-  }
-  return edge;
+__device__ __forceinline__ float velem(const uint4& q, int i) {
+  const uint32_t w = (i / (C::BF16 ? 2 : 1)) == 0 ? q.x : (i / (C::BF16 ? 2 : 1)) == 1 ? q.y
+                   : (i / (C::BF16 ? 2 : 1)) == 2 ? q.z : q.w;
+  if constexpr (C::BF16) return (i & 1) ? bf16hi(w) : bf16lo(w);
+  else return __uint_as_float(w);
 }
 
-// Same element mapping as `ref_geom` for a row staged with a different head.
-template <class C>
-__device__ __forceinline__ void load_tile_rephase(Tile<C>& t, const unsigned char* s, const RowGeom& g,
-                                                  const RowGeom& ref, int V) {
-  const int tid = threadIdx.x;
-#pragma unroll
-  for (int k = 0; k < C::NVT; ++k) {
-    const int j = tid + k * C::NT;
-    const int v0 = j * C::W - ref.head;
-#pragma unroll
-    for (int i = 0; i < C::W; ++i) {
-      const int v = v0 + i;
-      if (v < 0 || v >= V) t.set_neg_inf(k, i);
-      else t.set(k, i, load_elem_smem<C>(s, g, v));
-    }
-  }
+__device__ __forceinline__ uint4 lds128(const unsigned char* p) { return *reinterpret_cast<const uint4*>(p); }
+
+__device__ __forceinline__ uint32_t bmax2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bmin2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("min.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float fmin3(float a, float b, float c) {
+  float r;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
 // ------------------------------------------------------------ worklist
@@ -330,7 +250,7 @@ __global__ void worklist_kernel(const int64_t* __restrict__ xt, const uint8_t* _
 // ------------------------------------------------------------ sample kernel
 
 template <class C>
-__device__ __forceinline__ void issue_item(const SampleParams& P, Smem<C>& sm, int stage, int pos) {
+__device__ __forceinline__ void issue_item(const SampleParams& P, KSmem<C>& ks, int stage, int pos) {
   const int b = pos / P.L, l = pos - b * P.L;
   const int64_t base = (int64_t)b * P.stride_req + (int64_t)l * P.stride_pos;
   const RowGeom gc = row_geom<C>(P, base);
@@ -340,9 +260,9 @@ __device__ __forceinline__ void issue_item(const SampleParams& P, Smem<C>& sm, i
     gu = row_geom<C>(P, base + P.stride_branch);
     bytes += gu.bytes;
   }
-  mbar_arrive_expect_tx(&sm.full[stage], bytes);
-  if (gc.bytes) bulk_g2s(sm.stage[stage], gc.src, gc.bytes, &sm.full[stage]);
-  if (P.nb == 2 && gu.bytes) bulk_g2s(sm.stage[stage] + C::ROW_SLOT, gu.src, gu.bytes, &sm.full[stage]);
+  mbar_arrive_expect_tx(&ks.full[stage], bytes);
+  if (gc.bytes) bulk_g2s(ks.stage[stage], gc.src, gc.bytes, &ks.full[stage]);
+  if (P.nb == 2 && gu.bytes) bulk_g2s(ks.stage[stage] + C::ROW_SLOT, gu.src, gu.bytes, &ks.full[stage]);
 }
 
 template <class C>
@@ -350,34 +270,36 @@ __device__ __forceinline__ int item_pos(const SampleParams& P, int idx) {
   return P.n_identity > 0 ? idx : P.work[idx];
 }
 
-// Barrier over the compute warps only (the producer/finisher warp never joins).
+// Barrier over the warps of this thread's group (named barrier 1 + group).
 template <class C>
 __device__ __forceinline__ void csync() {
-  named_sync(1, C::NT);
+  named_sync(1 + gidx<C>(), C::NT);
 }
 
-// OR of a predicate over the compute warps (one barrier).
+// OR of a predicate over the group (one barrier).
 template <class C>
 __device__ __forceinline__ bool csync_or(bool pred) {
   uint32_t r;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
       "setp.ne.u32 p, %1, 0;\n\t"
-      "barrier.cta.red.or.pred q, 1, %2, p;\n\t"
+      "barrier.cta.red.or.pred q, %2, %3, p;\n\t"
       "selp.u32 %0, 1, 0, q;\n\t}"
       : "=r"(r)
-      : "r"((uint32_t)pred), "n"(C::NT)
+      : "r"((uint32_t)pred), "r"(1 + gidx<C>()), "n"(C::NT)
       : "memory");
   return r != 0;
 }
 
 // ------------------------------------------------------------ per-position core
 //
-// Hot path (registers, fully unrolled): row maxima, the sums of exp(x - max),
-// and z2 = log2(e) * (guided / T) - const for every element, computed with two
-// FMAs from the cond/uncond logits; then either the unfiltered argmax, or the
-// min-p candidate band.  Cold paths (top-k / top-p bracketing, massive ties,
-// NaN rows) recompute z2 from the staged shared-memory rows in rolled loops.
+// Each position is worked by one group of warps from its staged rows in shared
+// memory.  Hot path (streaming 16-byte vectors): per-thread maxima, then the
+// sums of exp(x - max) and of 2^(z2 - ref) against per-thread references, with
+// z2 = log2(e) * (guided / T) - const computed with two FMAs from the
+// cond/uncond logits, merged across the group by rescaling; then the min-p
+// candidate band.  Cold paths (unfiltered argmax, top-k / top-p bracketing,
+// massive ties, NaN rows) recompute z2 element by element in rolled loops.
 // Every decision that the reference's float rounding can flip is taken on
 // exact values recomputed with the reference's op order (exact_val).
 
@@ -443,8 +365,8 @@ __device__ __forceinline__ float2 red_max2(float a, float c, Smem<C>& sm, int& s
   float* s = sm.red8 + slot * 8 * C::NW;
   slot ^= 1;
   if ((threadIdx.x & 31) == 0) {
-    s[threadIdx.x >> 5] = a;
-    s[C::NW + (threadIdx.x >> 5)] = c;
+    s[gtid<C>() >> 5] = a;
+    s[C::NW + (gtid<C>() >> 5)] = c;
   }
   csync<C>();
   float ra = s[0], rc = s[C::NW];
@@ -470,7 +392,7 @@ __device__ __forceinline__ unsigned long long red_max_u64(unsigned long long v, 
   }
   unsigned long long* s = sm.redu + slot * C::NW;
   slot ^= 1;
-  if ((threadIdx.x & 31) == 0) s[threadIdx.x >> 5] = v;
+  if ((threadIdx.x & 31) == 0) s[gtid<C>() >> 5] = v;
   csync<C>();
   unsigned long long r = s[0];
 #pragma unroll
@@ -485,7 +407,7 @@ __device__ __forceinline__ void block_sum8(float (&v)[8], Smem<C>& sm, int& slot
   for (int j = 0; j < 8; ++j) v[j] = warp_sum(v[j]);
   float* s = sm.red8 + slot * 8 * C::NW;
   slot ^= 1;
-  const int w = threadIdx.x >> 5;
+  const int w = gtid<C>() >> 5;
   if ((threadIdx.x & 31) == 0) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) s[j * C::NW + w] = v[j];
@@ -507,57 +429,53 @@ __device__ __forceinline__ float block_sum1(float v, Smem<C>& sm, int& slot) {
   return a[0];
 }
 
-__device__ __forceinline__ void lse2_merge(float& m, float& s, float m2, float s2) {
-  const float M = fmaxf(m, m2);
-  if (M == kNegInf || !(M == M)) {
-    s = s + s2;
-    m = M;
-    return;
-  }
-  s = __fadd_rn(__fmul_rn(s, ex2_approx(__fsub_rn(m, M))), __fmul_rn(s2, ex2_approx(__fsub_rn(m2, M))));
-  m = M;
-}
+// Group merge of per-thread (reference, sum) pairs: sum_t s_t * 2^(ref_t - M*scale)
+// with M the group maximum of the per-thread maxima m_t.  Threads whose
+// maximum is -inf hold s_t = 0 (or NaN) and are added unscaled.  Each warp
+// rescales to its own maximum first; one barrier; the warp records are then
+// merged the same way (the rounded products m*scale cancel level to level).
+// Also clears the group's band counter (sm.misc[0]).
+struct Stats3 {
+  float m[3];    // per-thread maxima (cond, uncond, z2) -> group maxima
+  float ref[3];  // per-thread references, m*scale rounded (0 when m is not finite)
+  float s[3];    // per-thread sums relative to ref -> group sums relative to the maxima
+};
 
-// Block reduction of the (Sc, Su) sums and the (zmax, S) log-sum-exp pair:
-// S is carried relative to each thread's own maximum and rescaled once per
-// level (warp, block).
 template <class C>
-__device__ __forceinline__ void block_reduce_sums(float& sc, float& su, float& zm, float& s, Smem<C>& sm,
-                                                  int& slot) {
-  const float zw = warp_max(zm);
-  // threads without a finite element carry s = 0 (or NaN) unscaled
-  float sw = (zm > kNegInf) ? __fmul_rn(s, ex2_approx(__fsub_rn(zm, zw))) : s;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    sc += __shfl_xor_sync(0xffffffffu, sc, o);
-    su += __shfl_xor_sync(0xffffffffu, su, o);
-    sw += __shfl_xor_sync(0xffffffffu, sw, o);
-  }
+__device__ __forceinline__ void group_merge3(Stats3& t, const float (&mscale)[3], Smem<C>& sm, int& slot) {
+  const float kPosInf = __int_as_float(0x7f800000);
+  const int w = gtid<C>() >> 5, lane = threadIdx.x & 31;
   float* b = sm.red8 + slot * 8 * C::NW;
   slot ^= 1;
-  const int w = threadIdx.x >> 5;
-  if ((threadIdx.x & 31) == 0) {
-    b[w] = sc;
-    b[C::NW + w] = su;
-    b[2 * C::NW + w] = zw;
-    b[3 * C::NW + w] = sw;
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const float Mw = warp_max(t.m[j]);
+    float s = t.s[j];
+    if (t.m[j] > kNegInf && Mw < kPosInf) s = __fmul_rn(s, ex2_approx(__fsub_rn(t.ref[j], __fmul_rn(Mw, mscale[j]))));
+    s = warp_sum(s);
+    if (lane == 0) {
+      b[j * C::NW + w] = Mw;
+      b[(3 + j) * C::NW + w] = s;
+    }
   }
   csync<C>();
-  sc = 0.f;
-  su = 0.f;
-  zm = kNegInf;
+  // every read of the previous position's band counter precedes this barrier,
+  // and the next band pass follows a later one
+  if (gtid<C>() == 0) sm.misc[0] = 0;
 #pragma unroll
-  for (int q = 0; q < C::NW; ++q) {
-    sc += b[q];
-    su += b[C::NW + q];
-    zm = fmaxf(zm, b[2 * C::NW + q]);
-  }
-  s = 0.f;
+  for (int j = 0; j < 3; ++j) {
+    const float mq = lane < C::NW ? b[j * C::NW + lane] : kNegInf;
+    const float sq = lane < C::NW ? b[(3 + j) * C::NW + lane] : 0.f;
+    float M = mq;
 #pragma unroll
-  for (int q = 0; q < C::NW; ++q) {
-    const float zq = b[2 * C::NW + q];
-    const float sq = b[3 * C::NW + q];
-    s += (zq > kNegInf) ? __fmul_rn(sq, ex2_approx(__fsub_rn(zq, zm))) : sq;
+    for (int o = 1; o < C::NW; o <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float f = sq;
+    if (mq > kNegInf && M < kPosInf)
+      f = __fmul_rn(sq, ex2_approx(__fsub_rn(__fmul_rn(mq, mscale[j]), __fmul_rn(M, mscale[j]))));
+#pragma unroll
+    for (int o = 1; o < C::NW; o <<= 1) f += __shfl_xor_sync(0xffffffffu, f, o);
+    t.m[j] = __shfl_sync(0xffffffffu, M, 0);
+    t.s[j] = __shfl_sync(0xffffffffu, f, 0);
   }
 }
 
@@ -579,25 +497,38 @@ __device__ __noinline__ float philox_noise_nl(uint64_t seed, uint64_t offset, in
   return philox_token_gumbel(seed, offset, (uint32_t)pos, (uint32_t)v);
 }
 
+// Token noise; INL inlines the Philox rounds (hot callers whose live
+// registers a call would spill), otherwise one out-of-line copy is shared.
+template <bool INL = false>
 __device__ __forceinline__ float noise_at(const SampleParams& P, int b, int pos, int l, int v) {
   if (P.noise_kind == YAPD_NOISE_EXPLICIT)
     return __ldg(P.gumbel_tok + (int64_t)b * P.gt_stride_req + (int64_t)l * P.gt_stride_pos + v);
+  if (INL) return philox_token_gumbel(P.seed, P.offset, (uint32_t)pos, (uint32_t)v);
   return philox_noise_nl(P.seed, P.offset, pos, v);
 }
 
+// Whether token v is in request b's history (bitmap word or byte, from global memory).
+__device__ __forceinline__ bool hist_bit(const SampleParams& P, int b, int v) {
+  if (P.history_kind == YAPD_HISTORY_BITMAP) {
+    const uint32_t* h = reinterpret_cast<const uint32_t*>(P.history) + (int64_t)b * P.history_stride;
+    return (__ldg(h + (v >> 5)) >> (v & 31)) & 1u;
+  }
+  const uint8_t* h = reinterpret_cast<const uint8_t*>(P.history) + (int64_t)b * P.history_stride;
+  return __ldg(h + v) != 0;
+}
+
 struct ScoreCtx {
-  const uint32_t* hist;  // request history bitmap in shared memory
   int b, pos, l;
   bool pen_on, noisy, turbo, minp_on;
   float rep, rrep;
   float r, minp_thr;  // min-p: keep iff 2^(z2-zmax) * r >= minp_thr
 };
 
-template <class C>
+template <class C, bool INL = false>
 __device__ __forceinline__ float exact_score(const SampleParams& P, const ScoreCtx& K, int v, float vals) {
   float s = vals;
-  if (K.pen_on && ((K.hist[v >> 5] >> (v & 31)) & 1u)) s = penalize(vals, K.rep, K.rrep);
-  if (K.noisy) s = __fadd_rn(s, noise_at(P, K.b, K.pos, K.l, v));
+  if (K.pen_on && hist_bit(P, K.b, v)) s = penalize(vals, K.rep, K.rrep);
+  if (K.noisy) s = __fadd_rn(s, noise_at<INL>(P, K.b, K.pos, K.l, v));
   return s;
 }
 
@@ -605,7 +536,7 @@ template <class C>
 __device__ __forceinline__ float approx_score(const SampleParams& P, const PosCtx& X, const ScoreCtx& K, int v,
                                               float z) {
   float va = __fmaf_rn(z, kLn2, X.Kval);
-  if (K.pen_on && ((K.hist[v >> 5] >> (v & 31)) & 1u)) va = va > 0.f ? __fmul_rn(va, K.rrep) : __fmul_rn(va, K.rep);
+  if (K.pen_on && hist_bit(P, K.b, v)) va = va > 0.f ? __fmul_rn(va, K.rrep) : __fmul_rn(va, K.rep);
   return K.noisy ? __fadd_rn(va, noise_at(P, K.b, K.pos, K.l, v)) : va;
 }
 
@@ -625,42 +556,6 @@ __device__ __forceinline__ int block_pick(const Pick& bp, bool turbo, Smem<C>& s
   return 0x7fffffff - (int)(uint32_t)w2;
 }
 
-// Hot argmax over the register tile: every valid element with z2 >= H kept
-// (and the min-p test), scored approximately, the near-best rescored exactly.
-// zat(s) recomputes slot s's z2 from the tiles (-inf for invalid slots).
-template <class C, class ZF>
-__device__ __forceinline__ int argmax_regs(const SampleParams& P, const PosCtx& X, const RowRef<C>& R, ZF zat,
-                                           int vbase, float H, const ScoreCtx& K, Pick bp, Smem<C>& sm,
-                                           int& slot) {
-  const int V = P.V;
-  // approximate score of slot s, -inf when not kept (recomputed on the second pass)
-  auto score_at = [&](int s) -> float {
-    const int v = vbase + (s / C::W) * C::NT * C::W + (s % C::W);
-    const float z = zat(s);
-    bool keep = v >= 0 && v < V && z >= H;
-    if (keep && K.minp_on) keep = __fmul_rn(ex2_approx(__fsub_rn(z, X.zmax)), K.r) >= K.minp_thr;
-    return keep ? approx_score<C>(P, X, K, v, z) : kNegInf;
-  };
-  float best = kNegInf;
-#pragma unroll
-  for (int s = 0; s < C::NS; ++s) best = fmaxf(best, score_at(s));
-  const float gbest = red_max1<C>(best, sm, slot);
-  if (gbest > kNegInf) {
-    const float thr = gbest - score_margin(gbest);
-#pragma unroll
-    for (int s = 0; s < C::NS; ++s) {
-      if (score_at(s) >= thr) {
-        const int v = vbase + (s / C::W) * C::NT * C::W + (s % C::W);
-        const float vals = exact_val<C>(P, X, R, v);
-        const float es = exact_score<C>(P, K, v, vals);
-        const Pick cand{es, vals, v};
-        if (es == es && es > kNegInf && pick_better(cand, bp, K.turbo)) bp = cand;
-      }
-    }
-  }
-  return block_pick<C>(bp, K.turbo, sm, slot);
-}
-
 // Cold argmax from the staged rows (rolled loop): elements with z2 >= H are
 // kept (min-p test included); elements with band_lo <= z2 < H are kept iff
 // their composite (exact value, -id) key is >= Xcomp.
@@ -671,7 +566,7 @@ __device__ __noinline__ int argmax_smem(const SampleParams& P, const PosCtx X, c
   int slot = 2;
   const int V = P.V;
   float best = kNegInf;
-  for (int v = threadIdx.x; v < V; v += C::NT) {
+  for (int v = gtid<C>(); v < V; v += C::NT) {
     const float z = z2_smem<C>(X, R, v);
     if (!(z >= H)) continue;
     if (K.minp_on && !(__fmul_rn(ex2_approx(__fsub_rn(z, X.zmax)), K.r) >= K.minp_thr)) continue;
@@ -679,7 +574,7 @@ __device__ __noinline__ int argmax_smem(const SampleParams& P, const PosCtx X, c
   }
   const float gbest = red_max1<C>(best, sm, slot);
   const float thr = gbest > kNegInf ? gbest - score_margin(gbest) : kBig;
-  for (int v = threadIdx.x; v < V; v += C::NT) {
+  for (int v = gtid<C>(); v < V; v += C::NT) {
     const float z = z2_smem<C>(X, R, v);
     const bool in_main = z >= H;
     const bool in_band = z >= band_lo && z < H;
@@ -704,7 +599,7 @@ __device__ __noinline__ int argmax_smem(const SampleParams& P, const PosCtx X, c
 template <class C>
 __device__ __forceinline__ Pick band_pick(const SampleParams& P, const ScoreCtx& K, int nband, Smem<C>& sm) {
   Pick bp{kNegInf, kNegInf, 0x7fffffff};
-  for (int q = threadIdx.x; q < nband; q += C::NT) {
+  for (int q = gtid<C>(); q < nband; q += C::NT) {
     if (!sm.cflag[q]) continue;
     const unsigned long long c = sm.cand[q];
     const int v = cand_id(c);
@@ -729,7 +624,7 @@ struct Band {
 // Sort sm.cand[0..n) descending with sm.cande alongside (one thread per element).
 template <class C>
 __device__ __forceinline__ void rank_sort(int n, Smem<C>& sm) {
-  const int tid = threadIdx.x;
+  const int tid = gtid<C>();
   unsigned long long key = 0ull;
   float ev = 0.f;
   int rank = 0;
@@ -764,41 +659,6 @@ __device__ __forceinline__ void band_push(unsigned long long* cand, float* cande
   }
 }
 
-// Hot band from registers: {z2 >= lo_z} (nothing above it), unsorted in
-// sm.cand (exact value, id) and sm.cande (2^(z2 - zmax)).  sm.misc[0] must be
-// zero on entry.  zat(s) recomputes slot s's z2 from the tiles.
-template <class C, class ZF>
-__device__ __forceinline__ int band_regs(const SampleParams& P, const PosCtx& X, const RowRef<C>& R, ZF zat,
-                                         int vbase, float lo_z, Smem<C>& sm) {
-  uint64_t cm = 0ull;
-#pragma unroll
-  for (int s = 0; s < C::NS; ++s) cm |= (zat(s) >= lo_z) ? (1ull << s) : 0ull;
-  const int lane = threadIdx.x & 31;
-  const int cnt = __popcll(cm);
-  int incl = cnt;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int n = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += n;
-  }
-  const int wtot = __shfl_sync(0xffffffffu, incl, 31);
-  int base = 0;
-  if (lane == 31 && wtot > 0) base = atomicAdd(&sm.misc[0], wtot);
-  base = __shfl_sync(0xffffffffu, base, 31) + incl - cnt;
-  while (cm) {
-    const int s = __ffsll((long long)cm) - 1;
-    cm &= cm - 1ull;
-    const int v = vbase + (s / C::W) * C::NT * C::W + (s % C::W);
-    if (base < C::BAND) {
-      sm.cand[base] = cand_key(exact_val<C>(P, X, R, v), v);
-      sm.cande[base] = ex2_approx(__fsub_rn(z2_smem<C>(X, R, v), X.zmax));
-    }
-    ++base;
-  }
-  csync<C>();
-  return sm.misc[0];
-}
-
 // Cold band from the staged rows: {lo_z <= z2 < hi_z}, with count and mass above hi_z.
 template <class C>
 __device__ __noinline__ Band band_smem(const SampleParams& P, const PosCtx X, const RowRef<C> R, float lo_z,
@@ -807,11 +667,11 @@ __device__ __noinline__ Band band_smem(const SampleParams& P, const PosCtx X, co
   int slot = 2;
   const int V = P.V;
   csync<C>();
-  if (threadIdx.x == 0) sm.misc[0] = 0;
+  if (gtid<C>() == 0) sm.misc[0] = 0;
   csync<C>();
   float na = 0.f, ma = 0.f;
   for (int v0 = 0; v0 < V; v0 += C::NT) {
-    const int v = v0 + threadIdx.x;
+    const int v = v0 + gtid<C>();
     float z = kNegInf;
     if (v < V) z = z2_smem<C>(X, R, v);
     const bool above = v < V && z >= hi_z;
@@ -845,7 +705,7 @@ __device__ __noinline__ Band band_smem(const SampleParams& P, const PosCtx X, co
 template <class C>
 __device__ __forceinline__ void band_flags(const Band& bd, bool use_k, int k_left, bool topp_on, float top_p,
                                            float r, bool minp_on, float minp_thr, Smem<C>& sm) {
-  const int tid = threadIdx.x;
+  const int tid = gtid<C>();
   if (tid < 32) {
     double run = (double)bd.m_above * (double)r;
     for (int q0 = 0; q0 < bd.n; q0 += 32) {
@@ -876,7 +736,7 @@ template <class C>
 __device__ __forceinline__ void stats4_smem(const PosCtx& X, const RowRef<C>& R, int V, const float (&t)[4],
                                             float (&cnt)[4], float (&mass)[4], Smem<C>& sm, int& slot) {
   float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  for (int v = threadIdx.x; v < V; v += C::NT) {
+  for (int v = gtid<C>(); v < V; v += C::NT) {
     const float z = z2_smem<C>(X, R, v);
     const float e = ex2_approx(__fsub_rn(z, X.zmax));
 #pragma unroll
@@ -959,7 +819,7 @@ __device__ __noinline__ unsigned long long overflow_resolve(const SampleParams& 
       while (lo < hi) {
         const unsigned long long mid = lo + (hi - lo) / 2ull + 1ull;
         float cnt = 0.f;
-        for (int v = threadIdx.x; v < V; v += C::NT) {
+        for (int v = gtid<C>(); v < V; v += C::NT) {
           const float z = z2_smem<C>(X, R, v);
           if (z >= lo_z && z < hi_z) cnt += (cand_key(exact_val<C>(P, X, R, v), v) >= mid) ? 1.f : 0.f;
         }
@@ -969,7 +829,7 @@ __device__ __noinline__ unsigned long long overflow_resolve(const SampleParams& 
       Xk = lo;
     }
     float m = 0.f;
-    for (int v = threadIdx.x; v < V; v += C::NT) {
+    for (int v = gtid<C>(); v < V; v += C::NT) {
       const float z = z2_smem<C>(X, R, v);
       if (z >= lo_z && z < hi_z && cand_key(exact_val<C>(P, X, R, v), v) >= Xk)
         m += ex2_approx(__fsub_rn(z, X.zmax));
@@ -984,7 +844,7 @@ __device__ __noinline__ unsigned long long overflow_resolve(const SampleParams& 
     while (lo < hi) {
       const unsigned long long mid = lo + (hi - lo) / 2ull;
       float m = 0.f;
-      for (int v = threadIdx.x; v < V; v += C::NT) {
+      for (int v = gtid<C>(); v < V; v += C::NT) {
         const float z = z2_smem<C>(X, R, v);
         if (z >= lo_z && z < hi_z) {
           const unsigned long long ck = cand_key(exact_val<C>(P, X, R, v), v);
@@ -1005,7 +865,7 @@ __device__ __noinline__ int first_nan_or_inf(const PosCtx X, const RowRef<C> R, 
   csync<C>();  // out-of-line reductions use scratch slots 2/3
   int slot = 2;
   int fn = 0x7fffffff, fi = 0x7fffffff;
-  for (int v = threadIdx.x; v < V; v += C::NT) {
+  for (int v = gtid<C>(); v < V; v += C::NT) {
     const float z = z2_smem<C>(X, R, v);
     if (!(z == z) && v < fn) fn = v;
     if (z == __int_as_float(0x7f800000) && v < fi) fi = v;
@@ -1028,7 +888,7 @@ __device__ __noinline__ int top1_smem(const SampleParams& P, const PosCtx X, con
   int slot = 2;
   unsigned long long best = 0ull;
   const float zlo = __fsub_rn(X.zmax, zmargin(X.zmax));
-  for (int v = threadIdx.x; v < P.V; v += C::NT) {
+  for (int v = gtid<C>(); v < P.V; v += C::NT) {
     const float z = z2_smem<C>(X, R, v);
     if (z >= zlo) {
       const unsigned long long k = cand_key(exact_val<C>(P, X, R, v), v);
@@ -1078,7 +938,7 @@ __device__ __noinline__ int select_cold(const SampleParams& P, const PosCtx X, c
     } else {
       k_left = topk_raw - (int)bk.n_above;
       float part = 0.f;
-      for (int q = threadIdx.x; q < bk.n && q < k_left; q += C::NT) part += sm.cande[q];
+      for (int q = gtid<C>(); q < bk.n && q < k_left; q += C::NT) part += sm.cande[q];
       Sn = __fadd_rn(bk.m_above, block_sum1<C>(part, sm, slot));
       K.r = __fdiv_rn(1.0f, Sn);
       Hk = bk.H;
@@ -1124,36 +984,43 @@ __device__ __noinline__ int select_cold(const SampleParams& P, const PosCtx X, c
   return c >= 0 ? c : top1_smem<C>(P, X, R, sm);
 }
 
-// Per-stage side data: request parameters and history (filled by the
-// producer warp when it issues the stage), and the hand-off record from the
-// compute warps to the finisher.
-struct StageAux {
-  int item;  // flat position b*L + l of the staged item
-  float T, top_p, min_p, rep;
-  int top_k;
-  int hist_ok;
-  int kind;  // 0: outputs written by the compute warps; 1: band for the finisher
-  int pos, b, l;
-  int topp_on, pen_on, noisy;
-  float r, rrep;
-  float mc, Sc, mu, Su;
-  uint32_t hist[(YAPD_MAX_V + 31) / 32 + 3];
-};
-
+// Per-group scratch: reduction slots (0/1: hot path, 2/3: out-of-line paths),
+// the band counter and the candidate band.
 template <class C>
 struct Smem {
-  uint64_t full[C::NSTAGE];  // rows + parameters landed
-  uint64_t hand[C::NSTAGE];  // compute warps done with the stage
-  uint64_t candfree;         // finisher done with the candidate band
-  float red8[4 * 8 * C::NW];  // slots 0/1: hot path, 2/3: out-of-line paths
+  float red8[4 * 8 * C::NW];
   unsigned long long redu[4 * C::NW];
   int misc[8];
   unsigned long long cand[C::BAND];
   float cande[C::BAND];
+  float2 cpc[32];             // PMI inputs of the first 32 band members
+  float cscore[32];           // their exact scores (penalty + noise)
+  unsigned short vzh[C::KV * C::NT];  // per vector: its largest z2' (fp16, rounded up)
   unsigned char cflag[C::BAND];
-  StageAux aux[C::NSTAGE];
+};
+
+template <class C>
+struct KSmem {
+  uint64_t full[C::NSTAGE];   // rows landed (one expect_tx arrive + the copy bytes)
+  uint64_t empty[C::NSTAGE];  // every warp of the consuming group is done with the stage
+  int issued[C::NSTAGE];      // copies armed on full[s] ...
+  int landed[C::NSTAGE];      // ... and waited for (read only after the final barrier)
+  Smem<C> g[C::NG];
   alignas(128) unsigned char stage[C::NSTAGE][C::STAGE_BYTES];
 };
+
+// softmax(c)[v], softmax(u)[v] as the reference rounds them (server/engine.py:539-540, 553, 556).
+template <class C, bool CFG>
+__device__ __forceinline__ float2 pmi_inputs(const PosCtx& X, const RowRef<C>& R, int v) {
+  const float cv = load_elem_smem<C>(R.sc, R.gc, v);
+  const float pc = __fmul_rn(expf(__fsub_rn(cv, X.mc)), __fdiv_rn(1.0f, X.Sc));
+  float pu = 0.f;
+  if (CFG) {
+    const float uv = load_elem_smem<C>(R.su, R.gu, v);
+    pu = __fmul_rn(expf(__fsub_rn(uv, X.mu)), __fdiv_rn(1.0f, X.Su));
+  }
+  return make_float2(pc, pu);
+}
 
 // Write the sampled id and the PMI inputs softmax(c)[s], softmax(u)[s]
 // (server/engine.py:539-540, 553, 556); the unmask kernel forms the PMI.
@@ -1162,125 +1029,445 @@ __device__ __forceinline__ void write_choice(const SampleParams& P, const RowRef
                                              float mc, float Sc, float mu, float Su) {
   P.sampled[pos] = chosen;
   if (P.pcu) {
-    const float cv = load_elem_smem<C>(R.sc, R.gc, chosen);
-    const float pc = __fmul_rn(expf(__fsub_rn(cv, mc)), __fdiv_rn(1.0f, Sc));
-    float pu = 0.f;
-    if (CFG) {
-      const float uv = load_elem_smem<C>(R.su, R.gu, chosen);
-      pu = __fmul_rn(expf(__fsub_rn(uv, mu)), __fdiv_rn(1.0f, Su));
-    }
-    P.pcu[pos] = make_float2(pc, pu);
+    PosCtx X;
+    X.mc = mc;
+    X.Sc = Sc;
+    X.mu = mu;
+    X.Su = Su;
+    P.pcu[pos] = pmi_inputs<C, CFG>(X, R, chosen);
   }
 }
 
 template <class C, bool CFG>
-__device__ __forceinline__ RowRef<C> row_ref(const SampleParams& P, Smem<C>& sm, int stage, int pos) {
+__device__ __forceinline__ RowRef<C> row_ref(const SampleParams& P, KSmem<C>& ks, int stage, int pos) {
   const int b = pos / P.L, l = pos - b * P.L;
   const int64_t base = (int64_t)b * P.stride_req + (int64_t)l * P.stride_pos;
   RowRef<C> R;
-  R.sc = sm.stage[stage];
-  R.su = sm.stage[stage] + C::ROW_SLOT;
+  R.sc = ks.stage[stage];
+  R.su = ks.stage[stage] + C::ROW_SLOT;
   R.gc = row_geom<C>(P, base);
   R.gu = CFG ? row_geom<C>(P, base + P.stride_branch) : R.gc;
   return R;
 }
 
-// Compute warps: one position.
 template <class C, bool CFG>
-__device__ __forceinline__ void compute_item(const SampleParams& P, Smem<C>& sm, int& slot, int stage, int pos,
-                                             int it) {
-  const int tid = threadIdx.x;
+__device__ __forceinline__ Span make_span(const RowRef<C>& R, int V) {
+  Span S;
+  if (CFG && R.gu.head != R.gc.head) {
+    S.j0 = S.j1 = 0;
+    S.head = 0;
+    S.nlo = 0;
+    S.hi0 = 0;
+    S.nscal = V;
+    return S;
+  }
+  const int head = R.gc.head;
+  const int avail = CFG ? min(R.gc.avail, R.gu.avail) : R.gc.avail;
+  S.head = head;
+  S.j0 = head > 0 ? 1 : 0;
+  S.nlo = min(S.j0 * C::W - head, V);
+  int j1 = (avail + head) / C::W;
+  if (j1 < S.j0) j1 = S.j0;
+  S.j1 = j1;
+  S.hi0 = max(j1 * C::W - head, S.nlo);
+  S.nscal = S.nlo + (V - S.hi0);
+  return S;
+}
+
+// Pass 1 of the two-pass form: this thread's maxima of c and u and minimum
+// of u (NaN ignored).
+template <class C, bool CFG>
+__device__ __forceinline__ void pass_max(const RowRef<C>& R, const Span& S, float& mc, float& mu, float& nu) {
+  const int tid = gtid<C>();
+  if constexpr (C::BF16) {
+    uint32_t c2 = 0xff80ff80u, u2 = 0xff80ff80u, n2 = 0x7f807f80u;
+#pragma unroll 4
+    for (int j = S.j0 + tid; j < S.j1; j += C::NT) {
+      const uint4 a = lds128(R.sc + j * 16);
+      c2 = bmax2(c2, bmax2(bmax2(a.x, a.y), bmax2(a.z, a.w)));
+      if (CFG) {
+        const uint4 q = lds128(R.su + j * 16);
+        u2 = bmax2(u2, bmax2(bmax2(q.x, q.y), bmax2(q.z, q.w)));
+        n2 = bmin2(n2, bmin2(bmin2(q.x, q.y), bmin2(q.z, q.w)));
+      }
+    }
+    mc = fmaxf(bf16lo(c2), bf16hi(c2));
+    mu = fmaxf(bf16lo(u2), bf16hi(u2));
+    nu = fminf(bf16lo(n2), bf16hi(n2));
+  } else {
+    float c0 = kNegInf, u0 = kNegInf, n0 = __int_as_float(0x7f800000);
+#pragma unroll 4
+    for (int j = S.j0 + tid; j < S.j1; j += C::NT) {
+      const uint4 a = lds128(R.sc + j * 16);
+      c0 = fmax3(c0, __uint_as_float(a.x), __uint_as_float(a.y));
+      c0 = fmax3(c0, __uint_as_float(a.z), __uint_as_float(a.w));
+      if (CFG) {
+        const uint4 q = lds128(R.su + j * 16);
+        u0 = fmax3(u0, __uint_as_float(q.x), __uint_as_float(q.y));
+        u0 = fmax3(u0, __uint_as_float(q.z), __uint_as_float(q.w));
+        n0 = fmin3(n0, __uint_as_float(q.x), __uint_as_float(q.y));
+        n0 = fmin3(n0, __uint_as_float(q.z), __uint_as_float(q.w));
+      }
+    }
+    mc = c0;
+    mu = u0;
+    nu = n0;
+  }
+  for (int e = tid; e < S.nscal; e += C::NT) {
+    const int v = scalar_v(S, e);
+    mc = fmaxf(mc, load_elem_smem<C>(R.sc, R.gc, v));
+    if (CFG) {
+      const float u = load_elem_smem<C>(R.su, R.gu, v);
+      mu = fmaxf(mu, u);
+      nu = fminf(nu, u);
+    }
+  }
+  if (!CFG) {
+    mu = kNegInf;
+    nu = 0.f;
+  }
+}
+
+// Exact maximum of z2' = A2*c - B2*u over this thread's elements (NaN
+// ignored); the reference point when the bound from pass 1 is unusable.
+template <class C, bool CFG>
+__device__ __noinline__ float thread_zmax(const PosCtx X, const RowRef<C> R, const Span S) {
+  const int tid = gtid<C>();
+  float m = kNegInf;
+  for (int j = S.j0 + tid; j < S.j1; j += C::NT) {
+    const uint4 a = lds128(R.sc + j * 16);
+    uint4 q = a;
+    if (CFG) q = lds128(R.su + j * 16);
+#pragma unroll
+    for (int i = 0; i < C::W; ++i) {
+      const float c = velem<C>(a, i);
+      m = fmaxf(m, CFG ? __fmaf_rn(c, X.A2, __fmul_rn(velem<C>(q, i), -X.B2)) : __fmul_rn(c, X.A2));
+    }
+  }
+  for (int e = tid; e < S.nscal; e += C::NT) {
+    const int v = scalar_v(S, e);
+    const float c = load_elem_smem<C>(R.sc, R.gc, v);
+    m = fmaxf(m, CFG ? __fmaf_rn(c, X.A2, __fmul_rn(load_elem_smem<C>(R.su, R.gu, v), -X.B2))
+                     : __fmul_rn(c, X.A2));
+  }
+  return m;
+}
+
+// Pass 2 of the two-pass form: sc = sum 2^(c*log2e + nmcL), su likewise,
+// s = sum 2^d and dmax = max d with d = A2*c - B2*u + nzr (NaN ignored in the
+// maximum, kept in the sums).  With `mark`, each vector's largest d is kept
+// (fp16, rounded up) in vzh for the band pass.
+template <class C, bool CFG>
+__device__ __forceinline__ void pass_sums(const PosCtx& X, const RowRef<C>& R, const Span& S, float nmcL,
+                                          float nmuL, float nzr, bool mark, Smem<C>& sm, float& sc, float& su,
+                                          float& s, float& dmax, int& nvec) {
+  const int tid = gtid<C>();
+  const float A2 = X.A2, nB2 = -X.B2;
+  float sc0 = 0.f, sc1 = 0.f, su0 = 0.f, su1 = 0.f, s0 = 0.f, s1 = 0.f, dm = kNegInf;
+  int k = 0;
+#pragma unroll 2
+  for (int j = S.j0 + tid; j < S.j1; j += C::NT, ++k) {
+    const uint4 a = lds128(R.sc + j * 16);
+    uint4 q = a;
+    if (CFG) q = lds128(R.su + j * 16);
+    float d[C::W];
+#pragma unroll
+    for (int i = 0; i < C::W; ++i) {
+      const float c = velem<C>(a, i);
+      d[i] = CFG ? __fmaf_rn(c, A2, __fmaf_rn(velem<C>(q, i), nB2, nzr)) : __fmaf_rn(c, A2, nzr);
+    }
+#pragma unroll
+    for (int i = 0; i < C::W; i += 2) {
+      sc0 += ex2_approx(__fmaf_rn(velem<C>(a, i), kLog2e, nmcL));
+      sc1 += ex2_approx(__fmaf_rn(velem<C>(a, i + 1), kLog2e, nmcL));
+      if (CFG) {
+        su0 += ex2_approx(__fmaf_rn(velem<C>(q, i), kLog2e, nmuL));
+        su1 += ex2_approx(__fmaf_rn(velem<C>(q, i + 1), kLog2e, nmuL));
+      }
+      s0 += ex2_approx(d[i]);
+      s1 += ex2_approx(d[i + 1]);
+    }
+    float vz = fmaxf(d[0], d[1]);
+#pragma unroll
+    for (int i = 2; i + 1 < C::W; i += 2) vz = fmax3(vz, d[i], d[i + 1]);
+    dm = fmaxf(dm, vz);
+    if (mark && k < C::KV) sm.vzh[k * C::NT + tid] = __half_as_ushort(__float2half_ru(vz));
+  }
+  for (int e = tid; e < S.nscal; e += C::NT) {
+    const int v = scalar_v(S, e);
+    const float c = load_elem_smem<C>(R.sc, R.gc, v);
+    sc0 += ex2_approx(__fmaf_rn(c, kLog2e, nmcL));
+    float dv;
+    if (CFG) {
+      const float u = load_elem_smem<C>(R.su, R.gu, v);
+      su0 += ex2_approx(__fmaf_rn(u, kLog2e, nmuL));
+      dv = __fmaf_rn(c, A2, __fmaf_rn(u, nB2, nzr));
+    } else {
+      dv = __fmaf_rn(c, A2, nzr);
+    }
+    dm = fmaxf(dm, dv);
+    s0 += ex2_approx(dv);
+  }
+  sc = sc0 + sc1;
+  su = su0 + su1;
+  s = s0 + s1;
+  dmax = dm;
+  nvec = k;
+}
+
+// Sum of 2^(A2*c - B2*u + nzr) alone (after an underflowed pass 2).
+template <class C, bool CFG>
+__device__ __noinline__ float pass_resum(const PosCtx X, const RowRef<C> R, const Span S, float nzr) {
+  const int tid = gtid<C>();
+  float s = 0.f;
+  for (int j = S.j0 + tid; j < S.j1; j += C::NT) {
+    const uint4 a = lds128(R.sc + j * 16);
+    uint4 q = a;
+    if (CFG) q = lds128(R.su + j * 16);
+#pragma unroll
+    for (int i = 0; i < C::W; ++i) {
+      const float c = velem<C>(a, i);
+      s += ex2_approx(CFG ? __fmaf_rn(c, X.A2, __fmaf_rn(velem<C>(q, i), -X.B2, nzr)) : __fmaf_rn(c, X.A2, nzr));
+    }
+  }
+  for (int e = tid; e < S.nscal; e += C::NT) {
+    const int v = scalar_v(S, e);
+    const float c = load_elem_smem<C>(R.sc, R.gc, v);
+    s += ex2_approx(CFG ? __fmaf_rn(c, X.A2, __fmaf_rn(load_elem_smem<C>(R.su, R.gu, v), -X.B2, nzr))
+                        : __fmaf_rn(c, X.A2, nzr));
+  }
+  return s;
+}
+
+// Add token v to the band: its exact value and mass, and for the first 32
+// members also its exact score (penalty + noise) and PMI inputs, so that the
+// finishing warp needs neither the staged rows nor global memory.
+template <class C, bool CFG>
+__device__ __forceinline__ void band_add(const SampleParams& P, const PosCtx& X, const RowRef<C>& R,
+                                         const ScoreCtx& K, int v, Smem<C>& sm) {
+  const int at = atomicAdd(&sm.misc[0], 1);
+  if (at < C::BAND) {
+    const float vals = exact_val<C>(P, X, R, v);
+    sm.cand[at] = cand_key(vals, v);
+    sm.cande[at] = ex2_approx(__fsub_rn(z2_smem<C>(X, R, v), X.zmax));
+    if (at < 32) {
+      sm.cscore[at] = exact_score<C, true>(P, K, v, vals);
+      sm.cpc[at] = pmi_inputs<C, CFG>(X, R, v);
+    }
+  }
+}
+
+// The min-p band {z2 >= lo_z} from the vectors pass 2 marked (and
+// every scalar element), unsorted in sm.cand (exact value, id) and sm.cande
+// (2^(z2 - zmax)); returns its size (may exceed BAND).  sm.misc[0] must be
+// zero on entry.
+template <class C, bool CFG>
+__device__ __forceinline__ int band_marked(const SampleParams& P, const PosCtx& X, const RowRef<C>& R,
+                                           const ScoreCtx& K, const Span& S, uint32_t marks, float lo_z,
+                                           Smem<C>& sm) {
+  const int tid = gtid<C>();
+  while (marks) {
+    const int k = __ffs(marks) - 1;
+    marks &= marks - 1u;
+    const int j = S.j0 + tid + k * C::NT;
+    const uint4 a = lds128(R.sc + j * 16);
+    uint4 q = a;
+    if (CFG) q = lds128(R.su + j * 16);
+    uint32_t m = 0;
+#pragma unroll
+    for (int i = 0; i < C::W; ++i) {
+      const float z = z2_of(X, velem<C>(a, i), CFG ? velem<C>(q, i) : 0.f);
+      m |= (z >= lo_z ? 1u : 0u) << i;
+    }
+    const int v0 = j * C::W - S.head;
+    while (m) {
+      const int i = __ffs(m) - 1;
+      m &= m - 1u;
+      band_add<C, CFG>(P, X, R, K, v0 + i, sm);
+    }
+  }
+  for (int e = tid; e < S.nscal; e += C::NT) {
+    const int v = scalar_v(S, e);
+    if (z2_smem<C>(X, R, v) >= lo_z) band_add<C, CFG>(P, X, R, K, v, sm);
+  }
+  csync<C>();
+  return sm.misc[0];
+}
+
+// One warp resolves a band of at most 32 candidates: top-p / min-p flags
+// from prefix sums over the exactly sorted band, exact scores (penalty +
+// noise), argmax; the winner's PMI inputs were recorded with the band.
+template <class C>
+__device__ __forceinline__ void finish_band(const SampleParams& P, const Smem<C>& sm, int n, const ScoreCtx& K,
+                                            bool topp_on, float top_p, float min_p) {
+  const int lane = threadIdx.x & 31;
+  unsigned long long key = lane < n ? sm.cand[lane] : 0ull;
+  int q = lane;
+  // bitonic sort, descending, over the smallest power of two >= n lanes
+  int kmax = 2;
+  while (kmax < n) kmax <<= 1;
+  for (int k = 2; k <= kmax; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const unsigned long long y = __shfl_xor_sync(0xffffffffu, key, j);
+      const int qy = __shfl_xor_sync(0xffffffffu, q, j);
+      const bool up = ((lane & k) == 0) || k == kmax;
+      const bool lower = ((lane & j) == 0);
+      const bool take_max = (up == lower);
+      if (take_max ? (y > key) : (y < key)) {
+        key = y;
+        q = qy;
+      }
+    }
+  }
+  const bool live = lane < n;
+  const int v = cand_id(key);
+  const float vals = cand_val(key);
+  const float e = live ? sm.cande[q] : 0.f;
+  const float p = __fmul_rn(e, K.r);
+  double incl = (double)p;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  const float p0 = __shfl_sync(0xffffffffu, p, 0);
+  bool keep = live;
+  if (topp_on) keep = keep && (__fsub_rn((float)incl, p) < top_p);
+  keep = keep && (p >= __fmul_rn(min_p, p0));
+  float sc = keep ? sm.cscore[q] : kNegInf;
+  if (!(sc == sc)) sc = kNegInf;
+  const uint32_t ks = sc > kNegInf ? ord_key(sc) : 0u;
+  unsigned long long rec = ks ? (((unsigned long long)ks << 32) | (uint32_t)(31 - lane)) : 0ull;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long x = __shfl_xor_sync(0xffffffffu, rec, o);
+    rec = x > rec ? x : rec;
+  }
+  const int win_lane = rec ? 31 - (int)(uint32_t)(rec & 0xffffffffu) : 0;
+  if (lane == win_lane) {
+    int chosen = v;
+    float2 pcu = live ? sm.cpc[q] : make_float2(0.f, 0.f);
+    if (!live || chosen < 0 || chosen >= P.V) {
+      atomicOr(P.status, (unsigned)YAPD_STATUS_INTERNAL);
+      chosen = 0;
+    }
+    P.sampled[K.pos] = chosen;
+    if (P.pcu) P.pcu[K.pos] = pcu;
+  }
+}
+
+// Per-request sampling parameters of one position.
+struct ItemParams {
+  int pos;
+  float T, top_p, min_p, rep;
+  int top_k;
+};
+
+__device__ __forceinline__ ItemParams load_params(const SampleParams& P, int pos) {
+  ItemParams q;
+  const int b = pos / P.L;
+  q.pos = pos;
+  q.T = param_f(P.temperature, P.temperature_s, b);
+  q.top_k = param_i(P.top_k, P.top_k_s, b);
+  q.top_p = param_f(P.top_p, P.top_p_s, b);
+  q.min_p = param_f(P.min_p, P.min_p_s, b);
+  q.rep = param_f(P.rep_penalty, P.rep_penalty_s, b);
+  return q;
+}
+
+// One position, worked by the calling group.
+template <class C, bool CFG>
+__device__ __forceinline__ void compute_item(const SampleParams& P, KSmem<C>& ks, Smem<C>& sm, int& slot,
+                                             int stage, const ItemParams& Q) {
+  const int tid = gtid<C>();
   const int V = P.V;
+  const int pos = Q.pos;
   const int b = pos / P.L, l = pos - b * P.L;
-  const RowRef<C> R = row_ref<C, CFG>(P, sm, stage, pos);
-  StageAux& A = sm.aux[stage];
+  const RowRef<C> R = row_ref<C, CFG>(P, ks, stage, pos);
+  const float kPosInf = __int_as_float(0x7f800000);
+  const float kNaN = __int_as_float(0x7fc00000);
   PosCtx X;
   X.cfg = CFG;
-  X.T = A.T;
-  const int topk_raw = A.top_k;
-  const float top_p = A.top_p;
-  const float min_p = A.min_p;
-  const float rep = A.rep;
-  const bool pen_on = A.hist_ok && rep != 1.0f;
+  X.T = Q.T;
+  const int topk_raw = Q.top_k;
+  const float top_p = Q.top_p;
+  const float min_p = Q.min_p;
+  const float rep = Q.rep;
+  const bool pen_on = P.history_kind != YAPD_HISTORY_NONE && P.history != nullptr && rep != 1.0f;
   X.scale = X.T > 0.0f;
   X.rT = X.scale ? __fdiv_rn(1.0f, X.T) : 1.0f;
-
-  // ---- registers: cond and uncond tiles ----
-  Tile<C> tc, tu;
-  const uint32_t edge = load_tile<C>(tc, R.sc, R.gc, V);
-  if (CFG) {
-    if (R.gu.head == R.gc.head) load_tile<C>(tu, R.su, R.gu, V);
-    else load_tile_rephase<C>(tu, R.su, R.gu, R.gc, V);
-  }
-  const int vbase = tid * C::W - R.gc.head;
-
-  // ---- row maxima ----
-  const float2 ml = tile_max2<C>(tc, tu, CFG);
-  const float2 mx = red_max2<C>(ml.x, ml.y, sm, slot);
-  X.mc = mx.x;
-  X.mu = CFG ? mx.y : 0.f;
-
-  // ---- sums of exp(x - max) and z2 = log2(e)*guided/T - const ----
   const float w = P.cfg_w;
   const float sA = X.scale ? X.rT : 1.0f;
   X.A2 = CFG ? __fmul_rn(__fmul_rn(kLog2e, P.cfg_1pw), sA) : __fmul_rn(kLog2e, sA);
   X.B2 = CFG ? __fmul_rn(__fmul_rn(kLog2e, w), sA) : 0.f;
-  X.K2 = CFG ? __fmaf_rn(-X.mc, X.A2, __fmul_rn(X.mu, X.B2)) : __fmul_rn(-X.mc, X.A2);
-  const float mcL = __fmul_rn(X.mc, kLog2e), muL = __fmul_rn(X.mu, kLog2e);
-  float sc_t = 0.f, su_t = 0.f, zm_t = kNegInf;
-  // z2 of slot (k, i), -inf outside the row (recomputed where needed: two FMAs)
-  auto zat = [&](int s) -> float {
-    const int k = s / C::W, i = s % C::W;
-    float z = z2_of(X, tc.get(k, i), CFG ? tu.get(k, i) : 0.f);
-    if ((edge >> k) & 1u) {
-      const int v = (tid + k * C::NT) * C::W - R.gc.head + i;
-      if (v < 0 || v >= V) z = kNegInf;
-    }
-    return z;
+  const Span S = make_span<C, CFG>(R, V);
+  const bool topk_on = topk_raw > 0 && topk_raw < V;
+  const bool topp_on = top_p < 1.0f;
+  const bool minp_on = min_p > 0.0f;
+  const bool band_mode = minp_on && !topk_on;
+  const float lg_minp = band_mode ? fminf(log2f(min_p), 0.f) : 0.f;
+
+  // the stage goes back to the ring once every warp is done reading it
+  auto release = [&]() {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&ks.empty[stage]);
   };
-#pragma unroll
-  for (int k = 0; k < C::NVT; ++k)
-#pragma unroll
-    for (int i = 0; i < C::W; ++i) {
-      const float c = tc.get(k, i);
-      sc_t += ex2_approx(__fmaf_rn(c, kLog2e, -mcL));
-      float u = 0.f;
-      if (CFG) {
-        u = tu.get(k, i);
-        su_t += ex2_approx(__fmaf_rn(u, kLog2e, -muL));
-      }
-      zm_t = fmaxf(zm_t, z2_of(X, c, u));  // invalid slots give NaN or -inf: ignored
-    }
-  float s_t = 0.f;
+
+  // ---- pass 1: this thread's maxima ----
+  float mc_t, mu_t, nu_t;
+  pass_max<C, CFG>(R, S, mc_t, mu_t, nu_t);
+  const float mcr = (mc_t > kNegInf && mc_t < kPosInf) ? mc_t : 0.f;
+  const float mur = (mu_t > kNegInf && mu_t < kPosInf) ? mu_t : 0.f;
+  // reference for the z2' sum: the bound A2*max(c) - B2*min(u) >= every z2'
+  float zr;
+  if (X.A2 >= 0.f && X.B2 >= 0.f && mc_t > kNegInf && mc_t < kPosInf &&
+      (!CFG || (nu_t > kNegInf && nu_t < kPosInf))) {
+    zr = CFG ? __fmaf_rn(mc_t, X.A2, __fmul_rn(-X.B2, nu_t)) : __fmul_rn(mc_t, X.A2);
+  } else {
+    zr = thread_zmax<C, CFG>(X, R, S);
+  }
+  if (!(zr > kNegInf)) zr = 0.f;
+
+  // ---- pass 2: sums against the thread references; merged over the group ----
+  Stats3 st;
+  int nvec;
   {
-    // relative to this thread's maximum (0 when it has no finite element, so
-    // that a NaN still propagates)
-    const float zr = zm_t > kNegInf ? zm_t : 0.f;
-#pragma unroll
-    for (int s = 0; s < C::NS; ++s) s_t += ex2_approx(__fsub_rn(zat(s), zr));
+    float sc, su, s, dmax;
+    pass_sums<C, CFG>(X, R, S, -__fmul_rn(mcr, kLog2e), -__fmul_rn(mur, kLog2e), -zr, band_mode, sm, sc, su, s,
+                      dmax, nvec);
+    if (s == 0.f && dmax > kNegInf && dmax < kPosInf) {
+      // every term underflowed against the bound: use the exact thread maximum
+      // (the fp16 vector marks stay relative to the first reference)
+      s = pass_resum<C, CFG>(X, R, S, -__fadd_rn(zr, dmax));
+      st.ref[2] = __fadd_rn(zr, dmax);
+    } else {
+      st.ref[2] = zr;
+    }
+    st.m[0] = mc_t;
+    st.ref[0] = __fmul_rn(mcr, kLog2e);
+    st.s[0] = sc;
+    st.m[1] = CFG ? mu_t : kNegInf;
+    st.ref[1] = __fmul_rn(mur, kLog2e);
+    st.s[1] = su;
+    st.m[2] = dmax > kNegInf ? __fadd_rn(zr, dmax) : kNegInf;
+    st.s[2] = s;
   }
-  if (tid == 0) {
-    // the finisher must be done with the previous band before it is reused
-    if (it > 0 && !mbar_wait_bounded(&sm.candfree, (uint32_t)(it - 1) & 1u, kWaitLimitNs))
-      atomicOr(P.status, (unsigned)YAPD_STATUS_WAIT_TIMEOUT);
-    sm.misc[0] = 0;
-  }
-  block_reduce_sums<C>(sc_t, su_t, zm_t, s_t, sm, slot);
-  X.Sc = sc_t;
-  X.Su = su_t;
-  X.zmax = zm_t;
-  X.S = s_t;
+  const float mscale[3] = {kLog2e, kLog2e, 1.0f};
+  group_merge3<C>(st, mscale, sm, slot);
+  X.mc = st.m[0];
+  X.mu = CFG ? st.m[1] : 0.f;
+  X.Sc = (X.mc > kNegInf && X.mc < kPosInf) ? st.s[0] : kNaN;
+  X.Su = CFG ? ((X.mu > kNegInf && X.mu < kPosInf) ? st.s[1] : kNaN) : 0.f;
+  X.K2 = CFG ? __fmaf_rn(-X.mc, X.A2, __fmul_rn(X.mu, X.B2)) : __fmul_rn(-X.mc, X.A2);
+  X.zmax = __fadd_rn(st.m[2], X.K2);
+  X.S = (st.m[2] < kPosInf && st.s[2] < kPosInf) ? st.s[2] : kNaN;
   X.lc = logf(X.Sc);
   X.lu = CFG ? logf(X.Su) : 0.f;
   X.Kval = CFG ? __fmul_rn(__fsub_rn(__fmul_rn(w, X.lu), __fmul_rn(P.cfg_1pw, X.lc)), sA)
                : __fmul_rn(X.mc, sA);
 
   // ---- token choice ----
-  const bool topk_on = topk_raw > 0 && topk_raw < V;
-  const bool topp_on = top_p < 1.0f;
-  const bool minp_on = min_p > 0.0f;
   ScoreCtx K;
-  K.hist = A.hist;
   K.b = b;
   K.pos = pos;
   K.l = l;
@@ -1303,29 +1490,28 @@ __device__ __forceinline__ void compute_item(const SampleParams& P, Smem<C>& sm,
     chosen = f < 0 ? 0 : f;
   } else if (!topk_on && !topp_on && !minp_on) {
     // every token kept: server/engine.py:546-550 (or the penalty-only chain)
-    chosen = argmax_regs<C>(P, X, R, zat, vbase, -kBig, K, none, sm, slot);
+    chosen = argmax_smem<C>(P, X, R, -kBig, kBig, 0ull, K, none, sm);
     if (chosen < 0) chosen = 0;
   } else {
-    if (minp_on && !topk_on) {
-      const float zm = fminf(__fadd_rn(X.zmax, log2f(min_p)), X.zmax);
-      const int n = band_regs<C>(P, X, R, zat, vbase, __fsub_rn(zm, zmargin(zm)), sm);
-      if (n <= 32) {
-        // hand the short band to the finisher warp
-        if (tid == 0) {
-          A.kind = 1;
-          A.pos = pos;
-          A.b = b;
-          A.l = l;
-          A.topp_on = topp_on;
-          A.pen_on = K.pen_on;
-          A.noisy = K.noisy;
-          A.r = K.r;
-          A.rrep = K.rrep;
-          A.mc = X.mc;
-          A.Sc = X.Sc;
-          A.mu = X.mu;
-          A.Su = X.Su;
+    if (band_mode) {
+      const float zm = __fadd_rn(X.zmax, lg_minp);
+      const float lo_z = __fsub_rn(zm, zmargin(zm));
+      // vectors whose largest z2' can reach the band (z2' = z2 - K2 up to rounding)
+      uint32_t marks = 0u;
+      {
+        const float zmp = __fadd_rn(st.m[2], lg_minp);
+        const float thr = __fsub_rn(__fsub_rn(__fsub_rn(zmp, zmargin(zmp)),
+                                              __fadd_rn(1e-3f, __fmul_rn(4e-6f, __fadd_rn(fabsf(X.K2), fabsf(zmp))))),
+                                    zr);  // relative to this thread's reference, as stored
+        for (int k = 0; k < nvec; ++k) {
+          const bool hit = k >= C::KV || __half2float(__ushort_as_half(sm.vzh[k * C::NT + tid])) >= thr;
+          marks |= (hit ? 1u : 0u) << k;
         }
+      }
+      const int n = band_marked<C, CFG>(P, X, R, K, S, marks, lo_z, sm);
+      if (n <= 32) {
+        release();
+        if (tid < 32) finish_band<C>(P, sm, n, K, topp_on, top_p, min_p);
         handed = true;
       } else if (n <= C::BAND) {
         rank_sort<C>(n, sm);
@@ -1347,177 +1533,86 @@ __device__ __forceinline__ void compute_item(const SampleParams& P, Smem<C>& sm,
       chosen = select_cold<C>(P, X, R, K, topk_raw, topk_on, topp_on, top_p, min_p, sm);
     }
   }
-  if (!handed && tid == 0) {
-    if (chosen < 0 || chosen >= V) {
-      atomicOr(P.status, (unsigned)YAPD_STATUS_INTERNAL);
-      chosen = 0;
-    }
-    A.kind = 0;
-    write_choice<C, CFG>(P, R, pos, chosen, X.mc, X.Sc, X.mu, X.Su);
-  }
-}
-
-// Finisher: resolve a band of at most 32 candidates: top-p / min-p flags from
-// prefix sums over the exactly sorted band, exact scores (penalty + noise),
-// argmax, and the PMI inputs of the winner.
-template <class C, bool CFG>
-__device__ __forceinline__ void finish_band(const SampleParams& P, Smem<C>& sm, const StageAux& A,
-                                            const RowRef<C>& R) {
-  const int lane = threadIdx.x & 31;
-  const int n = sm.misc[0];
-  unsigned long long key = lane < n ? sm.cand[lane] : 0ull;
-  int q = lane;
-#pragma unroll
-  for (int k = 2; k <= 32; k <<= 1) {
-#pragma unroll
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      const unsigned long long y = __shfl_xor_sync(0xffffffffu, key, j);
-      const int qy = __shfl_xor_sync(0xffffffffu, q, j);
-      const bool up = ((lane & k) == 0);
-      const bool lower = ((lane & j) == 0);
-      const bool take_max = (up == lower);
-      if (take_max ? (y > key) : (y < key)) {
-        key = y;
-        q = qy;
+  if (!handed) {
+    if (tid == 0) {
+      if (chosen < 0 || chosen >= V) {
+        atomicOr(P.status, (unsigned)YAPD_STATUS_INTERNAL);
+        chosen = 0;
       }
+      write_choice<C, CFG>(P, R, pos, chosen, X.mc, X.Sc, X.mu, X.Su);
     }
-  }
-  const bool live = lane < n;
-  const int v = cand_id(key);
-  const float vals = cand_val(key);
-  const float e = live ? sm.cande[q] : 0.f;
-  const float p = __fmul_rn(e, A.r);
-  double incl = (double)p;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const double t = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += t;
-  }
-  const float p0 = __shfl_sync(0xffffffffu, p, 0);
-  bool keep = live;
-  if (A.topp_on) keep = keep && (__fsub_rn((float)incl, p) < A.top_p);
-  keep = keep && (p >= __fmul_rn(A.min_p, p0));
-  float sc = kNegInf;
-  if (keep) {
-    sc = vals;
-    if (A.pen_on && ((A.hist[v >> 5] >> (v & 31)) & 1u)) sc = penalize(vals, A.rep, A.rrep);
-    if (A.noisy) sc = __fadd_rn(sc, noise_at(P, A.b, A.pos, A.l, v));
-  }
-  if (!(sc == sc)) sc = kNegInf;
-  const uint32_t ks = sc > kNegInf ? ord_key(sc) : 0u;
-  unsigned long long rec = ks ? (((unsigned long long)ks << 32) | (uint32_t)(31 - lane)) : 0ull;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const unsigned long long x = __shfl_xor_sync(0xffffffffu, rec, o);
-    rec = x > rec ? x : rec;
-  }
-  const int win_lane = rec ? 31 - (int)(uint32_t)(rec & 0xffffffffu) : 0;
-  if (lane == win_lane) {
-    int chosen = v;
-    if (!live || chosen < 0 || chosen >= P.V) {
-      atomicOr(P.status, (unsigned)YAPD_STATUS_INTERNAL);
-      chosen = 0;
-    }
-    write_choice<C, CFG>(P, R, A.pos, chosen, A.mc, A.Sc, A.mu, A.Su);
+    release();
   }
 }
 
-// Producer: bulk copies of the position's rows plus its parameters and history.
+// One CTA per SM: NG groups of NT threads, each working one position at a
+// time from a shared NSTAGE-deep ring of staged rows.  Local item `it` (the
+// CTA's it-th position) uses stage it % NSTAGE and group it % NG; the group
+// that releases a stage issues the copies of item it + NSTAGE into it.
 template <class C, bool CFG>
-__device__ __forceinline__ void produce_item(const SampleParams& P, Smem<C>& sm, int stage, int pos) {
-  const int lane = threadIdx.x & 31;
-  if (lane == 0) issue_item<C>(P, sm, stage, pos);
-  const int b = pos / P.L;
-  StageAux& A = sm.aux[stage];
-  if (lane == 0) {
-    A.item = pos;
-    A.T = param_f(P.temperature, P.temperature_s, b);
-    A.top_k = param_i(P.top_k, P.top_k_s, b);
-    A.top_p = param_f(P.top_p, P.top_p_s, b);
-    A.min_p = param_f(P.min_p, P.min_p_s, b);
-    A.rep = param_f(P.rep_penalty, P.rep_penalty_s, b);
-    A.hist_ok = (P.history_kind != YAPD_HISTORY_NONE && P.history != nullptr) ? 1 : 0;
-  }
-  const float rep = param_f(P.rep_penalty, P.rep_penalty_s, b);
-  if (P.history_kind != YAPD_HISTORY_NONE && P.history != nullptr && rep != 1.0f) {
-    const int hwords = (P.V + 31) >> 5;
-    constexpr int kPer = ((YAPD_MAX_V + 31) / 32 + 31) / 32;
-    uint32_t hw[kPer];
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int wd = lane + 32 * j;
-      hw[j] = wd < hwords ? history_word(P, b, wd) : 0u;
-    }
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int wd = lane + 32 * j;
-      if (wd < hwords) A.hist[wd] = hw[j];
-    }
-  }
-  __syncwarp();
-  if (lane == 0) mbar_arrive(&sm.full[stage]);
-}
-
-template <class C, bool CFG>
-__global__ void __launch_bounds__(C::NT + 32, C::MINB) sample_kernel(const SampleParams P) {
+__global__ void __launch_bounds__(C::NTHREADS, 1) sample_kernel(const SampleParams P) {
   extern __shared__ unsigned char smem_raw[];
-  Smem<C>& sm = *reinterpret_cast<Smem<C>*>(
+  KSmem<C>& ks = *reinterpret_cast<KSmem<C>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
   const int n_items = P.n_identity > 0 ? P.n_identity : *P.work_count;
   const int first = blockIdx.x, stride = gridDim.x;
   if (first >= n_items) return;
   const int n_my = (n_items - first + stride - 1) / stride;
-  const bool finisher = threadIdx.x >= C::NT;
-  if (threadIdx.x == C::NT) {
+  if (threadIdx.x == 0) {
     for (int s = 0; s < C::NSTAGE; ++s) {
-      mbar_init(&sm.full[s], 2);        // expect_tx arrive + parameters arrive
-      mbar_init(&sm.hand[s], C::NW);    // one arrive per compute warp
+      mbar_init(&ks.full[s], 1);
+      mbar_init(&ks.empty[s], C::NW);
+      ks.issued[s] = 0;
+      ks.landed[s] = 0;
     }
-    mbar_init(&sm.candfree, 1);
     fence_mbar_init();
   }
   __syncthreads();
-  if (finisher) {
-    for (int s = 0; s < C::NSTAGE && s < n_my; ++s)
-      produce_item<C, CFG>(P, sm, s, item_pos<C>(P, first + s * stride));
-    for (int it = 0; it < n_my; ++it) {
-      const int stage = it % C::NSTAGE;
-      const uint32_t parity = (uint32_t)(it / C::NSTAGE) & 1u;
-      if (!mbar_wait_bounded(&sm.hand[stage], parity, kWaitLimitNs)) {
-        // the compute warps stopped: record it and give the copies still in
-        // flight (items it .. it+NSTAGE-1) a bounded chance to land
-        if ((threadIdx.x & 31) == 0) {
-          atomicOr(P.status, (unsigned)YAPD_STATUS_WAIT_TIMEOUT);
-          for (int q = it; q < n_my && q < it + C::NSTAGE; ++q)
-            (void)mbar_wait_bounded(&sm.full[q % C::NSTAGE], (uint32_t)(q / C::NSTAGE) & 1u, kWaitLimitNs);
-        }
-        break;
-      }
-      const StageAux& A = sm.aux[stage];
-      if (A.kind == 1) {
-        const RowRef<C> R = row_ref<C, CFG>(P, sm, stage, A.pos);
-        finish_band<C, CFG>(P, sm, A, R);
-      }
-      __syncwarp();
-      if ((threadIdx.x & 31) == 0) mbar_arrive(&sm.candfree);
-      if (it + C::NSTAGE < n_my) {
-        if ((threadIdx.x & 31) == 0) fence_proxy_async_smem();
-        __syncwarp();
-        produce_item<C, CFG>(P, sm, stage, item_pos<C>(P, first + (it + C::NSTAGE) * stride));
-      }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::NSTAGE && s < n_my; ++s) {
+      issue_item<C>(P, ks, s, item_pos<C>(P, first + s * stride));
+      ks.issued[s] = 1;
     }
-    return;
   }
+  const int g = gidx<C>();
+  const int tid = gtid<C>();
+  Smem<C>& sm = ks.g[g];
   int slot = 0;
-  for (int it = 0; it < n_my; ++it) {
+  ItemParams Q;
+  if (g < n_my) Q = load_params(P, item_pos<C>(P, first + g * stride));
+  for (int it = g; it < n_my; it += C::NG) {
     const int stage = it % C::NSTAGE;
     const uint32_t parity = (uint32_t)(it / C::NSTAGE) & 1u;
-    const bool ok = mbar_wait_bounded(&sm.full[stage], parity, kWaitLimitNs);
+    // positions of the items this group prefetches or issues next
+    const int nxt = it + C::NG;
+    const int ref_it = it + C::NSTAGE;
+    const int refill_pos = (tid == 32 && ref_it < n_my) ? item_pos<C>(P, first + ref_it * stride) : 0;
+    const bool ok = mbar_wait_bounded(&ks.full[stage], parity, kWaitLimitNs);
     if (!ok) atomicOr(P.status, (unsigned)YAPD_STATUS_WAIT_TIMEOUT);
-    if (csync_or<C>(!ok)) return;
-    compute_item<C, CFG>(P, sm, slot, stage, sm.aux[stage].item, it);
-    __syncwarp();
-    if ((threadIdx.x & 31) == 0) mbar_arrive(&sm.hand[stage]);
+    if (csync_or<C>(!ok)) break;
+    if (tid == 0) atomicAdd(&ks.landed[stage], 1);
+    ItemParams Qn;
+    if (nxt < n_my) Qn = load_params(P, item_pos<C>(P, first + nxt * stride));
+    compute_item<C, CFG>(P, ks, sm, slot, stage, Q);
+    // warp 1 refills the stage once the whole group has released it
+    if (tid == 32 && ref_it < n_my) {
+      if (mbar_wait_bounded(&ks.empty[stage], parity, kWaitLimitNs)) {
+        fence_proxy_async_smem();
+        issue_item<C>(P, ks, stage, refill_pos);
+        atomicAdd(&ks.issued[stage], 1);
+      } else {
+        atomicOr(P.status, (unsigned)YAPD_STATUS_WAIT_TIMEOUT);
+      }
+    }
+    Q = Qn;
+  }
+  // copies issued but never waited for (only after a timeout): give them a
+  // bounded chance to land before the CTA exits
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::NSTAGE; ++s)
+      for (int q = ks.landed[s]; q < ks.issued[s]; ++q)
+        (void)mbar_wait_bounded(&ks.full[s], (uint32_t)q & 1u, kWaitLimitNs);
   }
 }
 
@@ -1668,7 +1763,7 @@ __global__ void unmask_kernel(const UnmaskParams U) {
 
 template <class C>
 constexpr size_t smem_bytes() {
-  return sizeof(Smem<C>) + 128;
+  return sizeof(KSmem<C>) + 128;
 }
 
 struct DevInfo {
@@ -1684,7 +1779,7 @@ static int prepare_kernel(int* occ) {
   if (cudaFuncSetAttribute(sample_kernel<C, CFG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem_bytes<C>()) != cudaSuccess)
     return YAPD_ERR_LAUNCH;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(occ, sample_kernel<C, CFG>, C::NT + 32, smem_bytes<C>()) !=
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(occ, sample_kernel<C, CFG>, C::NTHREADS, smem_bytes<C>()) !=
       cudaSuccess)
     return YAPD_ERR_LAUNCH;
   return *occ >= 1 ? YAPD_OK : YAPD_ERR_LAUNCH;
@@ -1744,7 +1839,7 @@ static void launch_one(const SampleParams& P, int occ, int sms, int max_items, c
   int grid = sms * occ;
   if (grid > max_items) grid = max_items;
   if (grid < 1) grid = 1;
-  sample_kernel<C, CFG><<<grid, C::NT + 32, smem_bytes<C>(), st>>>(P);
+  sample_kernel<C, CFG><<<grid, C::NTHREADS, smem_bytes<C>(), st>>>(P);
 }
 
 static int launch_sample(const SampleParams& P, int dtype, int max_items, cudaStream_t st) {

@@ -45,9 +45,13 @@ struct KCfg {
   static constexpr int KV = ((YAPD_MAX_V + 2 * W) / W + NT - 1) / NT;  // vectors per thread per row (max)
   static_assert(NT % 32 == 0 && NT >= 64, "groups are whole warps");
   static_assert(NSTAGE >= NG, "every group needs a stage");
+  // Group g waits on full[s] for items g, g + NG, ...; consecutive phases of
+  // one stage must go to the same group, or a wait could be posted two phases
+  // ahead of the barrier (a parity wait would then pass at once).
+  static_assert(NSTAGE % NG == 0, "the groups must divide the stages");
 };
-using CfgBF16 = KCfg<96, 4, 8, 2, 6>;
-using CfgF32 = KCfg<192, 2, 4, 4, 3>;
+using CfgBF16 = KCfg<128, 3, 8, 2, 6>;
+using CfgF32 = KCfg<128, 3, 4, 4, 3>;
 
 // Thread index within its group, and the group index.
 template <class C>

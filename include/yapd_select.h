@@ -180,7 +180,9 @@ int yapd_read_status(const void* workspace, void* stream, uint32_t* status_out);
  * One select step.  Replaces server/engine.py:533-612 (the select body and
  * state update of FlashEngine._step_gpu, called from FlashEngine.tick at
  * server/engine.py:634); cache_len / blk_start advancement stays with the
- * caller.
+ * caller.  Two kernel launches: token selection (which also builds the work
+ * list and initialises the outputs of unsampled positions), then the
+ * per-request state update.
  */
 int yapd_select_step(const yapd_select_args* args, void* stream);
 

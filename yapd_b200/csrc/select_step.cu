@@ -1,14 +1,17 @@
 // Block-diffusion select step for B200 (sm_100a).
 //
-// Kernels (all launched on the caller's stream, no host sync, no allocation):
-//   worklist_kernel  compacts the positions that need a token (masked, non-commit)
-//   sample_kernel    one persistent CTA per SM slot; each position's cond and
-//                    uncond logit rows are staged into shared memory by 1-D bulk
-//                    copies (cp.async.bulk + mbarrier, a 3-deep ring) and held in
-//                    registers; CFG, temperature, filters, Gumbel-max and PMI are
-//                    computed with block reductions (no sort of the vocabulary)
-//   unmask_kernel    one warp per request: position noise, quantile threshold,
-//                    count schedule, rank, unmask and the state update
+// Two kernels, launched on the caller's stream (no host sync, no allocation).
+// sample_kernel runs one CTA per SM.  For the select step every CTA first
+// scans the block state (which positions are masked in a denoising request),
+// writes its own work-list entries and initialises the outputs of the
+// positions it will not sample.  Three groups of four warps then work
+// positions from a 6-deep ring of staged rows: each position's cond and
+// uncond logit rows are staged into shared memory by 1-D bulk copies
+// (cp.async.bulk + mbarrier); CFG, temperature, filters, Gumbel-max and the
+// PMI inputs come from two statistics passes and a candidate band (no sort of
+// the vocabulary).  unmask_kernel then runs one warp per request: position
+// noise, quantile threshold, count schedule, rank, unmask and the state
+// update.
 //
 // Reference semantics: server/engine.py:533-612 and server/engine_ar.py:220-243
 // of m8than/yapd (see include/yapd_select.h).  The file is compiled with
@@ -61,6 +64,33 @@ __device__ __forceinline__ int gidx() { return threadIdx.x / C::NT; }
 
 constexpr uint64_t kWaitLimitNs = 500ull * 1000ull * 1000ull;  // 0.5 s per pipeline wait
 
+// Parameters of the block-state update (server/engine.py:559-612).
+struct UnmaskParams {
+  const int64_t* xt;
+  const int64_t* k_step;
+  const uint8_t* is_commit;
+  const int64_t* sched_t;
+  const float* q_t;
+  const int32_t* sampled;
+  const float2* pcu;
+  const float* log_prior;
+  float pmi_lambda, cfg_w, cfg_1pw;
+  int nb;
+  float* pmi;
+  const float* gumbel_pos;
+  int noise_kind;
+  uint64_t seed, offset;
+  int B, L, K;
+  int64_t mask_id, stop_id;
+  int pos_noise, use_quantile;
+  int64_t* xt_out;
+  int32_t* n_unmask;
+  int32_t* n_mask_after;
+  uint8_t* hit_eos;
+  int64_t* k_step_out;
+  uint8_t* is_commit_out;
+};
+
 // Kernel parameters (flattened from the C ABI structs on the host).
 struct SampleParams {
   // logits
@@ -68,9 +98,7 @@ struct SampleParams {
   const char* logits_end;  // one past the last byte the call may read
   int64_t stride_req, stride_branch, stride_pos;
   int B, nb, L, V;
-  // work: positions p = b*L + l; `work` lists them, `work_count` counts them
-  const int32_t* work;
-  const int32_t* work_count;
+  // work: positions p = b*L + l, listed in work_w (select step)
   int n_identity;  // >0: items are 0..n_identity-1 (no work list)
   // sampling
   const float* temperature;
@@ -95,6 +123,12 @@ struct SampleParams {
   int32_t* sampled;
   float2* pcu;  // softmax(c)[s], softmax(u)[s] of the sampled token (PMI inputs), or null
   uint32_t* status;
+  // select step: the CTAs build the work list themselves and initialise the
+  // outputs of the positions they do not sample
+  int fused;
+  int dense;                // every position is sampled
+  int32_t* work_w;          // work list (each CTA writes its own entries)
+  UnmaskParams U;
 };
 
 struct RowGeom {
@@ -215,40 +249,183 @@ __device__ __forceinline__ float fmin3(float a, float b, float c) {
   return r;
 }
 
-// ------------------------------------------------------------ worklist
+// Total order used to rank PMI: NaN above +inf (torch's sort order).
+__device__ __forceinline__ uint32_t rank_key(float f) {
+  return (f != f) ? 0xffffffffu : ord_key(f);
+}
 
-__global__ void worklist_kernel(const int64_t* __restrict__ xt, const uint8_t* __restrict__ is_commit,
-                                int B, int L, int64_t mask_id, int dense, int32_t* __restrict__ work,
-                                int32_t* __restrict__ count) {
-  __shared__ int warp_cnt[32];
-  __shared__ int base_s;
-  const int total = B * L;
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  const int nw = blockDim.x >> 5;
-  if (threadIdx.x == 0) base_s = 0;
-  __syncthreads();
-  for (int p0 = 0; p0 < total; p0 += blockDim.x) {
-    const int p = p0 + threadIdx.x;
-    bool act = false;
-    if (p < total) {
-      const int b = p / L;
-      act = dense ? true : (is_commit[b] == 0 && xt[p] == mask_id);
+// Whether position p is sampled this step (masked in a denoising request).
+__device__ __forceinline__ bool pos_active(const UnmaskParams& U, int dense, int p) {
+  return dense || (U.is_commit[p / U.L] == 0 && U.xt[p] == U.mask_id);
+}
+
+// Block-state update of request b by one warp: server/engine.py:559-612.
+// Only positions sampled this step (pos_active) read `sampled` and `pcu`.
+__device__ __forceinline__ void unmask_request(const UnmaskParams& U, int dense, int b) {
+  const int lane = threadIdx.x & 31;
+  const int L = U.L, K = U.K;
+  const bool in = lane < L;
+  const int p = b * L + lane;
+  const int64_t x = in ? U.xt[p] : 0;
+  const bool is_mask = in && x == U.mask_id;
+  const bool commit = U.is_commit[b] != 0;
+  const bool denoise = !commit;
+  const int64_t ks = U.k_step[b];
+  int kc = (int)(ks < (int64_t)(K - 1) ? ks : (int64_t)(K - 1));
+  if (kc < 0) kc = 0;
+  // PMI of the sampled token (server/engine.py:553-558, calibration.py:58-60)
+  // and the position noise on masked positions (server/engine.py:559-561)
+  float pm = 0.f;
+  const int smp = (in && pos_active(U, dense, p)) ? U.sampled[p] : -1;
+  if (smp >= 0) {
+    const float2 pr = U.pcu[p];
+    const float lpl = __fmul_rn(U.pmi_lambda, __ldg(U.log_prior + smp));
+    pm = __fsub_rn(logf(fmaxf(pr.x, 1e-8f)), lpl);
+    if (U.nb == 2) {
+      const float pmi_u = __fsub_rn(logf(fmaxf(pr.y, 1e-8f)), lpl);
+      pm = __fsub_rn(__fmul_rn(U.cfg_1pw, pm), __fmul_rn(U.cfg_w, pmi_u));
     }
-    const unsigned bal = __ballot_sync(0xffffffffu, act);
-    if (lane == 0) warp_cnt[w] = __popc(bal);
-    __syncthreads();
-    int off = 0, tot = 0;
-    for (int q = 0; q < nw; ++q) {
-      const int c = warp_cnt[q];
-      off += (q < w) ? c : 0;
-      tot += c;
-    }
-    if (act) work[base_s + off + __popc(bal & ((1u << lane) - 1u))] = p;
-    __syncthreads();
-    if (threadIdx.x == 0) base_s += tot;
-    __syncthreads();
   }
-  if (threadIdx.x == 0) *count = base_s;
+  if (is_mask) {
+    if (U.pos_noise) {
+      const float gn = (U.noise_kind == YAPD_NOISE_EXPLICIT)
+                           ? U.gumbel_pos[p]
+                           : philox_position_gumbel(U.seed, U.offset, (uint32_t)p);
+      pm = __fadd_rn(pm, gn);
+    }
+  }
+  const unsigned mbal = __ballot_sync(0xffffffffu, is_mask);
+  const int m = __popc(mbal);
+  // ascending sort of masked PMI (+inf elsewhere), engine.py:566
+  const uint32_t ak = is_mask ? rank_key(pm) : ord_key(__int_as_float(0x7f800000));
+  uint32_t srt = ak;
+#pragma unroll
+  for (int kk = 2; kk <= 32; kk <<= 1) {
+#pragma unroll
+    for (int j = kk >> 1; j > 0; j >>= 1) {
+      const uint32_t y = __shfl_xor_sync(0xffffffffu, srt, j);
+      const bool up = ((lane & kk) == 0);
+      const bool lower = ((lane & j) == 0);
+      const bool take_min = (up == lower);
+      srt = take_min ? min(srt, y) : max(srt, y);
+    }
+  }
+  const float asc = (srt == 0xffffffffu) ? __int_as_float(0x7fc00000) : ord_key_inv(srt);
+  // quantile by linear interpolation (engine.py:567-572)
+  const float q = U.q_t[kc];
+  const float pq = __fmul_rn(q, (float)(m - 1 > 0 ? m - 1 : 0));
+  int lo = (int)floorf(pq), hi = (int)ceilf(pq);
+  lo = lo < 0 ? 0 : (lo > 31 ? 31 : lo);
+  hi = hi < 0 ? 0 : (hi > 31 ? 31 : hi);
+  const float v_lo = __shfl_sync(0xffffffffu, asc, lo);
+  const float v_hi = __shfl_sync(0xffffffffu, asc, hi);
+  const float tau = __fadd_rn(v_lo, __fmul_rn(__fsub_rn(pq, (float)lo), __fsub_rn(v_hi, v_lo)));
+  int n_quant = __popc(__ballot_sync(0xffffffffu, is_mask && pm >= tau));
+  if (!U.use_quantile) n_quant = 0;
+  const int64_t sch = U.sched_t[kc];
+  const int n_sched = (int)(sch < (int64_t)m ? sch : (int64_t)m);
+  int n_un = min(max(n_sched, n_quant), m);
+  if (ks >= (int64_t)(K - 1)) n_un = m;
+  if (m == 0) n_un = 0;
+  // rank among masked positions by PMI descending, ties to the lower position (engine.py:581-584)
+  const uint32_t mk = rank_key(pm);
+  int rank = 0;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const uint32_t kj = __shfl_sync(0xffffffffu, mk, j);
+    const bool mj = (mbal >> j) & 1u;
+    rank += (mj && (kj > mk || (kj == mk && j < lane))) ? 1 : 0;
+  }
+  const bool do_un = is_mask && rank < n_un;
+  int64_t xf = x;
+  if (denoise && do_un) xf = (int64_t)U.sampled[p];
+  if (in) {
+    U.xt_out[p] = xf;
+    if (smp >= 0) U.pmi[p] = pm;
+  }
+  const int n_after = __popc(__ballot_sync(0xffffffffu, in && xf == U.mask_id));
+  const bool eos = __any_sync(0xffffffffu, in && xf == U.stop_id);
+  if (lane == 0) {
+    const int64_t k_new = denoise ? ks + 1 : ks;
+    const int64_t k_fin = commit ? 0 : k_new;
+    const bool to_commit = denoise && !eos && (n_after == 0 || k_fin >= (int64_t)K);
+    U.n_unmask[b] = denoise ? n_un : 0;
+    U.n_mask_after[b] = n_after;
+    U.hit_eos[b] = eos ? 1 : 0;
+    U.k_step_out[b] = k_fin;
+    U.is_commit_out[b] = to_commit ? 1 : 0;
+  }
+}
+
+// One warp per request: the block-state update after the sample kernel.
+__global__ void unmask_kernel(const __grid_constant__ UnmaskParams U, int dense) {
+  const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (b < U.B) unmask_request(U, dense, b);
+}
+
+// Select step, preamble run by every CTA: scan the block state (warps own
+// contiguous spans of positions), count the sampled positions and write the
+// work-list entries this CTA will process (entries blockIdx + k*gridDim);
+// initialise the outputs of the unsampled positions p == blockIdx (mod
+// gridDim) (sampled -1, pmi NaN).  Returns the number of sampled positions.
+__device__ int cta_prepare(const SampleParams& P, int* scan) {
+  const UnmaskParams& U = P.U;
+  const int total = U.B * U.L;
+  const int nwarp = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int grid = (int)gridDim.x, me = (int)blockIdx.x;
+  // warp w owns positions [w*span, (w+1)*span), read 32 at a time; the
+  // ballots of the first kRounds rounds are kept (longer spans read again)
+  constexpr int kRounds = 32;
+  const int span = (((total + nwarp - 1) / nwarp) + 31) & ~31;
+  const int w0 = min(w * span, total), w1 = min(w0 + span, total);
+  unsigned masks[kRounds];
+  int cnt = 0;
+#pragma unroll
+  for (int r = 0; r < kRounds; ++r) {
+    const int p = w0 + r * 32 + lane;
+    masks[r] = __ballot_sync(0xffffffffu, p < w1 && pos_active(U, P.dense, p));
+    cnt += __popc(masks[r]);
+  }
+  for (int p0 = w0 + kRounds * 32; p0 < w1; p0 += 32) {
+    const int p = p0 + lane;
+    cnt += __popc(__ballot_sync(0xffffffffu, p < w1 && pos_active(U, P.dense, p)));
+  }
+  if (lane == 0) scan[w] = cnt;
+  __syncthreads();
+  int base = 0, tot = 0;
+  for (int q = 0; q < nwarp; ++q) {
+    const int c = scan[q];
+    base += q < w ? c : 0;
+    tot += c;
+  }
+  const unsigned lt = (1u << lane) - 1u;
+#pragma unroll
+  for (int r = 0; r < kRounds; ++r) {
+    const int p = w0 + r * 32 + lane;
+    const bool a = (masks[r] >> lane) & 1u;
+    const int idx = base + __popc(masks[r] & lt);
+    if (a && idx % grid == me) P.work_w[idx] = p;
+    if (!a && p < w1 && p % grid == me) {
+      P.sampled[p] = -1;
+      U.pmi[p] = __int_as_float(0x7fc00000);
+    }
+    base += __popc(masks[r]);
+  }
+  for (int p0 = w0 + kRounds * 32; p0 < w1; p0 += 32) {
+    const int p = p0 + lane;
+    const bool a = p < w1 && pos_active(U, P.dense, p);
+    const unsigned m = __ballot_sync(0xffffffffu, a);
+    const int idx = base + __popc(m & lt);
+    if (a && idx % grid == me) P.work_w[idx] = p;
+    if (!a && p < w1 && p % grid == me) {
+      P.sampled[p] = -1;
+      U.pmi[p] = __int_as_float(0x7fc00000);
+    }
+    base += __popc(m);
+  }
+  __syncthreads();
+  return tot;
 }
 
 // ------------------------------------------------------------ sample kernel
@@ -271,7 +448,7 @@ __device__ __forceinline__ void issue_item(const SampleParams& P, KSmem<C>& ks, 
 
 template <class C>
 __device__ __forceinline__ int item_pos(const SampleParams& P, int idx) {
-  return P.n_identity > 0 ? idx : P.work[idx];
+  return P.n_identity > 0 ? idx : P.work_w[idx];
 }
 
 // Barrier over the warps of this thread's group (named barrier 1 + group).
@@ -1009,6 +1186,7 @@ struct KSmem {
   uint64_t empty[C::NSTAGE];  // every warp of the consuming group is done with the stage
   int issued[C::NSTAGE];      // copies armed on full[s] ...
   int landed[C::NSTAGE];      // ... and waited for (read only after the final barrier)
+  int scan[32];               // per-warp counts of the fused preamble
   Smem<C> g[C::NG];
   alignas(128) unsigned char stage[C::NSTAGE][C::STAGE_BYTES];
 };
@@ -1387,6 +1565,7 @@ __device__ __forceinline__ void compute_item(const SampleParams& P, KSmem<C>& ks
   const int V = P.V;
   const int pos = Q.pos;
   const int b = pos / P.L, l = pos - b * P.L;
+
   const RowRef<C> R = row_ref<C, CFG>(P, ks, stage, pos);
   const float kPosInf = __int_as_float(0x7f800000);
   const float kNaN = __int_as_float(0x7fc00000);
@@ -1554,11 +1733,11 @@ __device__ __forceinline__ void compute_item(const SampleParams& P, KSmem<C>& ks
 // CTA's it-th position) uses stage it % NSTAGE and group it % NG; the group
 // that releases a stage issues the copies of item it + NSTAGE into it.
 template <class C, bool CFG>
-__global__ void __launch_bounds__(C::NTHREADS, 1) sample_kernel(const SampleParams P) {
+__global__ void __launch_bounds__(C::NTHREADS, 1) sample_kernel(const __grid_constant__ SampleParams P) {
   extern __shared__ unsigned char smem_raw[];
   KSmem<C>& ks = *reinterpret_cast<KSmem<C>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
-  const int n_items = P.n_identity > 0 ? P.n_identity : *P.work_count;
+  const int n_items = P.fused ? cta_prepare(P, ks.scan) : P.n_identity;
   const int first = blockIdx.x, stride = gridDim.x;
   if (first >= n_items) return;
   const int n_my = (n_items - first + stride - 1) / stride;
@@ -1617,149 +1796,6 @@ __global__ void __launch_bounds__(C::NTHREADS, 1) sample_kernel(const SamplePara
     for (int s = 0; s < C::NSTAGE; ++s)
       for (int q = ks.landed[s]; q < ks.issued[s]; ++q)
         (void)mbar_wait_bounded(&ks.full[s], (uint32_t)q & 1u, kWaitLimitNs);
-  }
-}
-
-// Positions that are not sampled (sparse mode) report sampled = -1, pmi = NaN.
-__global__ void init_outputs_kernel(const int64_t* __restrict__ xt, const uint8_t* __restrict__ is_commit,
-                                    int B, int L, int64_t mask_id, int dense, int32_t* __restrict__ sampled,
-                                    float* __restrict__ pmi) {
-  const int p = blockIdx.x * blockDim.x + threadIdx.x;
-  if (p >= B * L || dense) return;
-  const int b = p / L;
-  if (!(is_commit[b] == 0 && xt[p] == mask_id)) {
-    sampled[p] = -1;
-    pmi[p] = __int_as_float(0x7fc00000);
-  }
-}
-
-struct UnmaskParams {
-  const int64_t* xt;
-  const int64_t* k_step;
-  const uint8_t* is_commit;
-  const int64_t* sched_t;
-  const float* q_t;
-  const int32_t* sampled;
-  const float2* pcu;
-  const float* log_prior;
-  float pmi_lambda, cfg_w, cfg_1pw;
-  int nb;
-  float* pmi;
-  const float* gumbel_pos;
-  int noise_kind;
-  uint64_t seed, offset;
-  int B, L, K;
-  int64_t mask_id, stop_id;
-  int pos_noise, use_quantile;
-  int64_t* xt_out;
-  int32_t* n_unmask;
-  int32_t* n_mask_after;
-  uint8_t* hit_eos;
-  int64_t* k_step_out;
-  uint8_t* is_commit_out;
-};
-
-// Total order used to rank PMI: NaN above +inf (torch's sort order).
-__device__ __forceinline__ uint32_t rank_key(float f) {
-  return (f != f) ? 0xffffffffu : ord_key(f);
-}
-
-// One warp per request: server/engine.py:559-612.
-__global__ void unmask_kernel(const UnmaskParams U) {
-  const int lane = threadIdx.x & 31;
-  const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (b >= U.B) return;
-  const int L = U.L, K = U.K;
-  const bool in = lane < L;
-  const int p = b * L + lane;
-  const int64_t x = in ? U.xt[p] : 0;
-  const bool is_mask = in && x == U.mask_id;
-  const bool commit = U.is_commit[b] != 0;
-  const bool denoise = !commit;
-  const int64_t ks = U.k_step[b];
-  int kc = (int)(ks < (int64_t)(K - 1) ? ks : (int64_t)(K - 1));
-  if (kc < 0) kc = 0;
-  // PMI of the sampled token (server/engine.py:553-558, calibration.py:58-60)
-  // and the position noise on masked positions (server/engine.py:559-561)
-  float pm = 0.f;
-  const int smp = in ? U.sampled[p] : -1;
-  if (smp >= 0) {
-    const float2 pr = U.pcu[p];
-    const float lpl = __fmul_rn(U.pmi_lambda, __ldg(U.log_prior + smp));
-    pm = __fsub_rn(logf(fmaxf(pr.x, 1e-8f)), lpl);
-    if (U.nb == 2) {
-      const float pmi_u = __fsub_rn(logf(fmaxf(pr.y, 1e-8f)), lpl);
-      pm = __fsub_rn(__fmul_rn(U.cfg_1pw, pm), __fmul_rn(U.cfg_w, pmi_u));
-    }
-  }
-  if (is_mask) {
-    if (U.pos_noise) {
-      const float gn = (U.noise_kind == YAPD_NOISE_EXPLICIT)
-                           ? U.gumbel_pos[p]
-                           : philox_position_gumbel(U.seed, U.offset, (uint32_t)p);
-      pm = __fadd_rn(pm, gn);
-    }
-  }
-  const unsigned mbal = __ballot_sync(0xffffffffu, is_mask);
-  const int m = __popc(mbal);
-  // ascending sort of masked PMI (+inf elsewhere), engine.py:566
-  const uint32_t ak = is_mask ? rank_key(pm) : ord_key(__int_as_float(0x7f800000));
-  uint32_t srt = ak;
-#pragma unroll
-  for (int kk = 2; kk <= 32; kk <<= 1) {
-#pragma unroll
-    for (int j = kk >> 1; j > 0; j >>= 1) {
-      const uint32_t y = __shfl_xor_sync(0xffffffffu, srt, j);
-      const bool up = ((lane & kk) == 0);
-      const bool lower = ((lane & j) == 0);
-      const bool take_min = (up == lower);
-      srt = take_min ? min(srt, y) : max(srt, y);
-    }
-  }
-  const float asc = (srt == 0xffffffffu) ? __int_as_float(0x7fc00000) : ord_key_inv(srt);
-  // quantile by linear interpolation (engine.py:567-572)
-  const float q = U.q_t[kc];
-  const float pq = __fmul_rn(q, (float)(m - 1 > 0 ? m - 1 : 0));
-  int lo = (int)floorf(pq), hi = (int)ceilf(pq);
-  lo = lo < 0 ? 0 : (lo > 31 ? 31 : lo);
-  hi = hi < 0 ? 0 : (hi > 31 ? 31 : hi);
-  const float v_lo = __shfl_sync(0xffffffffu, asc, lo);
-  const float v_hi = __shfl_sync(0xffffffffu, asc, hi);
-  const float tau = __fadd_rn(v_lo, __fmul_rn(__fsub_rn(pq, (float)lo), __fsub_rn(v_hi, v_lo)));
-  int n_quant = __popc(__ballot_sync(0xffffffffu, is_mask && pm >= tau));
-  if (!U.use_quantile) n_quant = 0;
-  const int64_t sch = U.sched_t[kc];
-  const int n_sched = (int)(sch < (int64_t)m ? sch : (int64_t)m);
-  int n_un = min(max(n_sched, n_quant), m);
-  if (ks >= (int64_t)(K - 1)) n_un = m;
-  if (m == 0) n_un = 0;
-  // rank among masked positions by PMI descending, ties to the lower position (engine.py:581-584)
-  const uint32_t mk = rank_key(pm);
-  int rank = 0;
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    const uint32_t kj = __shfl_sync(0xffffffffu, mk, j);
-    const bool mj = (mbal >> j) & 1u;
-    rank += (mj && (kj > mk || (kj == mk && j < lane))) ? 1 : 0;
-  }
-  const bool do_un = is_mask && rank < n_un;
-  int64_t xf = x;
-  if (denoise && do_un) xf = (int64_t)U.sampled[p];
-  if (in) {
-    U.xt_out[p] = xf;
-    if (smp >= 0) U.pmi[p] = pm;
-  }
-  const int n_after = __popc(__ballot_sync(0xffffffffu, in && xf == U.mask_id));
-  const bool eos = __any_sync(0xffffffffu, in && xf == U.stop_id);
-  if (lane == 0) {
-    const int64_t k_new = denoise ? ks + 1 : ks;
-    const int64_t k_fin = commit ? 0 : k_new;
-    const bool to_commit = denoise && !eos && (n_after == 0 || k_fin >= (int64_t)K);
-    U.n_unmask[b] = denoise ? n_un : 0;
-    U.n_mask_after[b] = n_after;
-    U.hit_eos[b] = eos ? 1 : 0;
-    U.k_step_out[b] = k_fin;
-    U.is_commit_out[b] = to_commit ? 1 : 0;
   }
 }
 
@@ -1950,35 +1986,19 @@ int yapd_select_step(const yapd_select_args* a, void* stream) {
   int rc = fill_sampling(P, a->sampling, a->noise);
   if (rc != YAPD_OK) return rc;
   char* ws = static_cast<char*>(a->workspace);
+  const size_t n_pos = (size_t)a->B * a->L;
   P.status = reinterpret_cast<uint32_t*>(ws);
-  P.work_count = reinterpret_cast<int32_t*>(ws + 4);
-  P.work = reinterpret_cast<int32_t*>(ws + 256);
+  P.work_w = reinterpret_cast<int32_t*>(ws + 256);
+  P.pcu = reinterpret_cast<float2*>(ws + 256 + align256(n_pos * sizeof(int32_t)));
+
   P.n_identity = 0;
   P.cfg_w = a->cfg_scale;
   P.cfg_1pw = a->cfg_one_plus;
   P.sampled = a->sampled;
-  P.pcu = reinterpret_cast<float2*>(ws + 256 + align256((size_t)a->B * a->L * sizeof(int32_t)));
+  P.fused = 1;
+  P.dense = a->dense ? 1 : 0;
 
-  cudaStream_t st = (cudaStream_t)stream;
-  const int total = a->B * a->L;
-  worklist_kernel<<<1, 1024, 0, st>>>(a->xt, a->is_commit, a->B, a->L, a->mask_id, a->dense,
-                                      reinterpret_cast<int32_t*>(ws + 256),
-                                      reinterpret_cast<int32_t*>(ws + 4));
-  init_outputs_kernel<<<(total + 255) / 256, 256, 0, st>>>(a->xt, a->is_commit, a->B, a->L, a->mask_id,
-                                                           a->dense, a->sampled, a->pmi);
-  if (cudaGetLastError() != cudaSuccess) return YAPD_ERR_LAUNCH;
-  // profiling events: inside a stream capture they must be external event
-  // nodes so that graph replays record timestamps
-  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-  if (a->prof_event_begin || a->prof_event_end) cudaStreamIsCapturing(st, &cap);
-  const unsigned ev_flags = cap == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : 0u;
-  if (a->prof_event_begin)
-    cudaEventRecordWithFlags(static_cast<cudaEvent_t>(a->prof_event_begin), st, ev_flags);
-  rc = launch_sample(P, a->logits_dtype, total, st);
-  if (rc != YAPD_OK) return rc;
-  if (a->prof_event_end) cudaEventRecordWithFlags(static_cast<cudaEvent_t>(a->prof_event_end), st, ev_flags);
-
-  UnmaskParams U{};
+  UnmaskParams& U = P.U;
   U.xt = a->xt;
   U.k_step = a->k_step;
   U.is_commit = a->is_commit;
@@ -2009,7 +2029,21 @@ int yapd_select_step(const yapd_select_args* a, void* stream) {
   U.hit_eos = a->hit_eos;
   U.k_step_out = a->k_step_out;
   U.is_commit_out = a->is_commit_out;
-  unmask_kernel<<<(a->B + 3) / 4, 128, 0, st>>>(U);
+
+  cudaStream_t st = (cudaStream_t)stream;
+  // profiling events: inside a stream capture they must be external event
+  // nodes so that graph replays record timestamps
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (a->prof_event_begin || a->prof_event_end) cudaStreamIsCapturing(st, &cap);
+  const unsigned ev_flags = cap == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : 0u;
+  if (a->prof_event_begin)
+    cudaEventRecordWithFlags(static_cast<cudaEvent_t>(a->prof_event_begin), st, ev_flags);
+  // every CTA runs the preamble (work list, output init, idle requests), so
+  // the grid is one CTA per SM even when few positions are sampled
+  rc = launch_sample(P, a->logits_dtype, 1 << 30, st);
+  if (rc != YAPD_OK) return rc;
+  if (a->prof_event_end) cudaEventRecordWithFlags(static_cast<cudaEvent_t>(a->prof_event_end), st, ev_flags);
+  unmask_kernel<<<(a->B + 3) / 4, 128, 0, st>>>(U, P.dense);
   return cudaGetLastError() == cudaSuccess ? YAPD_OK : YAPD_ERR_LAUNCH;
 }
 
@@ -2037,8 +2071,9 @@ int yapd_sample_rows(const yapd_sample_args* a, void* stream) {
   int rc = fill_sampling(P, a->sampling, a->noise);
   if (rc != YAPD_OK) return rc;
   P.status = static_cast<uint32_t*>(a->workspace);
-  P.work = nullptr;
-  P.work_count = nullptr;
+  P.work_w = nullptr;
+  P.fused = 0;
+  P.dense = 0;
   P.n_identity = a->R;
   P.sampled = a->sampled;
   P.pcu = nullptr;

@@ -44,6 +44,30 @@ __device__ __forceinline__ float ord_key_inv(uint32_t k) {
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
+// Two fp32 values in one 64-bit register pair, for the sm_100 packed
+// arithmetic (add/fma .f32x2: both halves rounded exactly as the scalar ops).
+__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(unsigned long long v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b,
+                                                     unsigned long long c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// The two bf16 halves of w as a packed fp32 pair (exact).
+__device__ __forceinline__ unsigned long long f2_bf16(uint32_t w) { return f2_pack(bf16lo(w), bf16hi(w)); }
+
 // ------------------------------------------------------------ bulk / mbarrier
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -374,22 +374,33 @@ __device__ int cta_prepare(const SampleParams& P, int* scan) {
   const int nwarp = blockDim.x >> 5;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int grid = (int)gridDim.x, me = (int)blockIdx.x;
-  // warp w owns positions [w*span, (w+1)*span), read 32 at a time; the
-  // ballots of the first kRounds rounds are kept (longer spans read again)
-  constexpr int kRounds = 32;
+  // warp w owns positions [w0, w1), read 32 per round, kR rounds per chunk;
+  // every load is issued (clamped in range) before any of them is used
+  constexpr int kR = 8;
   const int span = (((total + nwarp - 1) / nwarp) + 31) & ~31;
   const int w0 = min(w * span, total), w1 = min(w0 + span, total);
-  unsigned masks[kRounds];
-  int cnt = 0;
+  const bool one_chunk = span <= kR * 32;
+  auto chunk = [&](int c0, unsigned (&m)[kR]) {
+    int64_t xv[kR];
+    uint8_t cv[kR];
 #pragma unroll
-  for (int r = 0; r < kRounds; ++r) {
-    const int p = w0 + r * 32 + lane;
-    masks[r] = __ballot_sync(0xffffffffu, p < w1 && pos_active(U, P.dense, p));
-    cnt += __popc(masks[r]);
-  }
-  for (int p0 = w0 + kRounds * 32; p0 < w1; p0 += 32) {
-    const int p = p0 + lane;
-    cnt += __popc(__ballot_sync(0xffffffffu, p < w1 && pos_active(U, P.dense, p)));
+    for (int r = 0; r < kR; ++r) {
+      const int pc = min(c0 + r * 32 + lane, total - 1);
+      xv[r] = U.xt[pc];
+      cv[r] = U.is_commit[pc / U.L];
+    }
+#pragma unroll
+    for (int r = 0; r < kR; ++r) {
+      const int p = c0 + r * 32 + lane;
+      m[r] = __ballot_sync(0xffffffffu, p < w1 && (P.dense || (cv[r] == 0 && xv[r] == U.mask_id)));
+    }
+  };
+  unsigned masks[kR];
+  int cnt = 0;
+  for (int c0 = w0; c0 < w1; c0 += kR * 32) {
+    chunk(c0, masks);
+#pragma unroll
+    for (int r = 0; r < kR; ++r) cnt += __popc(masks[r]);
   }
   if (lane == 0) scan[w] = cnt;
   __syncthreads();
@@ -400,29 +411,20 @@ __device__ int cta_prepare(const SampleParams& P, int* scan) {
     tot += c;
   }
   const unsigned lt = (1u << lane) - 1u;
+  for (int c0 = w0; c0 < w1; c0 += kR * 32) {
+    if (!one_chunk) chunk(c0, masks);
 #pragma unroll
-  for (int r = 0; r < kRounds; ++r) {
-    const int p = w0 + r * 32 + lane;
-    const bool a = (masks[r] >> lane) & 1u;
-    const int idx = base + __popc(masks[r] & lt);
-    if (a && idx % grid == me) P.work_w[idx] = p;
-    if (!a && p < w1 && p % grid == me) {
-      P.sampled[p] = -1;
-      U.pmi[p] = __int_as_float(0x7fc00000);
+    for (int r = 0; r < kR; ++r) {
+      const int p = c0 + r * 32 + lane;
+      const bool a = (masks[r] >> lane) & 1u;
+      const int idx = base + __popc(masks[r] & lt);
+      if (a && idx % grid == me) P.work_w[idx] = p;
+      if (!a && p < w1 && p % grid == me) {
+        P.sampled[p] = -1;
+        U.pmi[p] = __int_as_float(0x7fc00000);
+      }
+      base += __popc(masks[r]);
     }
-    base += __popc(masks[r]);
-  }
-  for (int p0 = w0 + kRounds * 32; p0 < w1; p0 += 32) {
-    const int p = p0 + lane;
-    const bool a = p < w1 && pos_active(U, P.dense, p);
-    const unsigned m = __ballot_sync(0xffffffffu, a);
-    const int idx = base + __popc(m & lt);
-    if (a && idx % grid == me) P.work_w[idx] = p;
-    if (!a && p < w1 && p % grid == me) {
-      P.sampled[p] = -1;
-      U.pmi[p] = __int_as_float(0x7fc00000);
-    }
-    base += __popc(m);
   }
   __syncthreads();
   return tot;
@@ -1347,6 +1349,46 @@ __device__ __forceinline__ void pass_sums(const PosCtx& X, const RowRef<C>& R, c
   const float A2 = X.A2, nB2 = -X.B2;
   float sc0 = 0.f, sc1 = 0.f, su0 = 0.f, su1 = 0.f, s0 = 0.f, s1 = 0.f, dm = kNegInf;
   int k = 0;
+  if constexpr (C::BF16) {
+    // packed pairs: element 2t in the low half, 2t+1 in the high half, so the
+    // two accumulators of each sum see the same additions as the scalar form
+    const unsigned long long L2p = f2_pack(kLog2e, kLog2e), A2p = f2_pack(A2, A2), nB2p = f2_pack(nB2, nB2);
+    const unsigned long long nmcLp = f2_pack(nmcL, nmcL), nmuLp = f2_pack(nmuL, nmuL), nzrp = f2_pack(nzr, nzr);
+    unsigned long long scp = f2_pack(0.f, 0.f), sup = scp, sp = scp;
+#pragma unroll 2
+    for (int j = S.j0 + tid; j < S.j1; j += C::NT, ++k) {
+      const uint4 a = lds128(R.sc + j * 16);
+      uint4 q = a;
+      if (CFG) q = lds128(R.su + j * 16);
+      const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+      const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+      float vz = kNegInf;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const unsigned long long cx = f2_bf16(aw[t]);
+        unsigned long long dx;
+        float lo, hi;
+        if (CFG) {
+          const unsigned long long ux = f2_bf16(qw[t]);
+          dx = f2_fma(cx, A2p, f2_fma(ux, nB2p, nzrp));
+          f2_unpack(f2_fma(ux, L2p, nmuLp), lo, hi);
+          sup = f2_add(sup, f2_pack(ex2_approx(lo), ex2_approx(hi)));
+        } else {
+          dx = f2_fma(cx, A2p, nzrp);
+        }
+        f2_unpack(f2_fma(cx, L2p, nmcLp), lo, hi);
+        scp = f2_add(scp, f2_pack(ex2_approx(lo), ex2_approx(hi)));
+        f2_unpack(dx, lo, hi);
+        sp = f2_add(sp, f2_pack(ex2_approx(lo), ex2_approx(hi)));
+        vz = fmax3(vz, lo, hi);
+      }
+      dm = fmaxf(dm, vz);
+      if (mark && k < C::KV) sm.vzh[k * C::NT + tid] = __half_as_ushort(__float2half_ru(vz));
+    }
+    f2_unpack(scp, sc0, sc1);
+    f2_unpack(sup, su0, su1);
+    f2_unpack(sp, s0, s1);
+  } else {
 #pragma unroll 2
   for (int j = S.j0 + tid; j < S.j1; j += C::NT, ++k) {
     const uint4 a = lds128(R.sc + j * 16);
@@ -1374,6 +1416,7 @@ __device__ __forceinline__ void pass_sums(const PosCtx& X, const RowRef<C>& R, c
     for (int i = 2; i + 1 < C::W; i += 2) vz = fmax3(vz, d[i], d[i + 1]);
     dm = fmaxf(dm, vz);
     if (mark && k < C::KV) sm.vzh[k * C::NT + tid] = __half_as_ushort(__float2half_ru(vz));
+  }
   }
   for (int e = tid; e < S.nscal; e += C::NT) {
     const int v = scalar_v(S, e);

@@ -41,7 +41,7 @@ struct KCfg {
   static constexpr int NSTAGE = NSTAGE_;
   static constexpr int BAND = NT_;      // candidate band capacity (one thread per element)
   static constexpr int NW = NT / 32;    // warps per group
-  static constexpr int NTHREADS = NG * NT;
+  static constexpr int NTHREADS = NG * NT + NG * 32;  // groups, then one tail warp per group
   static constexpr int ROW_SLOT = ((YAPD_MAX_V * ELEM + 32 + 127) / 128) * 128;
   static constexpr int STAGE_BYTES = 2 * ROW_SLOT;
   static constexpr bool BF16 = (ELEM == 2);
@@ -53,8 +53,8 @@ struct KCfg {
   // ahead of the barrier (a parity wait would then pass at once).
   static_assert(NSTAGE % NG == 0, "the groups must divide the stages");
 };
-using CfgBF16 = KCfg<128, 3, 8, 2, 6>;
-using CfgF32 = KCfg<128, 3, 4, 4, 3>;
+using CfgBF16 = KCfg<96, 3, 8, 2, 6>;
+using CfgF32 = KCfg<96, 3, 4, 4, 3>;
 
 // Thread index within its group, and the group index.
 template <class C>
@@ -1178,14 +1178,30 @@ struct Smem {
   float cande[C::BAND];
   float2 cpc[32];             // PMI inputs of the first 32 band members
   float cscore[32];           // their exact scores (penalty + noise)
-  unsigned short vzh[C::KV * C::NT];  // per vector: its largest z2' (fp16, rounded up)
   unsigned char cflag[C::BAND];
+};
+
+// The record a group leaves for its tail warp: the position's parameters,
+// merged statistics and (when `handed`) its min-p band of at most 32 ids.
+struct ItemParams {
+  int pos;
+  float T, top_p, min_p, rep;
+  int top_k;
+};
+
+struct Hand {
+  ItemParams Q;
+  float m[3], s[3];  // group maxima (c, u, z2') and sums relative to them
+  int n;             // band members found (ids of the first 32 in cv)
+  int handed;        // 1: the tail warp resolves the band and writes the outputs
+  int cv[32];
 };
 
 template <class C>
 struct KSmem {
   uint64_t full[C::NSTAGE];   // rows landed (one expect_tx arrive + the copy bytes)
-  uint64_t empty[C::NSTAGE];  // every warp of the consuming group is done with the stage
+  uint64_t ready[C::NSTAGE];  // the group is done with the position (one arrive per group warp)
+  Hand hand[C::NSTAGE];       // the group -> tail warp record of the stage's position
   int issued[C::NSTAGE];      // copies armed on full[s] ...
   int landed[C::NSTAGE];      // ... and waited for (read only after the final barrier)
   int scan[32];               // per-warp counts of the fused preamble
@@ -1339,84 +1355,91 @@ __device__ __noinline__ float thread_zmax(const PosCtx X, const RowRef<C> R, con
 
 // Pass 2 of the two-pass form: sc = sum 2^(c*log2e + nmcL), su likewise,
 // s = sum 2^d and dmax = max d with d = A2*c - B2*u + nzr (NaN ignored in the
-// maximum, kept in the sums).  With `mark`, each vector's largest d is kept
-// (fp16, rounded up) in vzh for the band pass.
+// maximum, kept in the sums); vz[k] = the largest d of this thread's k-th
+// vector (-inf past the row).
 template <class C, bool CFG>
 __device__ __forceinline__ void pass_sums(const PosCtx& X, const RowRef<C>& R, const Span& S, float nmcL,
-                                          float nmuL, float nzr, bool mark, Smem<C>& sm, float& sc, float& su,
-                                          float& s, float& dmax, int& nvec) {
+                                          float nmuL, float nzr, float& sc, float& su, float& s, float& dmax,
+                                          float (&vz)[C::KV]) {
   const int tid = gtid<C>();
   const float A2 = X.A2, nB2 = -X.B2;
   float sc0 = 0.f, sc1 = 0.f, su0 = 0.f, su1 = 0.f, s0 = 0.f, s1 = 0.f, dm = kNegInf;
-  int k = 0;
   if constexpr (C::BF16) {
     // packed pairs: element 2t in the low half, 2t+1 in the high half, so the
     // two accumulators of each sum see the same additions as the scalar form
     const unsigned long long L2p = f2_pack(kLog2e, kLog2e), A2p = f2_pack(A2, A2), nB2p = f2_pack(nB2, nB2);
     const unsigned long long nmcLp = f2_pack(nmcL, nmcL), nmuLp = f2_pack(nmuL, nmuL), nzrp = f2_pack(nzr, nzr);
     unsigned long long scp = f2_pack(0.f, 0.f), sup = scp, sp = scp;
-#pragma unroll 2
-    for (int j = S.j0 + tid; j < S.j1; j += C::NT, ++k) {
-      const uint4 a = lds128(R.sc + j * 16);
-      uint4 q = a;
-      if (CFG) q = lds128(R.su + j * 16);
-      const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
-      const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-      float vz = kNegInf;
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const unsigned long long cx = f2_bf16(aw[t]);
-        unsigned long long dx;
-        float lo, hi;
-        if (CFG) {
-          const unsigned long long ux = f2_bf16(qw[t]);
-          dx = f2_fma(cx, A2p, f2_fma(ux, nB2p, nzrp));
-          f2_unpack(f2_fma(ux, L2p, nmuLp), lo, hi);
-          sup = f2_add(sup, f2_pack(ex2_approx(lo), ex2_approx(hi)));
-        } else {
-          dx = f2_fma(cx, A2p, nzrp);
+    for (int k = 0; k < C::KV; ++k) {
+      const int j = S.j0 + tid + k * C::NT;
+      vz[k] = kNegInf;
+      if (j < S.j1) {
+        const uint4 a = lds128(R.sc + j * 16);
+        uint4 q = a;
+        if (CFG) q = lds128(R.su + j * 16);
+        const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+        float m = kNegInf;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const unsigned long long cx = f2_bf16(aw[t]);
+          unsigned long long dx;
+          float lo, hi;
+          if (CFG) {
+            const unsigned long long ux = f2_bf16(qw[t]);
+            dx = f2_fma(cx, A2p, f2_fma(ux, nB2p, nzrp));
+            f2_unpack(f2_fma(ux, L2p, nmuLp), lo, hi);
+            sup = f2_add(sup, f2_pack(ex2_approx(lo), ex2_approx(hi)));
+          } else {
+            dx = f2_fma(cx, A2p, nzrp);
+          }
+          f2_unpack(f2_fma(cx, L2p, nmcLp), lo, hi);
+          scp = f2_add(scp, f2_pack(ex2_approx(lo), ex2_approx(hi)));
+          f2_unpack(dx, lo, hi);
+          sp = f2_add(sp, f2_pack(ex2_approx(lo), ex2_approx(hi)));
+          m = fmax3(m, lo, hi);
         }
-        f2_unpack(f2_fma(cx, L2p, nmcLp), lo, hi);
-        scp = f2_add(scp, f2_pack(ex2_approx(lo), ex2_approx(hi)));
-        f2_unpack(dx, lo, hi);
-        sp = f2_add(sp, f2_pack(ex2_approx(lo), ex2_approx(hi)));
-        vz = fmax3(vz, lo, hi);
+        vz[k] = m;
+        dm = fmaxf(dm, m);
       }
-      dm = fmaxf(dm, vz);
-      if (mark && k < C::KV) sm.vzh[k * C::NT + tid] = __half_as_ushort(__float2half_ru(vz));
     }
     f2_unpack(scp, sc0, sc1);
     f2_unpack(sup, su0, su1);
     f2_unpack(sp, s0, s1);
   } else {
-#pragma unroll 2
-  for (int j = S.j0 + tid; j < S.j1; j += C::NT, ++k) {
-    const uint4 a = lds128(R.sc + j * 16);
-    uint4 q = a;
-    if (CFG) q = lds128(R.su + j * 16);
-    float d[C::W];
 #pragma unroll
-    for (int i = 0; i < C::W; ++i) {
-      const float c = velem<C>(a, i);
-      d[i] = CFG ? __fmaf_rn(c, A2, __fmaf_rn(velem<C>(q, i), nB2, nzr)) : __fmaf_rn(c, A2, nzr);
-    }
+    for (int k = 0; k < C::KV; ++k) {
+      const int j = S.j0 + tid + k * C::NT;
+      vz[k] = kNegInf;
+      if (j < S.j1) {
+        const uint4 a = lds128(R.sc + j * 16);
+        uint4 q = a;
+        if (CFG) q = lds128(R.su + j * 16);
+        float d[C::W];
 #pragma unroll
-    for (int i = 0; i < C::W; i += 2) {
-      sc0 += ex2_approx(__fmaf_rn(velem<C>(a, i), kLog2e, nmcL));
-      sc1 += ex2_approx(__fmaf_rn(velem<C>(a, i + 1), kLog2e, nmcL));
-      if (CFG) {
-        su0 += ex2_approx(__fmaf_rn(velem<C>(q, i), kLog2e, nmuL));
-        su1 += ex2_approx(__fmaf_rn(velem<C>(q, i + 1), kLog2e, nmuL));
+        for (int i = 0; i < C::W; ++i) {
+          const float c = velem<C>(a, i);
+          d[i] = CFG ? __fmaf_rn(c, A2, __fmaf_rn(velem<C>(q, i), nB2, nzr)) : __fmaf_rn(c, A2, nzr);
+        }
+#pragma unroll
+        for (int i = 0; i < C::W; i += 2) {
+          sc0 += ex2_approx(__fmaf_rn(velem<C>(a, i), kLog2e, nmcL));
+          sc1 += ex2_approx(__fmaf_rn(velem<C>(a, i + 1), kLog2e, nmcL));
+          if (CFG) {
+            su0 += ex2_approx(__fmaf_rn(velem<C>(q, i), kLog2e, nmuL));
+            su1 += ex2_approx(__fmaf_rn(velem<C>(q, i + 1), kLog2e, nmuL));
+          }
+          s0 += ex2_approx(d[i]);
+          s1 += ex2_approx(d[i + 1]);
+        }
+        float m = fmaxf(d[0], d[1]);
+#pragma unroll
+        for (int i = 2; i + 1 < C::W; i += 2) m = fmax3(m, d[i], d[i + 1]);
+        vz[k] = m;
+        dm = fmaxf(dm, m);
       }
-      s0 += ex2_approx(d[i]);
-      s1 += ex2_approx(d[i + 1]);
     }
-    float vz = fmaxf(d[0], d[1]);
-#pragma unroll
-    for (int i = 2; i + 1 < C::W; i += 2) vz = fmax3(vz, d[i], d[i + 1]);
-    dm = fmaxf(dm, vz);
-    if (mark && k < C::KV) sm.vzh[k * C::NT + tid] = __half_as_ushort(__float2half_ru(vz));
-  }
   }
   for (int e = tid; e < S.nscal; e += C::NT) {
     const int v = scalar_v(S, e);
@@ -1437,7 +1460,6 @@ __device__ __forceinline__ void pass_sums(const PosCtx& X, const RowRef<C>& R, c
   su = su0 + su1;
   s = s0 + s1;
   dmax = dm;
-  nvec = k;
 }
 
 // Sum of 2^(A2*c - B2*u + nzr) alone (after an underflowed pass 2).
@@ -1581,13 +1603,6 @@ __device__ __forceinline__ void finish_band(const SampleParams& P, const Smem<C>
   }
 }
 
-// Per-request sampling parameters of one position.
-struct ItemParams {
-  int pos;
-  float T, top_p, min_p, rep;
-  int top_k;
-};
-
 __device__ __forceinline__ ItemParams load_params(const SampleParams& P, int pos) {
   ItemParams q;
   const int b = pos / P.L;
@@ -1601,43 +1616,123 @@ __device__ __forceinline__ ItemParams load_params(const SampleParams& P, int pos
 }
 
 // One position, worked by the calling group.
+// Parts of the position context that need no statistics.
+template <bool CFG>
+__device__ __forceinline__ void item_ctx(const SampleParams& P, const ItemParams& Q, PosCtx& X, float& sA) {
+  X.cfg = CFG;
+  X.T = Q.T;
+  X.scale = X.T > 0.0f;
+  X.rT = X.scale ? __fdiv_rn(1.0f, X.T) : 1.0f;
+  sA = X.scale ? X.rT : 1.0f;
+  X.A2 = CFG ? __fmul_rn(__fmul_rn(kLog2e, P.cfg_1pw), sA) : __fmul_rn(kLog2e, sA);
+  X.B2 = CFG ? __fmul_rn(__fmul_rn(kLog2e, P.cfg_w), sA) : 0.f;
+}
+
+// Group maxima m[] and sums s[] (relative to m*scale) -> the position context
+// (stats_core: maxima, sums, z2 offset) and the scoring context (stats_rest).
+// The group and its tail warp both derive them here, so the two see
+// identical values.
+template <bool CFG>
+__device__ __forceinline__ void stats_core(const float (&m)[3], const float (&s)[3], PosCtx& X) {
+  const float kPosInf = __int_as_float(0x7f800000);
+  const float kNaN = __int_as_float(0x7fc00000);
+  X.mc = m[0];
+  X.mu = CFG ? m[1] : 0.f;
+  X.Sc = (X.mc > kNegInf && X.mc < kPosInf) ? s[0] : kNaN;
+  X.Su = CFG ? ((X.mu > kNegInf && X.mu < kPosInf) ? s[1] : kNaN) : 0.f;
+  X.K2 = CFG ? __fmaf_rn(-X.mc, X.A2, __fmul_rn(X.mu, X.B2)) : __fmul_rn(-X.mc, X.A2);
+  X.zmax = __fadd_rn(m[2], X.K2);
+  X.S = (m[2] < kPosInf && s[2] < kPosInf) ? s[2] : kNaN;
+}
+
+// The rest of the contexts (logs and reciprocals), for exact values and scores.
+template <bool CFG>
+__device__ __forceinline__ void stats_rest(const SampleParams& P, const ItemParams& Q, float sA, PosCtx& X,
+                                           ScoreCtx& K) {
+  X.lc = logf(X.Sc);
+  X.lu = CFG ? logf(X.Su) : 0.f;
+  X.Kval = CFG ? __fmul_rn(__fsub_rn(__fmul_rn(P.cfg_w, X.lu), __fmul_rn(P.cfg_1pw, X.lc)), sA)
+               : __fmul_rn(X.mc, sA);
+  const bool topk_on = Q.top_k > 0 && Q.top_k < P.V;
+  const bool pen_on = P.history_kind != YAPD_HISTORY_NONE && P.history != nullptr && Q.rep != 1.0f;
+  K.b = Q.pos / P.L;
+  K.pos = Q.pos;
+  K.l = Q.pos - K.b * P.L;
+  K.pen_on = pen_on;
+  K.noisy = X.T > 0.0f || !P.zero_temp_greedy;
+  K.turbo = topk_on || Q.top_p < 1.0f || Q.min_p > 0.0f || K.pen_on;
+  K.minp_on = false;
+  K.rep = Q.rep;
+  K.rrep = K.pen_on ? __fdiv_rn(1.0f, Q.rep) : 1.0f;
+  K.r = __fdiv_rn(1.0f, X.S);
+  K.minp_thr = 0.f;
+}
+
+// The min-p band's ids, from the vectors pass 2 marked (and every scalar
+// element), into the stage's hand-off record (the first 32 of them); returns
+// the band size.  h.n must be zero on entry.
+template <class C, bool CFG>
+__device__ __forceinline__ int band_collect(const PosCtx& X, const RowRef<C>& R, const Span& S, uint32_t marks,
+                                            float lo_z, Hand& h) {
+  const int tid = gtid<C>();
+  while (marks) {
+    const int k = __ffs(marks) - 1;
+    marks &= marks - 1u;
+    const int j = S.j0 + tid + k * C::NT;
+    const uint4 a = lds128(R.sc + j * 16);
+    uint4 q = a;
+    if (CFG) q = lds128(R.su + j * 16);
+    uint32_t m = 0;
+#pragma unroll
+    for (int i = 0; i < C::W; ++i) {
+      const float z = z2_of(X, velem<C>(a, i), CFG ? velem<C>(q, i) : 0.f);
+      m |= (z >= lo_z ? 1u : 0u) << i;
+    }
+    const int v0 = j * C::W - S.head;
+    while (m) {
+      const int i = __ffs(m) - 1;
+      m &= m - 1u;
+      const int at = atomicAdd(&h.n, 1);
+      if (at < 32) h.cv[at] = v0 + i;
+    }
+  }
+  for (int e = tid; e < S.nscal; e += C::NT) {
+    const int v = scalar_v(S, e);
+    if (z2_smem<C>(X, R, v) >= lo_z) {
+      const int at = atomicAdd(&h.n, 1);
+      if (at < 32) h.cv[at] = v;
+    }
+  }
+  csync<C>();
+  return h.n;
+}
+
+// One position worked by a group: statistics, group merge, and either the
+// whole token choice with the outputs, or (a min-p band of at most 32
+// members) the hand-off record for the group's tail warp.
 template <class C, bool CFG>
 __device__ __forceinline__ void compute_item(const SampleParams& P, KSmem<C>& ks, Smem<C>& sm, int& slot,
                                              int stage, const ItemParams& Q) {
   const int tid = gtid<C>();
   const int V = P.V;
   const int pos = Q.pos;
-  const int b = pos / P.L, l = pos - b * P.L;
-
   const RowRef<C> R = row_ref<C, CFG>(P, ks, stage, pos);
   const float kPosInf = __int_as_float(0x7f800000);
-  const float kNaN = __int_as_float(0x7fc00000);
   PosCtx X;
-  X.cfg = CFG;
-  X.T = Q.T;
-  const int topk_raw = Q.top_k;
-  const float top_p = Q.top_p;
-  const float min_p = Q.min_p;
-  const float rep = Q.rep;
-  const bool pen_on = P.history_kind != YAPD_HISTORY_NONE && P.history != nullptr && rep != 1.0f;
-  X.scale = X.T > 0.0f;
-  X.rT = X.scale ? __fdiv_rn(1.0f, X.T) : 1.0f;
-  const float w = P.cfg_w;
-  const float sA = X.scale ? X.rT : 1.0f;
-  X.A2 = CFG ? __fmul_rn(__fmul_rn(kLog2e, P.cfg_1pw), sA) : __fmul_rn(kLog2e, sA);
-  X.B2 = CFG ? __fmul_rn(__fmul_rn(kLog2e, w), sA) : 0.f;
+  float sA;
+  item_ctx<CFG>(P, Q, X, sA);
   const Span S = make_span<C, CFG>(R, V);
-  const bool topk_on = topk_raw > 0 && topk_raw < V;
-  const bool topp_on = top_p < 1.0f;
-  const bool minp_on = min_p > 0.0f;
+  const bool topk_on = Q.top_k > 0 && Q.top_k < V;
+  const bool topp_on = Q.top_p < 1.0f;
+  const bool minp_on = Q.min_p > 0.0f;
   const bool band_mode = minp_on && !topk_on;
-  const float lg_minp = band_mode ? fminf(log2f(min_p), 0.f) : 0.f;
-
-  // the stage goes back to the ring once every warp is done reading it
-  auto release = [&]() {
-    __syncwarp();
-    if ((threadIdx.x & 31) == 0) mbar_arrive(&ks.empty[stage]);
-  };
+  const float lg_minp = band_mode ? fminf(log2f(Q.min_p), 0.f) : 0.f;
+  Hand& h = ks.hand[stage];
+  if (tid == 0) {
+    h.Q = Q;
+    h.n = 0;
+    h.handed = 0;
+  }
 
   // ---- pass 1: this thread's maxima ----
   float mc_t, mu_t, nu_t;
@@ -1656,14 +1751,13 @@ __device__ __forceinline__ void compute_item(const SampleParams& P, KSmem<C>& ks
 
   // ---- pass 2: sums against the thread references; merged over the group ----
   Stats3 st;
-  int nvec;
+  float vz[C::KV];
   {
     float sc, su, s, dmax;
-    pass_sums<C, CFG>(X, R, S, -__fmul_rn(mcr, kLog2e), -__fmul_rn(mur, kLog2e), -zr, band_mode, sm, sc, su, s,
-                      dmax, nvec);
+    pass_sums<C, CFG>(X, R, S, -__fmul_rn(mcr, kLog2e), -__fmul_rn(mur, kLog2e), -zr, sc, su, s, dmax, vz);
     if (s == 0.f && dmax > kNegInf && dmax < kPosInf) {
       // every term underflowed against the bound: use the exact thread maximum
-      // (the fp16 vector marks stay relative to the first reference)
+      // (the vector maxima stay relative to the first reference)
       s = pass_resum<C, CFG>(X, R, S, -__fadd_rn(zr, dmax));
       st.ref[2] = __fadd_rn(zr, dmax);
     } else {
@@ -1680,34 +1774,16 @@ __device__ __forceinline__ void compute_item(const SampleParams& P, KSmem<C>& ks
   }
   const float mscale[3] = {kLog2e, kLog2e, 1.0f};
   group_merge3<C>(st, mscale, sm, slot);
-  X.mc = st.m[0];
-  X.mu = CFG ? st.m[1] : 0.f;
-  X.Sc = (X.mc > kNegInf && X.mc < kPosInf) ? st.s[0] : kNaN;
-  X.Su = CFG ? ((X.mu > kNegInf && X.mu < kPosInf) ? st.s[1] : kNaN) : 0.f;
-  X.K2 = CFG ? __fmaf_rn(-X.mc, X.A2, __fmul_rn(X.mu, X.B2)) : __fmul_rn(-X.mc, X.A2);
-  X.zmax = __fadd_rn(st.m[2], X.K2);
-  X.S = (st.m[2] < kPosInf && st.s[2] < kPosInf) ? st.s[2] : kNaN;
-  X.lc = logf(X.Sc);
-  X.lu = CFG ? logf(X.Su) : 0.f;
-  X.Kval = CFG ? __fmul_rn(__fsub_rn(__fmul_rn(w, X.lu), __fmul_rn(P.cfg_1pw, X.lc)), sA)
-               : __fmul_rn(X.mc, sA);
+  stats_core<CFG>(st.m, st.s, X);
+  ScoreCtx K;
+  bool rest = false;
+  auto need_rest = [&]() {
+    if (!rest) stats_rest<CFG>(P, Q, sA, X, K);
+    rest = true;
+  };
 
   // ---- token choice ----
-  ScoreCtx K;
-  K.b = b;
-  K.pos = pos;
-  K.l = l;
-  K.pen_on = pen_on;
-  K.noisy = X.T > 0.0f || !P.zero_temp_greedy;
-  K.turbo = topk_on || topp_on || minp_on || K.pen_on;
-  K.minp_on = false;
-  K.rep = rep;
-  K.rrep = K.pen_on ? __fdiv_rn(1.0f, rep) : 1.0f;
-  K.r = __fdiv_rn(1.0f, X.S);
-  K.minp_thr = 0.f;
-
   int chosen = -1;
-  bool handed = false;
   const Pick none{kNegInf, kNegInf, 0x7fffffff};
   if (!(X.Sc == X.Sc) || (CFG && !(X.Su == X.Su))) {
     chosen = 0;  // a NaN/+inf logit makes the whole reference row NaN: argmax -> 0
@@ -1716,6 +1792,7 @@ __device__ __forceinline__ void compute_item(const SampleParams& P, KSmem<C>& ks
     chosen = f < 0 ? 0 : f;
   } else if (!topk_on && !topp_on && !minp_on) {
     // every token kept: server/engine.py:546-550 (or the penalty-only chain)
+    need_rest();
     chosen = argmax_smem<C>(P, X, R, -kBig, kBig, 0ull, K, none, sm);
     if (chosen < 0) chosen = 0;
   } else {
@@ -1729,52 +1806,153 @@ __device__ __forceinline__ void compute_item(const SampleParams& P, KSmem<C>& ks
         const float thr = __fsub_rn(__fsub_rn(__fsub_rn(zmp, zmargin(zmp)),
                                               __fadd_rn(1e-3f, __fmul_rn(4e-6f, __fadd_rn(fabsf(X.K2), fabsf(zmp))))),
                                     zr);  // relative to this thread's reference, as stored
-        for (int k = 0; k < nvec; ++k) {
-          const bool hit = k >= C::KV || __half2float(__ushort_as_half(sm.vzh[k * C::NT + tid])) >= thr;
-          marks |= (hit ? 1u : 0u) << k;
+#pragma unroll
+        for (int k = 0; k < C::KV; ++k) {
+          const bool in_row = S.j0 + tid + k * C::NT < S.j1;
+          marks |= (in_row && (vz[k] >= thr || !(thr > kNegInf)) ? 1u : 0u) << k;
         }
       }
-      const int n = band_marked<C, CFG>(P, X, R, K, S, marks, lo_z, sm);
-      if (n <= 32) {
-        release();
-        if (tid < 32) finish_band<C>(P, sm, n, K, topp_on, top_p, min_p);
-        handed = true;
-      } else if (n <= C::BAND) {
-        rank_sort<C>(n, sm);
+      const int n = band_collect<C, CFG>(X, R, S, marks, lo_z, h);
+      if (n <= 32 && n > 0) {
+        // the group's tail warp resolves it
+        if (tid == 0) {
+#pragma unroll
+          for (int j = 0; j < 3; ++j) {
+            h.m[j] = st.m[j];
+            h.s[j] = st.s[j];
+          }
+          h.handed = 1;
+        }
+        return;
+      }
+      // a wide band: scored and resolved by the whole group
+      need_rest();
+      if (tid == 0) sm.misc[0] = 0;
+      csync<C>();
+      const int n2 = band_marked<C, CFG>(P, X, R, K, S, marks, lo_z, sm);
+      if (n2 <= C::BAND && n2 > 0) {
+        rank_sort<C>(n2, sm);
         Band bd;
-        bd.n = n;
+        bd.n = n2;
         bd.H = kBig;
         bd.n_above = 0.f;
         bd.m_above = 0.f;
         bd.overflow = false;
-        const float minp_thr = __fmul_rn(min_p, __fmul_rn(sm.cande[0], K.r));
-        band_flags<C>(bd, false, 0, topp_on, top_p, K.r, true, minp_thr, sm);
+        const float minp_thr = __fmul_rn(Q.min_p, __fmul_rn(sm.cande[0], K.r));
+        band_flags<C>(bd, false, 0, topp_on, Q.top_p, K.r, true, minp_thr, sm);
         const Pick bp = band_pick<C>(P, K, bd.n, sm);
         chosen = block_pick<C>(bp, true, sm, slot);
         if (chosen < 0) chosen = cand_id(sm.cand[0]);
       }
     }
-    if (!handed && chosen < 0) {
+    if (chosen < 0) {
+      need_rest();
       K.minp_on = minp_on;
-      chosen = select_cold<C>(P, X, R, K, topk_raw, topk_on, topp_on, top_p, min_p, sm);
+      chosen = select_cold<C>(P, X, R, K, Q.top_k, topk_on, topp_on, Q.top_p, Q.min_p, sm);
     }
   }
-  if (!handed) {
-    if (tid == 0) {
-      if (chosen < 0 || chosen >= V) {
-        atomicOr(P.status, (unsigned)YAPD_STATUS_INTERNAL);
-        chosen = 0;
-      }
-      write_choice<C, CFG>(P, R, pos, chosen, X.mc, X.Sc, X.mu, X.Su);
+  if (tid == 0) {
+    if (chosen < 0 || chosen >= V) {
+      atomicOr(P.status, (unsigned)YAPD_STATUS_INTERNAL);
+      chosen = 0;
     }
-    release();
+    write_choice<C, CFG>(P, R, pos, chosen, X.mc, X.Sc, X.mu, X.Su);
   }
 }
 
+// Tail warp: the min-p band of the position recorded for `stage` (at most 32
+// members, one per lane): exact value, mass, score (penalty + noise) per
+// member, a bitonic sort by (exact value, id), top-p / min-p flags from
+// double prefix sums, the best kept score, and the outputs.
+template <class C, bool CFG>
+__device__ __forceinline__ void tail_finish(const SampleParams& P, KSmem<C>& ks, int stage) {
+  const int lane = threadIdx.x & 31;
+  const Hand& h = ks.hand[stage];
+  const ItemParams Q = h.Q;
+  const int n = h.n;
+  const RowRef<C> R = row_ref<C, CFG>(P, ks, stage, Q.pos);
+  PosCtx X;
+  float sA;
+  item_ctx<CFG>(P, Q, X, sA);
+  float m[3], s[3];
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    m[j] = h.m[j];
+    s[j] = h.s[j];
+  }
+  ScoreCtx K;
+  stats_core<CFG>(m, s, X);
+  stats_rest<CFG>(P, Q, sA, X, K);
+  const bool live0 = lane < n;
+  const int v0 = live0 ? h.cv[lane] : 0;
+  unsigned long long key = 0ull;
+  float e = 0.f, score = kNegInf;
+  if (live0) {
+    const float vals = exact_val<C>(P, X, R, v0);
+    key = cand_key(vals, v0);
+    e = ex2_approx(__fsub_rn(z2_smem<C>(X, R, v0), X.zmax));
+    score = exact_score<C, true>(P, K, v0, vals);
+  }
+  // bitonic sort, descending key, over the smallest power of two >= n lanes
+  int kmax = 2;
+  while (kmax < n) kmax <<= 1;
+  for (int k = 2; k <= kmax; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const unsigned long long y = __shfl_xor_sync(0xffffffffu, key, j);
+      const float ey = __shfl_xor_sync(0xffffffffu, e, j);
+      const float sy = __shfl_xor_sync(0xffffffffu, score, j);
+      const bool up = ((lane & k) == 0) || k == kmax;
+      const bool lower = ((lane & j) == 0);
+      const bool take_max = (up == lower);
+      if (take_max ? (y > key) : (y < key)) {
+        key = y;
+        e = ey;
+        score = sy;
+      }
+    }
+  }
+  const bool live = lane < n;
+  const int v = cand_id(key);
+  const float p = __fmul_rn(e, K.r);
+  double incl = (double)p;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  const float p0 = __shfl_sync(0xffffffffu, p, 0);
+  bool keep = live;
+  if (Q.top_p < 1.0f) keep = keep && (__fsub_rn((float)incl, p) < Q.top_p);
+  keep = keep && (p >= __fmul_rn(Q.min_p, p0));
+  float sc = keep ? score : kNegInf;
+  if (!(sc == sc)) sc = kNegInf;
+  const uint32_t ks2 = sc > kNegInf ? ord_key(sc) : 0u;
+  unsigned long long rec = ks2 ? (((unsigned long long)ks2 << 32) | (uint32_t)(31 - lane)) : 0ull;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long x = __shfl_xor_sync(0xffffffffu, rec, o);
+    rec = x > rec ? x : rec;
+  }
+  const int win_lane = rec ? 31 - (int)(uint32_t)(rec & 0xffffffffu) : 0;
+  if (lane == win_lane) {
+    int chosen = v;
+    if (!live || chosen < 0 || chosen >= P.V) {
+      atomicOr(P.status, (unsigned)YAPD_STATUS_INTERNAL);
+      chosen = 0;
+    }
+    P.sampled[Q.pos] = chosen;
+    if (P.pcu) P.pcu[Q.pos] = pmi_inputs<C, CFG>(X, R, chosen);
+  }
+  __syncwarp();
+}
+
 // One CTA per SM: NG groups of NT threads, each working one position at a
-// time from a shared NSTAGE-deep ring of staged rows.  Local item `it` (the
-// CTA's it-th position) uses stage it % NSTAGE and group it % NG; the group
-// that releases a stage issues the copies of item it + NSTAGE into it.
+// time from a shared NSTAGE-deep ring of staged rows, and one tail warp per
+// group.  Local item `it` (the CTA's it-th position) uses stage it % NSTAGE
+// and group it % NG (NG divides NSTAGE, so each stage serves one group).  The
+// group runs the statistics and either finishes the position or hands its
+// band to the group's tail warp; the tail warp finishes a handed band, then
+// issues the copies of item it + NSTAGE into the stage.
 template <class C, bool CFG>
 __global__ void __launch_bounds__(C::NTHREADS, 1) sample_kernel(const __grid_constant__ SampleParams P) {
   extern __shared__ unsigned char smem_raw[];
@@ -1787,7 +1965,7 @@ __global__ void __launch_bounds__(C::NTHREADS, 1) sample_kernel(const __grid_con
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::NSTAGE; ++s) {
       mbar_init(&ks.full[s], 1);
-      mbar_init(&ks.empty[s], C::NW);
+      mbar_init(&ks.ready[s], C::NW);
       ks.issued[s] = 0;
       ks.landed[s] = 0;
     }
@@ -1797,40 +1975,52 @@ __global__ void __launch_bounds__(C::NTHREADS, 1) sample_kernel(const __grid_con
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::NSTAGE && s < n_my; ++s) {
       issue_item<C>(P, ks, s, item_pos<C>(P, first + s * stride));
-      ks.issued[s] = 1;
+      atomicAdd(&ks.issued[s], 1);
     }
   }
-  const int g = gidx<C>();
-  const int tid = gtid<C>();
-  Smem<C>& sm = ks.g[g];
-  int slot = 0;
-  ItemParams Q;
-  if (g < n_my) Q = load_params(P, item_pos<C>(P, first + g * stride));
-  for (int it = g; it < n_my; it += C::NG) {
-    const int stage = it % C::NSTAGE;
-    const uint32_t parity = (uint32_t)(it / C::NSTAGE) & 1u;
-    // positions of the items this group prefetches or issues next
-    const int nxt = it + C::NG;
-    const int ref_it = it + C::NSTAGE;
-    const int refill_pos = (tid == 32 && ref_it < n_my) ? item_pos<C>(P, first + ref_it * stride) : 0;
-    const bool ok = mbar_wait_bounded(&ks.full[stage], parity, kWaitLimitNs);
-    if (!ok) atomicOr(P.status, (unsigned)YAPD_STATUS_WAIT_TIMEOUT);
-    if (csync_or<C>(!ok)) break;
-    if (tid == 0) atomicAdd(&ks.landed[stage], 1);
-    ItemParams Qn;
-    if (nxt < n_my) Qn = load_params(P, item_pos<C>(P, first + nxt * stride));
-    compute_item<C, CFG>(P, ks, sm, slot, stage, Q);
-    // warp 1 refills the stage once the whole group has released it
-    if (tid == 32 && ref_it < n_my) {
-      if (mbar_wait_bounded(&ks.empty[stage], parity, kWaitLimitNs)) {
+  if (threadIdx.x < C::NG * C::NT) {
+    // ---- groups ----
+    const int g = gidx<C>();
+    const int tid = gtid<C>();
+    Smem<C>& sm = ks.g[g];
+    int slot = 0;
+    ItemParams Q;
+    if (g < n_my) Q = load_params(P, item_pos<C>(P, first + g * stride));
+    for (int it = g; it < n_my; it += C::NG) {
+      const int stage = it % C::NSTAGE;
+      const uint32_t parity = (uint32_t)(it / C::NSTAGE) & 1u;
+      const int nxt = it + C::NG;
+      const bool ok = mbar_wait_bounded(&ks.full[stage], parity, kWaitLimitNs);
+      if (!ok) atomicOr(P.status, (unsigned)YAPD_STATUS_WAIT_TIMEOUT);
+      if (csync_or<C>(!ok)) break;
+      if (tid == 0) atomicAdd(&ks.landed[stage], 1);
+      ItemParams Qn;
+      if (nxt < n_my) Qn = load_params(P, item_pos<C>(P, first + nxt * stride));
+      compute_item<C, CFG>(P, ks, sm, slot, stage, Q);
+      __syncwarp();
+      if ((threadIdx.x & 31) == 0) mbar_arrive(&ks.ready[stage]);
+      Q = Qn;
+    }
+  } else {
+    // ---- tail warp of group g ----
+    const int g = (threadIdx.x - C::NG * C::NT) >> 5;
+    for (int it = g; it < n_my; it += C::NG) {
+      const int stage = it % C::NSTAGE;
+      const uint32_t parity = (uint32_t)(it / C::NSTAGE) & 1u;
+      const int ref_it = it + C::NSTAGE;
+      const int refill_pos = ref_it < n_my ? item_pos<C>(P, first + ref_it * stride) : 0;
+      if (!mbar_wait_bounded(&ks.ready[stage], parity, kWaitLimitNs)) {
+        if ((threadIdx.x & 31) == 0) atomicOr(P.status, (unsigned)YAPD_STATUS_WAIT_TIMEOUT);
+        break;
+      }
+      if (ks.hand[stage].handed) tail_finish<C, CFG>(P, ks, stage);
+      if ((threadIdx.x & 31) == 0 && ref_it < n_my) {
         fence_proxy_async_smem();
         issue_item<C>(P, ks, stage, refill_pos);
         atomicAdd(&ks.issued[stage], 1);
-      } else {
-        atomicOr(P.status, (unsigned)YAPD_STATUS_WAIT_TIMEOUT);
       }
+      __syncwarp();
     }
-    Q = Qn;
   }
   // copies issued but never waited for (only after a timeout): give them a
   // bounded chance to land before the CTA exits

@@ -192,11 +192,15 @@ __device__ __forceinline__ float load_elem_global(const char* row, int v) {
 template <class C>
 __device__ __forceinline__ float load_elem_smem(const unsigned char* s, const RowGeom& g, int v) {
   if (v >= g.avail) return load_elem_global<C>(g.row, v);
+  const uint32_t a = smem_u32(s) + (uint32_t)(v + g.head) * C::ELEM;
   if constexpr (C::BF16) {
-    const unsigned short h = reinterpret_cast<const unsigned short*>(s)[v + g.head];
+    unsigned short h;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(a));
     return __uint_as_float((uint32_t)h << 16);
   } else {
-    return reinterpret_cast<const float*>(s)[v + g.head];
+    float f;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(f) : "r"(a));
+    return f;
   }
 }
 
@@ -226,7 +230,15 @@ __device__ __forceinline__ float velem(const uint4& q, int i) {
   else return __uint_as_float(w);
 }
 
-__device__ __forceinline__ uint4 lds128(const unsigned char* p) { return *reinterpret_cast<const uint4*>(p); }
+// 16-byte load from the staged rows (explicitly shared-space: the ring is
+// reached through pointers the compiler cannot always classify).
+__device__ __forceinline__ uint4 lds128(const unsigned char* p) {
+  uint4 r;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "r"(smem_u32(p)));
+  return r;
+}
 
 __device__ __forceinline__ uint32_t bmax2(uint32_t a, uint32_t b) {
   uint32_t r;
@@ -1955,9 +1967,8 @@ __device__ __forceinline__ void tail_finish(const SampleParams& P, KSmem<C>& ks,
 // issues the copies of item it + NSTAGE into the stage.
 template <class C, bool CFG>
 __global__ void __launch_bounds__(C::NTHREADS, 1) sample_kernel(const __grid_constant__ SampleParams P) {
-  extern __shared__ unsigned char smem_raw[];
-  KSmem<C>& ks = *reinterpret_cast<KSmem<C>*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  KSmem<C>& ks = *reinterpret_cast<KSmem<C>*>(smem_raw);
   const int n_items = P.fused ? cta_prepare(P, ks.scan) : P.n_identity;
   const int first = blockIdx.x, stride = gridDim.x;
   if (first >= n_items) return;

@@ -139,6 +139,25 @@ struct RowGeom {
   int avail;          // elements [0, avail) are inside the copy
 };
 
+// The record a group leaves for its tail warp: the position's parameters,
+// merged statistics and (when `handed`) its min-p band of at most 32 ids.
+struct ItemParams {
+  int pos;
+  float T, top_p, min_p, rep;
+  int top_k;
+};
+
+struct Hand {
+  // written with the stage's copies (by the warp that issues them)
+  ItemParams Q;
+  RowGeom gc, gu;    // staged cond / uncond rows
+  // written by the group
+  float m[3], s[3];  // group maxima (c, u, z2') and sums relative to them
+  int n;             // band members found (ids of the first 32 in cv)
+  int handed;        // 1: the tail warp resolves the band and writes the outputs
+  int cv[32];
+};
+
 template <class C>
 __device__ __forceinline__ RowGeom row_geom(const SampleParams& P, int64_t elem_off) {
   RowGeom g;
@@ -444,17 +463,36 @@ __device__ int cta_prepare(const SampleParams& P, int* scan) {
 
 // ------------------------------------------------------------ sample kernel
 
+__device__ __forceinline__ ItemParams load_params(const SampleParams& P, int pos) {
+  ItemParams q;
+  const int b = pos / P.L;
+  q.pos = pos;
+  q.T = param_f(P.temperature, P.temperature_s, b);
+  q.top_k = param_i(P.top_k, P.top_k_s, b);
+  q.top_p = param_f(P.top_p, P.top_p_s, b);
+  q.min_p = param_f(P.min_p, P.min_p_s, b);
+  q.rep = param_f(P.rep_penalty, P.rep_penalty_s, b);
+  return q;
+}
+
+// Issue the copies of position Q.pos into `stage` and record its parameters
+// and row geometry for the group (one thread).
 template <class C>
-__device__ __forceinline__ void issue_item(const SampleParams& P, KSmem<C>& ks, int stage, int pos) {
+__device__ __forceinline__ void issue_item(const SampleParams& P, KSmem<C>& ks, int stage, const ItemParams& Q) {
+  const int pos = Q.pos;
   const int b = pos / P.L, l = pos - b * P.L;
   const int64_t base = (int64_t)b * P.stride_req + (int64_t)l * P.stride_pos;
   const RowGeom gc = row_geom<C>(P, base);
   uint32_t bytes = gc.bytes;
-  RowGeom gu;
+  RowGeom gu = gc;
   if (P.nb == 2) {
     gu = row_geom<C>(P, base + P.stride_branch);
     bytes += gu.bytes;
   }
+  Hand& h = ks.hand[stage];
+  h.Q = Q;
+  h.gc = gc;
+  h.gu = gu;
   mbar_arrive_expect_tx(&ks.full[stage], bytes);
   if (gc.bytes) bulk_g2s(ks.stage[stage], gc.src, gc.bytes, &ks.full[stage]);
   if (P.nb == 2 && gu.bytes) bulk_g2s(ks.stage[stage] + C::ROW_SLOT, gu.src, gu.bytes, &ks.full[stage]);
@@ -1193,22 +1231,6 @@ struct Smem {
   unsigned char cflag[C::BAND];
 };
 
-// The record a group leaves for its tail warp: the position's parameters,
-// merged statistics and (when `handed`) its min-p band of at most 32 ids.
-struct ItemParams {
-  int pos;
-  float T, top_p, min_p, rep;
-  int top_k;
-};
-
-struct Hand {
-  ItemParams Q;
-  float m[3], s[3];  // group maxima (c, u, z2') and sums relative to them
-  int n;             // band members found (ids of the first 32 in cv)
-  int handed;        // 1: the tail warp resolves the band and writes the outputs
-  int cv[32];
-};
-
 template <class C>
 struct KSmem {
   uint64_t full[C::NSTAGE];   // rows landed (one expect_tx arrive + the copy bytes)
@@ -1252,13 +1274,13 @@ __device__ __forceinline__ void write_choice(const SampleParams& P, const RowRef
 
 template <class C, bool CFG>
 __device__ __forceinline__ RowRef<C> row_ref(const SampleParams& P, KSmem<C>& ks, int stage, int pos) {
-  const int b = pos / P.L, l = pos - b * P.L;
-  const int64_t base = (int64_t)b * P.stride_req + (int64_t)l * P.stride_pos;
+  (void)P;
+  (void)pos;
   RowRef<C> R;
   R.sc = ks.stage[stage];
   R.su = ks.stage[stage] + C::ROW_SLOT;
-  R.gc = row_geom<C>(P, base);
-  R.gu = CFG ? row_geom<C>(P, base + P.stride_branch) : R.gc;
+  R.gc = ks.hand[stage].gc;
+  R.gu = CFG ? ks.hand[stage].gu : R.gc;
   return R;
 }
 
@@ -1615,17 +1637,6 @@ __device__ __forceinline__ void finish_band(const SampleParams& P, const Smem<C>
   }
 }
 
-__device__ __forceinline__ ItemParams load_params(const SampleParams& P, int pos) {
-  ItemParams q;
-  const int b = pos / P.L;
-  q.pos = pos;
-  q.T = param_f(P.temperature, P.temperature_s, b);
-  q.top_k = param_i(P.top_k, P.top_k_s, b);
-  q.top_p = param_f(P.top_p, P.top_p_s, b);
-  q.min_p = param_f(P.min_p, P.min_p_s, b);
-  q.rep = param_f(P.rep_penalty, P.rep_penalty_s, b);
-  return q;
-}
 
 // One position, worked by the calling group.
 // Parts of the position context that need no statistics.
@@ -1741,7 +1752,6 @@ __device__ __forceinline__ void compute_item(const SampleParams& P, KSmem<C>& ks
   const float lg_minp = band_mode ? fminf(log2f(Q.min_p), 0.f) : 0.f;
   Hand& h = ks.hand[stage];
   if (tid == 0) {
-    h.Q = Q;
     h.n = 0;
     h.handed = 0;
   }
@@ -1985,7 +1995,7 @@ __global__ void __launch_bounds__(C::NTHREADS, 1) sample_kernel(const __grid_con
   __syncthreads();
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::NSTAGE && s < n_my; ++s) {
-      issue_item<C>(P, ks, s, item_pos<C>(P, first + s * stride));
+      issue_item<C>(P, ks, s, load_params(P, item_pos<C>(P, first + s * stride)));
       atomicAdd(&ks.issued[s], 1);
     }
   }
@@ -1995,22 +2005,17 @@ __global__ void __launch_bounds__(C::NTHREADS, 1) sample_kernel(const __grid_con
     const int tid = gtid<C>();
     Smem<C>& sm = ks.g[g];
     int slot = 0;
-    ItemParams Q;
-    if (g < n_my) Q = load_params(P, item_pos<C>(P, first + g * stride));
     for (int it = g; it < n_my; it += C::NG) {
       const int stage = it % C::NSTAGE;
       const uint32_t parity = (uint32_t)(it / C::NSTAGE) & 1u;
-      const int nxt = it + C::NG;
       const bool ok = mbar_wait_bounded(&ks.full[stage], parity, kWaitLimitNs);
       if (!ok) atomicOr(P.status, (unsigned)YAPD_STATUS_WAIT_TIMEOUT);
       if (csync_or<C>(!ok)) break;
       if (tid == 0) atomicAdd(&ks.landed[stage], 1);
-      ItemParams Qn;
-      if (nxt < n_my) Qn = load_params(P, item_pos<C>(P, first + nxt * stride));
+      const ItemParams Q = ks.hand[stage].Q;
       compute_item<C, CFG>(P, ks, sm, slot, stage, Q);
       __syncwarp();
       if ((threadIdx.x & 31) == 0) mbar_arrive(&ks.ready[stage]);
-      Q = Qn;
     }
   } else {
     // ---- tail warp of group g ----
@@ -2019,7 +2024,8 @@ __global__ void __launch_bounds__(C::NTHREADS, 1) sample_kernel(const __grid_con
       const int stage = it % C::NSTAGE;
       const uint32_t parity = (uint32_t)(it / C::NSTAGE) & 1u;
       const int ref_it = it + C::NSTAGE;
-      const int refill_pos = ref_it < n_my ? item_pos<C>(P, first + ref_it * stride) : 0;
+      ItemParams refill{};
+      if (ref_it < n_my) refill = load_params(P, item_pos<C>(P, first + ref_it * stride));
       if (!mbar_wait_bounded(&ks.ready[stage], parity, kWaitLimitNs)) {
         if ((threadIdx.x & 31) == 0) atomicOr(P.status, (unsigned)YAPD_STATUS_WAIT_TIMEOUT);
         break;
@@ -2027,7 +2033,7 @@ __global__ void __launch_bounds__(C::NTHREADS, 1) sample_kernel(const __grid_con
       if (ks.hand[stage].handed) tail_finish<C, CFG>(P, ks, stage);
       if ((threadIdx.x & 31) == 0 && ref_it < n_my) {
         fence_proxy_async_smem();
-        issue_item<C>(P, ks, stage, refill_pos);
+        issue_item<C>(P, ks, stage, refill);
         atomicAdd(&ks.issued[stage], 1);
       }
       __syncwarp();

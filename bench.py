@@ -39,6 +39,7 @@ from yapd_b200 import select as S  # noqa: E402
 from yapd_b200 import workloads as WL  # noqa: E402
 
 METRIC = "logit rows/sec at V=8194"
+LAUNCHES_PER_STEP = 2  # sample_kernel + unmask_kernel per select step
 N_BUFFERS = 5  # rotating logits buffers, total well above the 126 MB L2
 
 
@@ -397,7 +398,7 @@ def run_ours(args, ws, rank, local):
                          "bytes_per_launch": sum(byt) / K},
             "e2e": {"value": e2e_rows / (e2e_ms * 1e-3), "unit": "rows/s",
                     "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"]},
-            "gpu_launches": 4 * args.steps,
+            "gpu_launches": LAUNCHES_PER_STEP * args.steps,
             "clocks": ck,
             "cpu_baseline": cpu,
         }

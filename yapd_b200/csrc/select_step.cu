@@ -1,17 +1,20 @@
 // Block-diffusion select step for B200 (sm_100a).
 //
 // Two kernels, launched on the caller's stream (no host sync, no allocation).
-// sample_kernel runs one CTA per SM.  For the select step every CTA first
-// scans the block state (which positions are masked in a denoising request),
-// writes its own work-list entries and initialises the outputs of the
-// positions it will not sample.  Three groups of four warps then work
-// positions from a 6-deep ring of staged rows: each position's cond and
-// uncond logit rows are staged into shared memory by 1-D bulk copies
-// (cp.async.bulk + mbarrier); CFG, temperature, filters, Gumbel-max and the
-// PMI inputs come from two statistics passes and a candidate band (no sort of
-// the vocabulary).  unmask_kernel then runs one warp per request: position
-// noise, quantile threshold, count schedule, rank, unmask and the state
-// update.
+// The sampling kernel runs one CTA per SM.  For the select step every CTA
+// first scans the block state (which positions are masked in a denoising
+// request), writes its own work-list entries and initialises the outputs of
+// the positions it will not sample.  With bf16 logits (wsample_kernel) teams
+// of warps then work the positions in min-p band mode: each warp streams its
+// share of a position's cond / uncond rows through its own ring of 2 KB
+// chunks (cp.async.bulk + mbarrier) and computes maxima, the sums of the
+// three softmaxes and the candidate band in one pass; the team merges and its
+// first warp resolves the band.  Positions that path does not take, and every
+// position with fp32 logits or of yapd_sample_rows (sample_kernel), go to the
+// grouped pipeline: groups of warps over a 6-deep ring of staged whole rows,
+// two statistics passes and a candidate band (no sort of the vocabulary).
+// unmask_kernel then runs one warp per request: position noise, quantile
+// threshold, count schedule, rank, unmask and the state update.
 //
 // Reference semantics: server/engine.py:533-612 and server/engine_ar.py:220-243
 // of m8than/yapd (see include/yapd_select.h).  The file is compiled with
@@ -394,12 +397,24 @@ __global__ void unmask_kernel(const __grid_constant__ UnmaskParams U, int dense)
   if (b < U.B) unmask_request(U, dense, b);
 }
 
+__device__ __forceinline__ ItemParams load_params(const SampleParams& P, int pos) {
+  ItemParams q;
+  const int b = pos / P.L;
+  q.pos = pos;
+  q.T = param_f(P.temperature, P.temperature_s, b);
+  q.top_k = param_i(P.top_k, P.top_k_s, b);
+  q.top_p = param_f(P.top_p, P.top_p_s, b);
+  q.min_p = param_f(P.min_p, P.min_p_s, b);
+  q.rep = param_f(P.rep_penalty, P.rep_penalty_s, b);
+  return q;
+}
+
 // Select step, preamble run by every CTA: scan the block state (warps own
 // contiguous spans of positions), count the sampled positions and write the
 // work-list entries this CTA will process (entries blockIdx + k*gridDim);
 // initialise the outputs of the unsampled positions p == blockIdx (mod
 // gridDim) (sampled -1, pmi NaN).  Returns the number of sampled positions.
-__device__ int cta_prepare(const SampleParams& P, int* scan) {
+__device__ int cta_prepare(const SampleParams& P, int* scan, ItemParams* items = nullptr, int cap = 0) {
   const UnmaskParams& U = P.U;
   const int total = U.B * U.L;
   const int nwarp = blockDim.x >> 5;
@@ -449,7 +464,11 @@ __device__ int cta_prepare(const SampleParams& P, int* scan) {
       const int p = c0 + r * 32 + lane;
       const bool a = (masks[r] >> lane) & 1u;
       const int idx = base + __popc(masks[r] & lt);
-      if (a && idx % grid == me) P.work_w[idx] = p;
+      if (a && idx % grid == me) {
+        P.work_w[idx] = p;
+        // the CTA's item idx / grid: its sampling parameters, kept on chip
+        if (idx / grid < cap) items[idx / grid] = load_params(P, p);
+      }
       if (!a && p < w1 && p % grid == me) {
         P.sampled[p] = -1;
         U.pmi[p] = __int_as_float(0x7fc00000);
@@ -462,18 +481,6 @@ __device__ int cta_prepare(const SampleParams& P, int* scan) {
 }
 
 // ------------------------------------------------------------ sample kernel
-
-__device__ __forceinline__ ItemParams load_params(const SampleParams& P, int pos) {
-  ItemParams q;
-  const int b = pos / P.L;
-  q.pos = pos;
-  q.T = param_f(P.temperature, P.temperature_s, b);
-  q.top_k = param_i(P.top_k, P.top_k_s, b);
-  q.top_p = param_f(P.top_p, P.top_p_s, b);
-  q.min_p = param_f(P.min_p, P.min_p_s, b);
-  q.rep = param_f(P.rep_penalty, P.rep_penalty_s, b);
-  return q;
-}
 
 // Issue the copies of position Q.pos into `stage` and record its parameters
 // and row geometry for the group (one thread).
@@ -561,13 +568,11 @@ struct RowRef {
   RowGeom gc, gu;
 };
 
-// guided / T exactly as the reference rounds it (server/engine.py:536-538, :548).
-template <class C>
-__device__ __forceinline__ float exact_val(const SampleParams& P, const PosCtx& X, const RowRef<C>& R, int v) {
-  const float c = load_elem_smem<C>(R.sc, R.gc, v);
+// guided / T exactly as the reference rounds it (server/engine.py:536-538,
+// :548), from the token's cond / uncond logits.
+__device__ __forceinline__ float exact_val_cu(const SampleParams& P, const PosCtx& X, float c, float u) {
   float g;
   if (X.cfg) {
-    const float u = load_elem_smem<C>(R.su, R.gu, v);
     const float lsc = __fsub_rn(__fsub_rn(c, X.mc), X.lc);
     const float lsu = __fsub_rn(__fsub_rn(u, X.mu), X.lu);
     g = __fadd_rn(lsc, __fmul_rn(P.cfg_w, __fsub_rn(lsc, lsu)));
@@ -575,6 +580,13 @@ __device__ __forceinline__ float exact_val(const SampleParams& P, const PosCtx& 
     g = c;
   }
   return X.scale ? div_rn(g, X.T, X.rT) : g;
+}
+
+template <class C>
+__device__ __forceinline__ float exact_val(const SampleParams& P, const PosCtx& X, const RowRef<C>& R, int v) {
+  const float c = load_elem_smem<C>(R.sc, R.gc, v);
+  const float u = X.cfg ? load_elem_smem<C>(R.su, R.gu, v) : 0.f;
+  return exact_val_cu(P, X, c, u);
 }
 
 __device__ __forceinline__ float z2_of(const PosCtx& X, float c, float u) {
@@ -1243,17 +1255,21 @@ struct KSmem {
   alignas(128) unsigned char stage[C::NSTAGE][C::STAGE_BYTES];
 };
 
-// softmax(c)[v], softmax(u)[v] as the reference rounds them (server/engine.py:539-540, 553, 556).
+// softmax(c)[v], softmax(u)[v] as the reference rounds them (server/engine.py:539-540, 553, 556),
+// from the token's cond / uncond logits.
+template <bool CFG>
+__device__ __forceinline__ float2 pmi_cu(const PosCtx& X, float cv, float uv) {
+  const float pc = __fmul_rn(expf(__fsub_rn(cv, X.mc)), __fdiv_rn(1.0f, X.Sc));
+  float pu = 0.f;
+  if (CFG) pu = __fmul_rn(expf(__fsub_rn(uv, X.mu)), __fdiv_rn(1.0f, X.Su));
+  return make_float2(pc, pu);
+}
+
 template <class C, bool CFG>
 __device__ __forceinline__ float2 pmi_inputs(const PosCtx& X, const RowRef<C>& R, int v) {
   const float cv = load_elem_smem<C>(R.sc, R.gc, v);
-  const float pc = __fmul_rn(expf(__fsub_rn(cv, X.mc)), __fdiv_rn(1.0f, X.Sc));
-  float pu = 0.f;
-  if (CFG) {
-    const float uv = load_elem_smem<C>(R.su, R.gu, v);
-    pu = __fmul_rn(expf(__fsub_rn(uv, X.mu)), __fdiv_rn(1.0f, X.Su));
-  }
-  return make_float2(pc, pu);
+  const float uv = CFG ? load_elem_smem<C>(R.su, R.gu, v) : 0.f;
+  return pmi_cu<CFG>(X, cv, uv);
 }
 
 // Write the sampled id and the PMI inputs softmax(c)[s], softmax(u)[s]
@@ -1575,69 +1591,6 @@ __device__ __forceinline__ int band_marked(const SampleParams& P, const PosCtx& 
   return sm.misc[0];
 }
 
-// One warp resolves a band of at most 32 candidates: top-p / min-p flags
-// from prefix sums over the exactly sorted band, exact scores (penalty +
-// noise), argmax; the winner's PMI inputs were recorded with the band.
-template <class C>
-__device__ __forceinline__ void finish_band(const SampleParams& P, const Smem<C>& sm, int n, const ScoreCtx& K,
-                                            bool topp_on, float top_p, float min_p) {
-  const int lane = threadIdx.x & 31;
-  unsigned long long key = lane < n ? sm.cand[lane] : 0ull;
-  int q = lane;
-  // bitonic sort, descending, over the smallest power of two >= n lanes
-  int kmax = 2;
-  while (kmax < n) kmax <<= 1;
-  for (int k = 2; k <= kmax; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      const unsigned long long y = __shfl_xor_sync(0xffffffffu, key, j);
-      const int qy = __shfl_xor_sync(0xffffffffu, q, j);
-      const bool up = ((lane & k) == 0) || k == kmax;
-      const bool lower = ((lane & j) == 0);
-      const bool take_max = (up == lower);
-      if (take_max ? (y > key) : (y < key)) {
-        key = y;
-        q = qy;
-      }
-    }
-  }
-  const bool live = lane < n;
-  const int v = cand_id(key);
-  const float vals = cand_val(key);
-  const float e = live ? sm.cande[q] : 0.f;
-  const float p = __fmul_rn(e, K.r);
-  double incl = (double)p;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const double t = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += t;
-  }
-  const float p0 = __shfl_sync(0xffffffffu, p, 0);
-  bool keep = live;
-  if (topp_on) keep = keep && (__fsub_rn((float)incl, p) < top_p);
-  keep = keep && (p >= __fmul_rn(min_p, p0));
-  float sc = keep ? sm.cscore[q] : kNegInf;
-  if (!(sc == sc)) sc = kNegInf;
-  const uint32_t ks = sc > kNegInf ? ord_key(sc) : 0u;
-  unsigned long long rec = ks ? (((unsigned long long)ks << 32) | (uint32_t)(31 - lane)) : 0ull;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const unsigned long long x = __shfl_xor_sync(0xffffffffu, rec, o);
-    rec = x > rec ? x : rec;
-  }
-  const int win_lane = rec ? 31 - (int)(uint32_t)(rec & 0xffffffffu) : 0;
-  if (lane == win_lane) {
-    int chosen = v;
-    float2 pcu = live ? sm.cpc[q] : make_float2(0.f, 0.f);
-    if (!live || chosen < 0 || chosen >= P.V) {
-      atomicOr(P.status, (unsigned)YAPD_STATUS_INTERNAL);
-      chosen = 0;
-    }
-    P.sampled[K.pos] = chosen;
-    if (P.pcu) P.pcu[K.pos] = pcu;
-  }
-}
-
-
 // One position, worked by the calling group.
 // Parts of the position context that need no statistics.
 template <bool CFG>
@@ -1882,37 +1835,22 @@ __device__ __forceinline__ void compute_item(const SampleParams& P, KSmem<C>& ks
   }
 }
 
-// Tail warp: the min-p band of the position recorded for `stage` (at most 32
-// members, one per lane): exact value, mass, score (penalty + noise) per
-// member, a bitonic sort by (exact value, id), top-p / min-p flags from
-// double prefix sums, the best kept score, and the outputs.
+// One warp resolves a min-p band of n <= 32 members (member `v0` in lane
+// < n): exact value, mass and score (penalty + noise) per member, a bitonic
+// sort by (exact value, id), top-p / min-p flags from double prefix sums,
+// the best kept score, and the outputs.
 template <class C, bool CFG>
-__device__ __forceinline__ void tail_finish(const SampleParams& P, KSmem<C>& ks, int stage) {
+__device__ __forceinline__ void band_finish_warp(const SampleParams& P, const ItemParams& Q, const PosCtx& X,
+                                                 const ScoreCtx& K, int n, int v0, float c0, float u0) {
   const int lane = threadIdx.x & 31;
-  const Hand& h = ks.hand[stage];
-  const ItemParams Q = h.Q;
-  const int n = h.n;
-  const RowRef<C> R = row_ref<C, CFG>(P, ks, stage, Q.pos);
-  PosCtx X;
-  float sA;
-  item_ctx<CFG>(P, Q, X, sA);
-  float m[3], s[3];
-#pragma unroll
-  for (int j = 0; j < 3; ++j) {
-    m[j] = h.m[j];
-    s[j] = h.s[j];
-  }
-  ScoreCtx K;
-  stats_core<CFG>(m, s, X);
-  stats_rest<CFG>(P, Q, sA, X, K);
   const bool live0 = lane < n;
-  const int v0 = live0 ? h.cv[lane] : 0;
   unsigned long long key = 0ull;
   float e = 0.f, score = kNegInf;
+  float cw = c0, uw = u0;  // the logits of the member this lane holds (moved with the sort)
   if (live0) {
-    const float vals = exact_val<C>(P, X, R, v0);
+    const float vals = exact_val_cu(P, X, c0, u0);
     key = cand_key(vals, v0);
-    e = ex2_approx(__fsub_rn(z2_smem<C>(X, R, v0), X.zmax));
+    e = ex2_approx(__fsub_rn(z2_of(X, c0, u0), X.zmax));
     score = exact_score<C, true>(P, K, v0, vals);
   }
   // bitonic sort, descending key, over the smallest power of two >= n lanes
@@ -1923,6 +1861,8 @@ __device__ __forceinline__ void tail_finish(const SampleParams& P, KSmem<C>& ks,
       const unsigned long long y = __shfl_xor_sync(0xffffffffu, key, j);
       const float ey = __shfl_xor_sync(0xffffffffu, e, j);
       const float sy = __shfl_xor_sync(0xffffffffu, score, j);
+      const float cy = __shfl_xor_sync(0xffffffffu, cw, j);
+      const float uy = __shfl_xor_sync(0xffffffffu, uw, j);
       const bool up = ((lane & k) == 0) || k == kmax;
       const bool lower = ((lane & j) == 0);
       const bool take_max = (up == lower);
@@ -1930,6 +1870,8 @@ __device__ __forceinline__ void tail_finish(const SampleParams& P, KSmem<C>& ks,
         key = y;
         e = ey;
         score = sy;
+        cw = cy;
+        uw = uy;
       }
     }
   }
@@ -1963,26 +1905,48 @@ __device__ __forceinline__ void tail_finish(const SampleParams& P, KSmem<C>& ks,
       chosen = 0;
     }
     P.sampled[Q.pos] = chosen;
-    if (P.pcu) P.pcu[Q.pos] = pmi_inputs<C, CFG>(X, R, chosen);
+    if (P.pcu) P.pcu[Q.pos] = pmi_cu<CFG>(X, cw, uw);
   }
   __syncwarp();
 }
 
-// One CTA per SM: NG groups of NT threads, each working one position at a
-// time from a shared NSTAGE-deep ring of staged rows, and one tail warp per
-// group.  Local item `it` (the CTA's it-th position) uses stage it % NSTAGE
-// and group it % NG (NG divides NSTAGE, so each stage serves one group).  The
-// group runs the statistics and either finishes the position or hands its
-// band to the group's tail warp; the tail warp finishes a handed band, then
-// issues the copies of item it + NSTAGE into the stage.
+// Tail warp: the min-p band of the position recorded for `stage`.
 template <class C, bool CFG>
-__global__ void __launch_bounds__(C::NTHREADS, 1) sample_kernel(const __grid_constant__ SampleParams P) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  KSmem<C>& ks = *reinterpret_cast<KSmem<C>*>(smem_raw);
-  const int n_items = P.fused ? cta_prepare(P, ks.scan) : P.n_identity;
-  const int first = blockIdx.x, stride = gridDim.x;
-  if (first >= n_items) return;
-  const int n_my = (n_items - first + stride - 1) / stride;
+__device__ __forceinline__ void tail_finish(const SampleParams& P, KSmem<C>& ks, int stage) {
+  const int lane = threadIdx.x & 31;
+  const Hand& h = ks.hand[stage];
+  const ItemParams Q = h.Q;
+  const int n = h.n;
+  const RowRef<C> R = row_ref<C, CFG>(P, ks, stage, Q.pos);
+  PosCtx X;
+  float sA;
+  item_ctx<CFG>(P, Q, X, sA);
+  float m[3], s[3];
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    m[j] = h.m[j];
+    s[j] = h.s[j];
+  }
+  ScoreCtx K;
+  stats_core<CFG>(m, s, X);
+  stats_rest<CFG>(P, Q, sA, X, K);
+  const int v0 = lane < n ? h.cv[lane] : 0;
+  const float c0 = load_elem_smem<C>(R.sc, R.gc, v0);
+  const float u0 = CFG ? load_elem_smem<C>(R.su, R.gu, v0) : 0.f;
+  band_finish_warp<C, CFG>(P, Q, X, K, n, v0, c0, u0);
+}
+
+// The grouped pipeline over this CTA's items 0..n_my-1 (global item index
+// first + k * stride): NG groups of NT threads, each working one position at
+// a time from a shared NSTAGE-deep ring of staged rows, and one tail warp per
+// group.  Local item `it` uses stage it % NSTAGE and group it % NG (NG
+// divides NSTAGE, so each stage serves one group).  The group runs the
+// statistics and either finishes the position or hands its band to the
+// group's tail warp; the tail warp finishes a handed band, then issues the
+// copies of item it + NSTAGE into the stage.  Threads past C::NTHREADS only
+// take part in the CTA barriers.
+template <class C, bool CFG>
+__device__ __forceinline__ void group_phase(const SampleParams& P, KSmem<C>& ks, int n_my, int first, int stride) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::NSTAGE; ++s) {
       mbar_init(&ks.full[s], 1);
@@ -1994,6 +1958,8 @@ __global__ void __launch_bounds__(C::NTHREADS, 1) sample_kernel(const __grid_con
   }
   __syncthreads();
   if (threadIdx.x == 0) {
+    // the stages may have been read through the generic proxy before
+    fence_proxy_async_smem();
     for (int s = 0; s < C::NSTAGE && s < n_my; ++s) {
       issue_item<C>(P, ks, s, load_params(P, item_pos<C>(P, first + s * stride)));
       atomicAdd(&ks.issued[s], 1);
@@ -2017,7 +1983,7 @@ __global__ void __launch_bounds__(C::NTHREADS, 1) sample_kernel(const __grid_con
       __syncwarp();
       if ((threadIdx.x & 31) == 0) mbar_arrive(&ks.ready[stage]);
     }
-  } else {
+  } else if (threadIdx.x < C::NTHREADS) {
     // ---- tail warp of group g ----
     const int g = (threadIdx.x - C::NG * C::NT) >> 5;
     for (int it = g; it < n_my; it += C::NG) {
@@ -2040,13 +2006,724 @@ __global__ void __launch_bounds__(C::NTHREADS, 1) sample_kernel(const __grid_con
     }
   }
   // copies issued but never waited for (only after a timeout): give them a
-  // bounded chance to land before the CTA exits
+  // bounded chance to land before the CTA moves on
   __syncthreads();
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::NSTAGE; ++s)
       for (int q = ks.landed[s]; q < ks.issued[s]; ++q)
         (void)mbar_wait_bounded(&ks.full[s], (uint32_t)q & 1u, kWaitLimitNs);
   }
+}
+
+// One CTA per SM (grouped pipeline only): token sampling of independent rows
+// (yapd_sample_rows) and the fp32 select step.
+template <class C, bool CFG>
+__global__ void __launch_bounds__(C::NTHREADS, 1) sample_kernel(const __grid_constant__ SampleParams P) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  KSmem<C>& ks = *reinterpret_cast<KSmem<C>*>(smem_raw);
+  const int n_items = P.fused ? cta_prepare(P, ks.scan) : P.n_identity;
+  const int first = blockIdx.x, stride = gridDim.x;
+  if (first >= n_items) return;
+  const int n_my = (n_items - first + stride - 1) / stride;
+  group_phase<C, CFG>(P, ks, n_my, first, stride);
+}
+
+// ------------------------------------------------------- warp-per-position path
+//
+// bf16 select step.  Positions in min-p band mode (min-p on, top-k off) are
+// worked by teams of T warps (T = 1 when the CTA has at least 9 positions, up
+// to 16 when it has one).  Warp r of a team streams chunks r, r + T, ... of
+// the position's cond / uncond rows through its own ring of slots (1-D bulk
+// copies issued by its lane 0, one mbarrier per slot) and computes, in one
+// pass: the exact row maxima (bf16 max), the three sums of exponentials
+// against per-lane references (the maxima of the lane's first vector), and
+// the vectors that can reach the min-p band (largest z2' against the warp's
+// running maximum), which it copies to its stash.  Lanes merge with shuffles,
+// warps through shared memory; the band is collected from the stashes and
+// resolved by the team's first warp (band_finish_warp, or band_finish_wide
+// for up to BANDW members) while the others move on.  Other filter modes,
+// wider bands, non-finite rows and rows whose cond / uncond copies differ in
+// alignment are deferred to the grouped pipeline, which the same CTA runs
+// afterwards over its deferred items.
+
+struct WCfg {
+  static constexpr int NWARP = 16;
+  static constexpr int NTHREADS = NWARP * 32;
+  static constexpr int CHV = 128;            // 16-byte vectors per chunk and row
+  static constexpr int CHB = CHV * 16;       // bytes per chunk and row
+  static constexpr int NSLOT = 2;            // ring slots per warp
+  static constexpr int TPC = CHV / 32;       // vectors per lane and chunk
+  static constexpr int MAXCH = ((YAPD_MAX_V * 2 + 15) / 16 + CHV - 1) / CHV;  // chunks per position
+  static constexpr int STASH = 32;           // marked vectors a warp keeps on chip per position
+  static constexpr int ICAP = 256;           // item parameter records on chip per CTA
+  static constexpr int BANDW = 128;          // widest band the warp path resolves
+};
+static_assert(WCfg::MAXCH * WCfg::TPC <= 64, "the marks of a position fit one 64-bit word");
+static_assert(WCfg::NTHREADS >= CfgBF16::NTHREADS, "the grouped pipeline runs inside the warp kernel's CTA");
+
+// Work-list entries of deferred positions carry this bit until the CTA
+// compacts them (positions are below 2^30).
+constexpr int kDeferBit = 1 << 30;
+
+// A position as the warp path sees it.
+struct WItem {
+  ItemParams Q;
+  RowGeom gc, gu;
+  Span S;
+  int nvi;  // interior vectors S.j1 - S.j0
+  int nch;  // chunks
+  bool ok;  // eligible for the warp path
+};
+
+struct WStash {
+  uint4 c[WCfg::STASH];
+  uint4 u[WCfg::STASH];
+  int j[WCfg::STASH];  // vector index in the row copy
+};
+
+// Band members of a position (ids and logits), then the wide finisher's
+// sorted arrays.
+struct WBand {
+  int n;
+  int id[WCfg::BANDW];
+  float c[WCfg::BANDW];
+  float u[WCfg::BANDW];
+  float w[WCfg::BANDW];
+};
+
+struct WSmem {
+  int scan[32];
+  int ndef;
+  uint64_t bar[WCfg::NWARP][WCfg::NSLOT];
+  float wstat[WCfg::NWARP][2][6];  // per-warp (m, s) of the statistics, by item parity
+  WItem item[WCfg::NWARP];         // the position each warp is working
+  ItemParams items[WCfg::ICAP];    // sampling parameters of the CTA's first ICAP items
+  WStash stash[WCfg::NWARP];
+  WBand band[WCfg::NWARP];
+  alignas(128) unsigned char ring[WCfg::NWARP][WCfg::NSLOT][2 * WCfg::CHB];
+};
+
+// The parameters of this CTA's item k (on chip for the first ICAP items).
+__device__ __forceinline__ ItemParams w_params(const SampleParams& P, const WSmem& ws, int k, int first,
+                                               int stride) {
+  if (k < WCfg::ICAP) return ws.items[k];
+  return load_params(P, P.work_w[first + k * stride] & ~kDeferBit);
+}
+
+template <bool CFG>
+__device__ __forceinline__ WItem witem(const SampleParams& P, const ItemParams& Q) {
+  using C = CfgBF16;
+  WItem I;
+  I.Q = Q;
+  const int b = Q.pos / P.L, l = Q.pos - b * P.L;
+  const int64_t base = (int64_t)b * P.stride_req + (int64_t)l * P.stride_pos;
+  I.gc = row_geom<C>(P, base);
+  I.gu = CFG ? row_geom<C>(P, base + P.stride_branch) : I.gc;
+  RowRef<C> R;
+  R.sc = R.su = nullptr;
+  R.gc = I.gc;
+  R.gu = I.gu;
+  I.S = make_span<C, CFG>(R, P.V);
+  I.nvi = I.S.j1 - I.S.j0;
+  I.nch = (I.nvi + WCfg::CHV - 1) / WCfg::CHV;
+  const bool topk_on = Q.top_k > 0 && Q.top_k < P.V;
+  I.ok = Q.min_p > 0.0f && !topk_on && (!CFG || I.gc.head == I.gu.head) && I.nch <= WCfg::MAXCH &&
+         I.S.nscal <= 32;
+  return I;
+}
+
+// Team layout of the CTA: NTEAM teams of T warps; team `team`, rank `r`.
+struct WTeam {
+  int T, NTEAM, team, r;
+};
+
+// Copy cursor of a warp (lane 0): chunks r, r + T, ... of the team's
+// eligible items k = team, team + NTEAM, ... in order.
+struct WCursor {
+  int k;            // CTA-local item index
+  int q, nch, nvi;  // next chunk, chunks and interior vectors of item k
+  const char* c;    // first interior vector of the cond / uncond copies
+  const char* u;
+  uint32_t gi;      // chunks issued so far
+};
+
+// Issue the warp's next chunk into its slot; false at the end of the stream.
+template <bool CFG>
+__device__ __forceinline__ bool w_issue(const SampleParams& P, WSmem& ws, int warp, const WTeam& tm, int n_my,
+                                        int first, int stride, WCursor& c) {
+  while (c.q >= c.nch) {
+    c.k += tm.NTEAM;
+    if (c.k >= n_my) {
+      c.k = n_my;
+      c.q = c.nch = 0;
+      return false;
+    }
+    const WItem I = witem<CFG>(P, w_params(P, ws, c.k, first, stride));
+    c.q = tm.r;
+    c.nch = I.ok ? I.nch : 0;
+    c.nvi = I.nvi;
+    c.c = I.gc.src + I.S.j0 * 16;
+    c.u = I.gu.src + I.S.j0 * 16;
+  }
+  const int s = (int)(c.gi % WCfg::NSLOT);
+  const int nv = min(WCfg::CHV, c.nvi - c.q * WCfg::CHV);
+  const uint32_t bytes = (uint32_t)nv * 16u;
+  uint64_t* bar = &ws.bar[warp][s];
+  mbar_arrive_expect_tx(bar, CFG ? 2u * bytes : bytes);
+  bulk_g2s(ws.ring[warp][s], c.c + c.q * WCfg::CHB, bytes, bar);
+  if (CFG) bulk_g2s(ws.ring[warp][s] + WCfg::CHB, c.u + c.q * WCfg::CHB, bytes, bar);
+  c.q += tm.T;
+  ++c.gi;
+  return true;
+}
+
+__device__ __forceinline__ uint4 ldg128(const char* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// The lane's sums again from global memory against new references (a lane
+// whose maxima lie more than 2^100 from its first vector's references).
+template <bool CFG>
+__device__ __noinline__ void w_resum(const WItem I, const WTeam tm, int lane, float xsc, float xsu, float nmcL,
+                                     float nmuL, float nzr, float A2, float nB2, float& sc, float& su, float& s) {
+  float a0 = 0.f, b0 = 0.f, c0 = 0.f;
+  for (int q = tm.r; q < I.nch; q += tm.T) {
+    const int nv = min(WCfg::CHV, I.nvi - q * WCfg::CHV);
+    for (int v = lane; v < nv; v += 32) {
+      const int j = I.S.j0 + q * WCfg::CHV + v;
+      const uint4 a = ldg128(I.gc.src + j * 16);
+      uint4 b = a;
+      if (CFG) b = ldg128(I.gu.src + j * 16);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float c = velem<CfgBF16>(a, i);
+        a0 += ex2_approx(__fmaf_rn(c, kLog2e, nmcL));
+        if (CFG) {
+          const float u = velem<CfgBF16>(b, i);
+          b0 += ex2_approx(__fmaf_rn(u, kLog2e, nmuL));
+          c0 += ex2_approx(__fmaf_rn(c, A2, __fmaf_rn(u, nB2, nzr)));
+        } else {
+          c0 += ex2_approx(__fmaf_rn(c, A2, nzr));
+        }
+      }
+    }
+  }
+  if (tm.r == 0 && lane < I.S.nscal) {
+    a0 += ex2_approx(__fmaf_rn(xsc, kLog2e, nmcL));
+    if (CFG) {
+      b0 += ex2_approx(__fmaf_rn(xsu, kLog2e, nmuL));
+      c0 += ex2_approx(__fmaf_rn(xsc, A2, __fmaf_rn(xsu, nB2, nzr)));
+    } else {
+      c0 += ex2_approx(__fmaf_rn(xsc, A2, nzr));
+    }
+  }
+  sc = a0;
+  su = b0;
+  s = c0;
+}
+
+__device__ __forceinline__ float finite_or0(float x) {
+  return (x > kNegInf && x < __int_as_float(0x7f800000)) ? x : 0.f;
+}
+
+// Barrier over the warps of a team (named barrier 1 + team; one warp: none).
+__device__ __forceinline__ void team_sync(const WTeam& tm) {
+  if (tm.T > 1) named_sync(1 + tm.team, tm.T * 32);
+  else __syncwarp();
+}
+
+__device__ __forceinline__ void band_push(WBand& B, int id, float c, float u) {
+  const int at = atomicAdd(&B.n, 1);
+  if (at < WCfg::BANDW) {
+    B.id[at] = id;
+    B.c[at] = c;
+    B.u[at] = u;
+  }
+}
+
+// The band members of 16-byte vector j (row copy index) into B.
+template <bool CFG>
+__device__ __forceinline__ void band_vector(const PosCtx& X, const Span& S, int j, const uint4& a, const uint4& b,
+                                            float lo_z, WBand& B) {
+  using C = CfgBF16;
+  const int v0 = j * C::W - S.head;
+#pragma unroll
+  for (int i = 0; i < C::W; ++i) {
+    const float c = velem<C>(a, i);
+    const float u = CFG ? velem<C>(b, i) : 0.f;
+    if (z2_of(X, c, u) >= lo_z) band_push(B, v0 + i, c, u);
+  }
+}
+
+// Leader warp: a band of 32 < n <= BANDW members.  Exact value, mass and
+// score per member (four per lane), rank by (exact value, id), then top-p /
+// min-p flags from double prefix sums in rank order and the best kept score
+// (ties to the lower rank), as band_finish_warp does for a one-lane band.
+template <bool CFG>
+__device__ __noinline__ void band_finish_wide(const SampleParams& P, const ItemParams Q, const PosCtx X,
+                                              const ScoreCtx K, WBand& B, int n) {
+  using C = CfgBF16;
+  constexpr int PER = WCfg::BANDW / 32;
+  const int lane = threadIdx.x & 31;
+  unsigned long long key[PER];
+  float e[PER], sc[PER], cw[PER], uw[PER];
+  int id[PER];
+#pragma unroll
+  for (int t = 0; t < PER; ++t) {
+    const int i = lane + 32 * t;
+    key[t] = 0ull;
+    e[t] = 0.f;
+    sc[t] = kNegInf;
+    id[t] = 0;
+    cw[t] = uw[t] = 0.f;
+    if (i < n) {
+      id[t] = B.id[i];
+      cw[t] = B.c[i];
+      uw[t] = B.u[i];
+      const float vals = exact_val_cu(P, X, cw[t], uw[t]);
+      key[t] = cand_key(vals, id[t]);
+      e[t] = ex2_approx(__fsub_rn(z2_of(X, cw[t], uw[t]), X.zmax));
+      sc[t] = exact_score<C, true>(P, K, id[t], vals);
+    }
+  }
+  __syncwarp();
+  // keys to shared memory (high word in c, low word in u), then ranks
+#pragma unroll
+  for (int t = 0; t < PER; ++t) {
+    const int i = lane + 32 * t;
+    if (i < n) {
+      B.c[i] = __uint_as_float((uint32_t)(key[t] >> 32));
+      B.u[i] = __uint_as_float((uint32_t)key[t]);
+    }
+  }
+  __syncwarp();
+  int rank[PER];
+#pragma unroll
+  for (int t = 0; t < PER; ++t) rank[t] = 0;
+  for (int j = 0; j < n; ++j) {
+    const unsigned long long kj =
+        ((unsigned long long)__float_as_uint(B.c[j]) << 32) | __float_as_uint(B.u[j]);
+#pragma unroll
+    for (int t = 0; t < PER; ++t) rank[t] += (kj > key[t]) ? 1 : 0;
+  }
+  __syncwarp();
+  // rank order: mass in c, score in u, id in id
+#pragma unroll
+  for (int t = 0; t < PER; ++t) {
+    if (lane + 32 * t < n) {
+      B.c[rank[t]] = e[t];
+      B.u[rank[t]] = sc[t];
+      B.w[rank[t]] = __int_as_float(id[t]);
+    }
+  }
+  __syncwarp();
+  const float p0 = __fmul_rn(B.c[0], K.r);
+  double carry = 0.0;
+  unsigned long long best = 0ull;
+  for (int r0 = 0; r0 < n; r0 += 32) {
+    const int r = r0 + lane;
+    const bool live = r < n;
+    const float p = live ? __fmul_rn(B.c[r], K.r) : 0.f;
+    double incl = (double)p;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    incl += carry;
+    carry = __shfl_sync(0xffffffffu, incl, 31);
+    bool keep = live;
+    if (Q.top_p < 1.0f) keep = keep && (__fsub_rn((float)incl, p) < Q.top_p);
+    keep = keep && (p >= __fmul_rn(Q.min_p, p0));
+    float s = keep ? B.u[r] : kNegInf;
+    if (!(s == s)) s = kNegInf;
+    const uint32_t ks = s > kNegInf ? ord_key(s) : 0u;
+    const unsigned long long rec = ks ? (((unsigned long long)ks << 32) | (uint32_t)(0x7fffffff - r)) : 0ull;
+    best = rec > best ? rec : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long x = __shfl_xor_sync(0xffffffffu, best, o);
+    best = x > best ? x : best;
+  }
+  const int win = best ? 0x7fffffff - (int)(uint32_t)(best & 0xffffffffu) : 0;
+  const int chosen_id = __float_as_int(B.w[win]);
+#pragma unroll
+  for (int t = 0; t < PER; ++t) {
+    if (lane + 32 * t < n && rank[t] == win) {
+      int chosen = chosen_id;
+      if (chosen < 0 || chosen >= P.V) {
+        atomicOr(P.status, (unsigned)YAPD_STATUS_INTERNAL);
+        chosen = 0;
+      }
+      P.sampled[Q.pos] = chosen;
+      if (P.pcu) P.pcu[Q.pos] = pmi_cu<CFG>(X, cw[t], uw[t]);
+    }
+  }
+  __syncwarp();
+}
+
+// One position by one warp of its team.  Returns false when the team defers
+// the position (the same answer in every warp of the team).  `gcons` counts
+// the chunks this warp has consumed; `ok_wait` turns false when a slot wait
+// expired (the warp then keeps the team's barriers but reads nothing more).
+template <bool CFG>
+__device__ __forceinline__ bool w_position(const SampleParams& P, WSmem& ws, int warp, const WTeam& tm,
+                                           int parity, int n_my, int first, int stride, uint32_t& gcons,
+                                           WCursor& cur, bool& ok_wait) {
+  using C = CfgBF16;
+  const int lane = threadIdx.x & 31;
+  const WItem& I = ws.item[warp];
+  const ItemParams Q = I.Q;
+  const float kPosInf = __int_as_float(0x7f800000);
+  const int leader = tm.team * tm.T;
+  WBand& B = ws.band[tm.T > 1 ? leader + parity : warp];
+  WStash& st_ = ws.stash[warp];
+  PosCtx X;
+  float sA;
+  item_ctx<CFG>(P, Q, X, sA);
+  const float A2 = X.A2, nB2 = -X.B2;
+  const float lg_minp = fminf(log2f(Q.min_p), 0.f);
+  // scalar elements (partial vectors at the row ends): rank 0, one per lane
+  const bool has_scalar = tm.r == 0 && lane < I.S.nscal;
+  float xsc = kNegInf, xsu = kNegInf;
+  if (has_scalar) {
+    const int v = scalar_v(I.S, lane);
+    xsc = load_elem_global<C>(I.gc.row, v);
+    if (CFG) xsu = load_elem_global<C>(I.gu.row, v);
+  }
+  const unsigned long long L2p = f2_pack(kLog2e, kLog2e), A2p = f2_pack(A2, A2), nB2p = f2_pack(nB2, nB2);
+  const unsigned long long zero = f2_pack(0.f, 0.f);
+  uint32_t cm2 = 0xff80ff80u, um2 = 0xff80ff80u;
+  unsigned long long scp = zero, sup = zero, sp = zero;
+  unsigned long long nrcp = zero, nrup = zero, nrzp = zero;
+  float rc = 0.f, ru = 0.f, rz = 0.f;
+  float dm = kNegInf, W = kNegInf, mg_min = kBig;
+  unsigned long long ovf = 0ull;  // marked vectors the stash could not take
+  int nst = 0;                    // stash entries (warp-uniform)
+  bool first_vec = true;
+  for (int q = tm.r; q < I.nch; q += tm.T) {
+    // after an expired wait nothing more is read (the chunks still count as
+    // issued, so the drain at the end waits for them)
+    if (!ok_wait) continue;
+    const int s = (int)(gcons % WCfg::NSLOT);
+    const uint32_t par = (gcons / WCfg::NSLOT) & 1u;
+    const bool ok = mbar_wait_bounded(&ws.bar[warp][s], par, kWaitLimitNs);
+    if (!__all_sync(0xffffffffu, ok)) {
+      if (lane == 0) atomicOr(P.status, (unsigned)YAPD_STATUS_WAIT_TIMEOUT);
+      ok_wait = false;
+      continue;
+    }
+    ++gcons;
+    const int nv = min(WCfg::CHV, I.nvi - q * WCfg::CHV);
+    const unsigned char* slot = ws.ring[warp][s];
+    float vzl[WCfg::TPC];
+#pragma unroll
+    for (int t = 0; t < WCfg::TPC; ++t) {
+      const int v = lane + 32 * t;
+      vzl[t] = kNegInf;
+      if (v < nv) {
+        const uint4 a = lds128(slot + v * 16);
+        uint4 b = a;
+        if (CFG) b = lds128(slot + WCfg::CHB + v * 16);
+        const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+        const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+        const uint32_t ac = bmax2(bmax2(a.x, a.y), bmax2(a.z, a.w));
+        cm2 = bmax2(cm2, ac);
+        uint32_t au = 0u;
+        if (CFG) {
+          au = bmax2(bmax2(b.x, b.y), bmax2(b.z, b.w));
+          um2 = bmax2(um2, au);
+        }
+        if (t == 0 && first_vec) {
+          // references: this lane's first vector's maxima
+          rc = __fmul_rn(finite_or0(fmaxf(bf16lo(ac), bf16hi(ac))), kLog2e);
+          ru = CFG ? __fmul_rn(finite_or0(fmaxf(bf16lo(au), bf16hi(au))), kLog2e) : 0.f;
+          float zm = kNegInf;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const unsigned long long cx = f2_bf16(aw[k]);
+            const unsigned long long zx =
+                CFG ? f2_fma(cx, A2p, f2_fma(f2_bf16(bw[k]), nB2p, zero)) : f2_fma(cx, A2p, zero);
+            float lo, hi;
+            f2_unpack(zx, lo, hi);
+            zm = fmax3(zm, lo, hi);
+          }
+          rz = finite_or0(zm);
+          nrcp = f2_pack(-rc, -rc);
+          nrup = f2_pack(-ru, -ru);
+          nrzp = f2_pack(-rz, -rz);
+        }
+        float m = kNegInf;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const unsigned long long cx = f2_bf16(aw[k]);
+          unsigned long long dx;
+          float lo, hi;
+          if (CFG) {
+            const unsigned long long ux = f2_bf16(bw[k]);
+            dx = f2_fma(cx, A2p, f2_fma(ux, nB2p, nrzp));
+            f2_unpack(f2_fma(ux, L2p, nrup), lo, hi);
+            sup = f2_add(sup, f2_pack(ex2_approx(lo), ex2_approx(hi)));
+          } else {
+            dx = f2_fma(cx, A2p, nrzp);
+          }
+          f2_unpack(f2_fma(cx, L2p, nrcp), lo, hi);
+          scp = f2_add(scp, f2_pack(ex2_approx(lo), ex2_approx(hi)));
+          f2_unpack(dx, lo, hi);
+          sp = f2_add(sp, f2_pack(ex2_approx(lo), ex2_approx(hi)));
+          m = fmax3(m, lo, hi);
+        }
+        vzl[t] = m;
+        dm = fmaxf(dm, m);
+      }
+    }
+    first_vec = false;
+    // marks: vectors whose largest z2' reaches the running maximum + log2(min_p)
+    float cmx = vzl[0];
+#pragma unroll
+    for (int t = 1; t < WCfg::TPC; ++t) cmx = fmaxf(cmx, vzl[t]);
+    W = fmaxf(W, warp_max(__fadd_rn(cmx, rz)));
+    const float mg = __fadd_rn(0.02f, __fmul_rn(1e-4f, fabsf(W)));
+    mg_min = fminf(mg_min, mg);
+    const float thr = __fsub_rn(__fadd_rn(W, lg_minp), mg);
+    uint32_t mk = 0u;
+#pragma unroll
+    for (int t = 0; t < WCfg::TPC; ++t)
+      mk |= ((__fadd_rn(vzl[t], rz) >= thr || !(thr > kNegInf)) && lane + 32 * t < nv ? 1u : 0u) << t;
+    // marked vectors to the stash (warp-aggregated slots)
+    const int cnt = __popc(mk);
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    int at = nst + incl - cnt;
+    nst += __shfl_sync(0xffffffffu, incl, 31);
+    while (mk) {
+      const int t = __ffs(mk) - 1;
+      mk &= mk - 1u;
+      const int v = lane + 32 * t;
+      if (at < WCfg::STASH) {
+        st_.c[at] = lds128(slot + v * 16);
+        st_.u[at] = CFG ? lds128(slot + WCfg::CHB + v * 16) : make_uint4(0u, 0u, 0u, 0u);
+        st_.j[at] = I.S.j0 + q * WCfg::CHV + v;
+      } else {
+        ovf |= 1ull << ((q / tm.T) * WCfg::TPC + t);
+      }
+      ++at;
+    }
+    __syncwarp();
+    if (lane == 0) {
+      fence_proxy_async_smem();
+      (void)w_issue<CFG>(P, ws, warp, tm, n_my, first, stride, cur);
+    }
+  }
+  // lane statistics (with the scalar elements)
+  float sc0, sc1, su0, su1, s0, s1;
+  f2_unpack(scp, sc0, sc1);
+  f2_unpack(sup, su0, su1);
+  f2_unpack(sp, s0, s1);
+  float sc = sc0 + sc1, su = su0 + su1, s = s0 + s1;
+  float mcl = fmaxf(bf16lo(cm2), bf16hi(cm2));
+  float mul = CFG ? fmaxf(bf16lo(um2), bf16hi(um2)) : kNegInf;
+  if (has_scalar) {
+    mcl = fmaxf(mcl, xsc);
+    sc += ex2_approx(__fmaf_rn(xsc, kLog2e, -rc));
+    float dz;
+    if (CFG) {
+      mul = fmaxf(mul, xsu);
+      su += ex2_approx(__fmaf_rn(xsu, kLog2e, -ru));
+      dz = __fmaf_rn(xsc, A2, __fmaf_rn(xsu, nB2, -rz));
+    } else {
+      dz = __fmaf_rn(xsc, A2, -rz);
+    }
+    s += ex2_approx(dz);
+    dm = fmaxf(dm, dz);
+  }
+  // a lane whose maxima lie far from its references (more than 2^100 either
+  // way: terms could overflow or flush) sums again
+  const float zabs = dm > kNegInf ? __fadd_rn(rz, dm) : kNegInf;
+  const bool far =
+      (mcl > kNegInf && mcl < kPosInf && fabsf(__fsub_rn(__fmul_rn(mcl, kLog2e), rc)) > 100.f) ||
+      (CFG && mul > kNegInf && mul < kPosInf && fabsf(__fsub_rn(__fmul_rn(mul, kLog2e), ru)) > 100.f) ||
+      (dm > kNegInf && dm < kPosInf && fabsf(dm) > 100.f);
+  if (far && ok_wait) {
+    rc = __fmul_rn(finite_or0(mcl), kLog2e);
+    ru = CFG ? __fmul_rn(finite_or0(mul), kLog2e) : 0.f;
+    rz = finite_or0(zabs);
+    w_resum<CFG>(I, tm, lane, xsc, xsu, -rc, -ru, -rz, A2, nB2, sc, su, s);
+  }
+  // merge: lanes (shuffles), then the team's warps (shared memory)
+  float m3[3] = {mcl, CFG ? mul : kNegInf, zabs};
+  const float r3[3] = {rc, ru, rz};
+  float s3[3] = {sc, su, s};
+  const float mscale[3] = {kLog2e, kLog2e, 1.0f};
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const float Mw = warp_max(m3[j]);
+    float sj = s3[j];
+    if (m3[j] > kNegInf && Mw < kPosInf) sj = __fmul_rn(sj, ex2_approx(__fsub_rn(r3[j], __fmul_rn(Mw, mscale[j]))));
+    m3[j] = Mw;
+    s3[j] = warp_sum(sj);
+  }
+  if (tm.T > 1) {
+    if (lane == 0) {
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        ws.wstat[warp][parity][j] = m3[j];
+        ws.wstat[warp][parity][3 + j] = s3[j];
+      }
+      if (tm.r == 0) B.n = 0;
+    }
+    team_sync(tm);
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      const float mq = lane < tm.T ? ws.wstat[leader + lane][parity][j] : kNegInf;
+      const float sq = lane < tm.T ? ws.wstat[leader + lane][parity][3 + j] : 0.f;
+      float M = mq;
+      for (int o = 1; o < tm.T; o <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+      float f = sq;
+      if (mq > kNegInf && M < kPosInf)
+        f = __fmul_rn(sq, ex2_approx(__fsub_rn(__fmul_rn(mq, mscale[j]), __fmul_rn(M, mscale[j]))));
+      for (int o = 1; o < tm.T; o <<= 1) f += __shfl_xor_sync(0xffffffffu, f, o);
+      m3[j] = __shfl_sync(0xffffffffu, M, 0);
+      s3[j] = __shfl_sync(0xffffffffu, f, 0);
+    }
+  } else {
+    if (lane == 0) B.n = 0;
+    __syncwarp();
+  }
+  stats_core<CFG>(m3, s3, X);
+  // (team-uniform: every warp of the team holds the same statistics)
+  if (!(X.Sc == X.Sc) || (CFG && !(X.Su == X.Su)) || !(X.S == X.S) || !(X.zmax > kNegInf)) return false;
+  ScoreCtx K;
+  stats_rest<CFG>(P, Q, sA, X, K);
+  // the band {z2 >= lo_z}: stash, overflowed marks, scalar elements
+  const float zm = __fadd_rn(X.zmax, lg_minp);
+  const float lo_z = __fsub_rn(zm, zmargin(zm));
+  const float zmp = __fadd_rn(m3[2], lg_minp);
+  const float need = __fadd_rn(zmargin(zmp), __fadd_rn(1e-3f, __fmul_rn(4e-6f, __fadd_rn(fabsf(X.K2), fabsf(zmp)))));
+  if (mg_min >= need) {
+    for (int i = lane; i < min(nst, WCfg::STASH); i += 32)
+      band_vector<CFG>(X, I.S, st_.j[i], st_.c[i], st_.u[i], lo_z, B);
+    while (ovf) {
+      const int bit = __ffsll((long long)ovf) - 1;
+      ovf &= ovf - 1ull;
+      const int q = tm.r + tm.T * (bit / WCfg::TPC);
+      const int v = lane + 32 * (bit % WCfg::TPC) + WCfg::CHV * q;
+      const int j = I.S.j0 + v;
+      const uint4 a = ldg128(I.gc.src + j * 16);
+      const uint4 b = CFG ? ldg128(I.gu.src + j * 16) : a;
+      band_vector<CFG>(X, I.S, j, a, b, lo_z, B);
+    }
+  } else {
+    // the running margins were too thin for this warp: test all its vectors
+    for (int q = tm.r; q < I.nch; q += tm.T) {
+      const int nv = min(WCfg::CHV, I.nvi - q * WCfg::CHV);
+      for (int v = lane; v < nv; v += 32) {
+        const int j = I.S.j0 + q * WCfg::CHV + v;
+        const uint4 a = ldg128(I.gc.src + j * 16);
+        const uint4 b = CFG ? ldg128(I.gu.src + j * 16) : a;
+        band_vector<CFG>(X, I.S, j, a, b, lo_z, B);
+      }
+    }
+  }
+  if (has_scalar && z2_of(X, xsc, CFG ? xsu : 0.f) >= lo_z) band_push(B, scalar_v(I.S, lane), xsc, xsu);
+  team_sync(tm);
+  if (tm.r != 0) return true;  // the team's first warp resolves the band
+  const int n = B.n;
+  if (n <= 0 || n > WCfg::BANDW) return false;
+  if (n <= 32) {
+    const bool live = lane < n;
+    band_finish_warp<C, CFG>(P, Q, X, K, n, live ? B.id[lane] : 0, live ? B.c[lane] : 0.f,
+                             live ? B.u[lane] : 0.f);
+  } else {
+    band_finish_wide<CFG>(P, Q, X, K, B, n);
+  }
+  return true;
+}
+
+// bf16 select step: preamble, the warp-per-position pass over this CTA's
+// items, then the grouped pipeline over the items it deferred.
+template <bool CFG>
+__global__ void __launch_bounds__(WCfg::NTHREADS, 1) wsample_kernel(const __grid_constant__ SampleParams P) {
+  using C = CfgBF16;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  WSmem& ws = *reinterpret_cast<WSmem*>(smem_raw);
+  const int n_items = cta_prepare(P, ws.scan, ws.items, WCfg::ICAP);
+  const int first = blockIdx.x, stride = gridDim.x;
+  if (first >= n_items) return;
+  const int n_my = (n_items - first + stride - 1) / stride;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // teams: the fewer the items, the more warps per item
+  WTeam tm;
+  tm.NTEAM = WCfg::NWARP;
+  while (tm.NTEAM > 1 && (tm.NTEAM >> 1) >= n_my) tm.NTEAM >>= 1;
+  tm.T = WCfg::NWARP / tm.NTEAM;
+  tm.team = warp / tm.T;
+  tm.r = warp % tm.T;
+  if (lane == 0) {
+    for (int s = 0; s < WCfg::NSLOT; ++s) mbar_init(&ws.bar[warp][s], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  WCursor cur;
+  cur.k = tm.team - tm.NTEAM;
+  cur.q = cur.nch = cur.nvi = 0;
+  cur.c = cur.u = nullptr;
+  cur.gi = 0;
+  if (lane == 0)
+    for (int s = 0; s < WCfg::NSLOT; ++s)
+      if (!w_issue<CFG>(P, ws, warp, tm, n_my, first, stride, cur)) break;
+  uint32_t gcons = 0;
+  bool ok_wait = true;
+  int parity = 0;
+  for (int k = tm.team; k < n_my; k += tm.NTEAM) {
+    const int idx = first + k * stride;
+    if (lane == 0) ws.item[warp] = witem<CFG>(P, w_params(P, ws, k, first, stride));
+    __syncwarp();
+    bool done = false;
+    if (ws.item[warp].ok) {
+      done = w_position<CFG>(P, ws, warp, tm, parity, n_my, first, stride, gcons, cur, ok_wait);
+      parity ^= 1;
+    }
+    if (!done && tm.r == 0 && lane == 0) P.work_w[idx] = ws.item[warp].Q.pos | kDeferBit;
+    __syncwarp();
+  }
+  // copies issued but not consumed (only after an expired wait)
+  const uint32_t gi = __shfl_sync(0xffffffffu, cur.gi, 0);
+  if (lane == 0) {
+    for (uint32_t g = gcons; g < gi; ++g)
+      (void)mbar_wait_bounded(&ws.bar[warp][g % WCfg::NSLOT], (g / WCfg::NSLOT) & 1u, kWaitLimitNs);
+    for (int s = 0; s < WCfg::NSLOT; ++s)
+      asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_u32(&ws.bar[warp][s])) : "memory");
+  }
+  __syncthreads();
+  // compact the deferred entries to the front of this CTA's work-list slots
+  if (warp == 0) {
+    int j = 0;
+    for (int k0 = 0; k0 < n_my; k0 += 32) {
+      const int k = k0 + lane;
+      const int e = k < n_my ? P.work_w[first + k * stride] : 0;
+      const bool d = k < n_my && (e & kDeferBit);
+      const unsigned bal = __ballot_sync(0xffffffffu, d);
+      __syncwarp();
+      if (d) P.work_w[first + (j + __popc(bal & ((1u << lane) - 1u))) * stride] = e & ~kDeferBit;
+      j += __popc(bal);
+      __syncwarp();
+    }
+    if (lane == 0) ws.ndef = j;
+  }
+  __syncthreads();
+  const int n_def = ws.ndef;
+  __syncthreads();
+  if (n_def > 0) group_phase<C, CFG>(P, *reinterpret_cast<KSmem<C>*>(smem_raw), n_def, first, stride);
 }
 
 // ---------------------------------------------------------------- host side
@@ -2056,11 +2733,27 @@ constexpr size_t smem_bytes() {
   return sizeof(KSmem<C>) + 128;
 }
 
+constexpr size_t wsmem_bytes() {
+  return (sizeof(WSmem) > sizeof(KSmem<CfgBF16>) ? sizeof(WSmem) : sizeof(KSmem<CfgBF16>)) + 128;
+}
+
 struct DevInfo {
   int sms = 0;
   int occ[2][2] = {{0, 0}, {0, 0}};  // [bf16][cfg]
   bool init = false;
 };
+
+template <bool CFG>
+static int prepare_wkernel() {
+  if (cudaFuncSetAttribute(wsample_kernel<CFG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem_bytes()) !=
+      cudaSuccess)
+    return YAPD_ERR_LAUNCH;
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, wsample_kernel<CFG>, WCfg::NTHREADS, wsmem_bytes()) !=
+      cudaSuccess)
+    return YAPD_ERR_LAUNCH;
+  return occ >= 1 ? YAPD_OK : YAPD_ERR_LAUNCH;
+}
 
 static DevInfo g_dev[64];
 
@@ -2086,6 +2779,8 @@ static int device_info(DevInfo** out) {
     if (rc == YAPD_OK) rc = prepare_kernel<CfgBF16, false>(&d.occ[1][0]);
     if (rc == YAPD_OK) rc = prepare_kernel<CfgF32, true>(&d.occ[0][1]);
     if (rc == YAPD_OK) rc = prepare_kernel<CfgF32, false>(&d.occ[0][0]);
+    if (rc == YAPD_OK) rc = prepare_wkernel<true>();
+    if (rc == YAPD_OK) rc = prepare_wkernel<false>();
     if (rc != YAPD_OK) return rc;
     d.init = true;
   }
@@ -2139,7 +2834,11 @@ static int launch_sample(const SampleParams& P, int dtype, int max_items, cudaSt
   const bool bf = dtype == YAPD_DTYPE_BF16;
   const bool cfg = P.nb == 2;
   const int occ = d->occ[bf ? 1 : 0][cfg ? 1 : 0];
-  if (bf) {
+  if (bf && P.fused) {
+    // select step: warp-per-position kernel, one CTA per SM
+    if (cfg) wsample_kernel<true><<<d->sms, WCfg::NTHREADS, wsmem_bytes(), st>>>(P);
+    else wsample_kernel<false><<<d->sms, WCfg::NTHREADS, wsmem_bytes(), st>>>(P);
+  } else if (bf) {
     if (cfg) launch_one<CfgBF16, true>(P, occ, d->sms, max_items, st);
     else launch_one<CfgBF16, false>(P, occ, d->sms, max_items, st);
   } else {

@@ -173,3 +173,26 @@ def test_status_word_clear():
     inp = make_config(0, seed=1)
     run_gpu(inp)
     assert S.read_status() == 0
+
+
+@pytest.mark.parametrize("scale", [0.9, 1.1, 1.3, 2.0])
+@pytest.mark.parametrize("noise", ["explicit", "philox"])
+def test_min_p_band_widths(scale, noise):
+    # bf16 CFG rows without boosted tokens: the min-p band of a N(0, scale)
+    # row holds roughly 140, 90, 45 and 18 tokens for these scales, so the
+    # one-lane, the four-per-lane and the deferred band paths all run
+    inp = make_config(1, seed=int(scale * 100), B=6, masked="ragged", explicit_noise=(noise == "explicit"))
+    g = torch.Generator().manual_seed(int(scale * 1000))
+    inp.logits = (torch.randn(inp.logits.shape, generator=g) * scale).to(inp.logits.dtype)
+    inp = _uniform(inp, temperature=0.8, top_k=0, top_p=0.95, min_p=0.05, rep=1.2)
+    check(inp, noise=noise, seed=99, offset=3, dense=False)
+
+
+def test_min_p_wide_bands_many_items():
+    # 2560 positions: each CTA holds more items than it has warps, so the
+    # wide bands of items that are not a warp's last are resolved in the warp
+    inp = make_config(1, seed=77, B=80, masked="all")
+    g = torch.Generator().manual_seed(7)
+    inp.logits = (torch.randn(inp.logits.shape, generator=g) * 1.1).to(inp.logits.dtype)
+    inp = _uniform(inp, temperature=0.8, top_k=0, top_p=0.95, min_p=0.05, rep=1.2)
+    check(inp, dense=True)

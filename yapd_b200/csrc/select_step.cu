@@ -94,6 +94,29 @@ struct UnmaskParams {
   uint8_t* is_commit_out;
 };
 
+// Unsigned division by an invariant divisor d >= 1 for dividends below 2^31:
+// q = umulhi(x, m) >> sh with l = ceil(log2 d), m = ceil(2^(31 + l) / d),
+// sh = l - 1 (Granlund and Montgomery, PLDI 1994; for d >= 2, m < 2^32 and
+// the error term stays below 1/d).  d = 1 is the identity.
+struct DivU {
+  uint32_t m;
+  int sh;
+  int d;
+};
+static inline DivU divu_make(int d) {
+  DivU r{0u, 0, d};
+  if (d <= 1) return r;
+  int l = 0;
+  while ((1ull << l) < (unsigned long long)d) ++l;
+  const unsigned long long num = 1ull << (31 + l);
+  r.m = (uint32_t)((num + (unsigned long long)d - 1) / (unsigned long long)d);
+  r.sh = l - 1;
+  return r;
+}
+__device__ __forceinline__ int divu(int x, const DivU& f) {
+  return f.d <= 1 ? x : (int)(__umulhi((uint32_t)x, f.m) >> f.sh);
+}
+
 // Kernel parameters (flattened from the C ABI structs on the host).
 struct SampleParams {
   // logits
@@ -130,6 +153,8 @@ struct SampleParams {
   // outputs of the positions they do not sample
   int fused;
   int dense;                // every position is sampled
+  DivU div_L;               // division by L
+  DivU div_grid;            // division by the launch's grid size
   int32_t* work_w;          // work list (each CTA writes its own entries)
   UnmaskParams U;
 };
@@ -397,6 +422,14 @@ __global__ void unmask_kernel(const __grid_constant__ UnmaskParams U, int dense)
   if (b < U.B) unmask_request(U, dense, b);
 }
 
+// Sampling parameters of the first RCAP requests, kept on chip by the
+// preamble of the warp kernel.
+constexpr int kReqCap = 512;
+struct ReqTable {
+  float T[kReqCap], top_p[kReqCap], min_p[kReqCap], rep[kReqCap];
+  int top_k[kReqCap];
+};
+
 __device__ __forceinline__ ItemParams load_params(const SampleParams& P, int pos) {
   ItemParams q;
   const int b = pos / P.L;
@@ -409,12 +442,28 @@ __device__ __forceinline__ ItemParams load_params(const SampleParams& P, int pos
   return q;
 }
 
+// The request table: every thread loads the parameters of requests
+// threadIdx.x + k * blockDim.x (the first kReqCap).
+__device__ __forceinline__ void load_req_table(const SampleParams& P, ReqTable& rt) {
+  const int nb = min(P.B, kReqCap);
+  for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+    rt.T[b] = param_f(P.temperature, P.temperature_s, b);
+    rt.top_k[b] = param_i(P.top_k, P.top_k_s, b);
+    rt.top_p[b] = param_f(P.top_p, P.top_p_s, b);
+    rt.min_p[b] = param_f(P.min_p, P.min_p_s, b);
+    rt.rep[b] = param_f(P.rep_penalty, P.rep_penalty_s, b);
+  }
+}
+
 // Select step, preamble run by every CTA: scan the block state (warps own
 // contiguous spans of positions), count the sampled positions and write the
 // work-list entries this CTA will process (entries blockIdx + k*gridDim);
 // initialise the outputs of the unsampled positions p == blockIdx (mod
 // gridDim) (sampled -1, pmi NaN).  Returns the number of sampled positions.
-__device__ int cta_prepare(const SampleParams& P, int* scan, ItemParams* items = nullptr, int cap = 0) {
+// With `rt`, the request table is loaded alongside the first scan loads and
+// the positions of the CTA's first `cap` items go to items_pos[].
+__device__ int cta_prepare(const SampleParams& P, int* scan, ReqTable* rt = nullptr, int* items_pos = nullptr,
+                           int cap = 0) {
   const UnmaskParams& U = P.U;
   const int total = U.B * U.L;
   const int nwarp = blockDim.x >> 5;
@@ -426,15 +475,17 @@ __device__ int cta_prepare(const SampleParams& P, int* scan, ItemParams* items =
   const int span = (((total + nwarp - 1) / nwarp) + 31) & ~31;
   const int w0 = min(w * span, total), w1 = min(w0 + span, total);
   const bool one_chunk = span <= kR * 32;
-  auto chunk = [&](int c0, unsigned (&m)[kR]) {
+  auto chunk = [&](int c0, unsigned (&m)[kR], bool with_table) {
     int64_t xv[kR];
     uint8_t cv[kR];
 #pragma unroll
     for (int r = 0; r < kR; ++r) {
       const int pc = min(c0 + r * 32 + lane, total - 1);
       xv[r] = U.xt[pc];
-      cv[r] = U.is_commit[pc / U.L];
+      cv[r] = U.is_commit[divu(pc, P.div_L)];
     }
+    // the table loads go out while the scan loads are in flight
+    if (with_table) load_req_table(P, *rt);
 #pragma unroll
     for (int r = 0; r < kR; ++r) {
       const int p = c0 + r * 32 + lane;
@@ -444,10 +495,11 @@ __device__ int cta_prepare(const SampleParams& P, int* scan, ItemParams* items =
   unsigned masks[kR];
   int cnt = 0;
   for (int c0 = w0; c0 < w1; c0 += kR * 32) {
-    chunk(c0, masks);
+    chunk(c0, masks, rt != nullptr && c0 == w0);
 #pragma unroll
     for (int r = 0; r < kR; ++r) cnt += __popc(masks[r]);
   }
+  if (rt != nullptr && w0 >= w1) load_req_table(P, *rt);
   if (lane == 0) scan[w] = cnt;
   __syncthreads();
   int base = 0, tot = 0;
@@ -458,18 +510,19 @@ __device__ int cta_prepare(const SampleParams& P, int* scan, ItemParams* items =
   }
   const unsigned lt = (1u << lane) - 1u;
   for (int c0 = w0; c0 < w1; c0 += kR * 32) {
-    if (!one_chunk) chunk(c0, masks);
+    if (!one_chunk) chunk(c0, masks, false);
 #pragma unroll
     for (int r = 0; r < kR; ++r) {
       const int p = c0 + r * 32 + lane;
       const bool a = (masks[r] >> lane) & 1u;
       const int idx = base + __popc(masks[r] & lt);
-      if (a && idx % grid == me) {
+      const int qi = divu(idx, P.div_grid);
+      if (a && idx - qi * grid == me) {
         P.work_w[idx] = p;
-        // the CTA's item idx / grid: its sampling parameters, kept on chip
-        if (idx / grid < cap) items[idx / grid] = load_params(P, p);
+        // the CTA's item qi
+        if (qi < cap) items_pos[qi] = p;
       }
-      if (!a && p < w1 && p % grid == me) {
+      if (!a && p < w1 && p - divu(p, P.div_grid) * grid == me) {
         P.sampled[p] = -1;
         U.pmi[p] = __int_as_float(0x7fc00000);
       }
@@ -769,12 +822,29 @@ struct ScoreCtx {
   float r, minp_thr;  // min-p: keep iff 2^(z2-zmax) * r >= minp_thr
 };
 
+// The memory-borne inputs of a token's score (history bit, noise), fetched
+// ahead of the arithmetic so that their latency overlaps other work.
+struct ScoreIn {
+  bool hb;
+  float nz;
+};
+template <bool INL = false>
+__device__ __forceinline__ ScoreIn score_in(const SampleParams& P, const ScoreCtx& K, int v) {
+  ScoreIn r;
+  r.hb = K.pen_on ? hist_bit(P, K.b, v) : false;
+  r.nz = K.noisy ? noise_at<INL>(P, K.b, K.pos, K.l, v) : 0.f;
+  return r;
+}
+__device__ __forceinline__ float score_from(const ScoreCtx& K, float vals, const ScoreIn& in) {
+  float s = vals;
+  if (K.pen_on && in.hb) s = penalize(vals, K.rep, K.rrep);
+  if (K.noisy) s = __fadd_rn(s, in.nz);
+  return s;
+}
+
 template <class C, bool INL = false>
 __device__ __forceinline__ float exact_score(const SampleParams& P, const ScoreCtx& K, int v, float vals) {
-  float s = vals;
-  if (K.pen_on && hist_bit(P, K.b, v)) s = penalize(vals, K.rep, K.rrep);
-  if (K.noisy) s = __fadd_rn(s, noise_at<INL>(P, K.b, K.pos, K.l, v));
-  return s;
+  return score_from(K, vals, score_in<INL>(P, K, v));
 }
 
 template <class C>
@@ -1848,10 +1918,11 @@ __device__ __forceinline__ void band_finish_warp(const SampleParams& P, const It
   float e = 0.f, score = kNegInf;
   float cw = c0, uw = u0;  // the logits of the member this lane holds (moved with the sort)
   if (live0) {
+    const ScoreIn si = score_in<true>(P, K, v0);
     const float vals = exact_val_cu(P, X, c0, u0);
     key = cand_key(vals, v0);
     e = ex2_approx(__fsub_rn(z2_of(X, c0, u0), X.zmax));
-    score = exact_score<C, true>(P, K, v0, vals);
+    score = score_from(K, vals, si);
   }
   // bitonic sort, descending key, over the smallest power of two >= n lanes
   int kmax = 2;
@@ -2054,11 +2125,13 @@ struct WCfg {
   static constexpr int NSLOT = 2;            // ring slots per warp
   static constexpr int TPC = CHV / 32;       // vectors per lane and chunk
   static constexpr int MAXCH = ((YAPD_MAX_V * 2 + 15) / 16 + CHV - 1) / CHV;  // chunks per position
-  static constexpr int STASH = 32;           // marked vectors a warp keeps on chip per position
-  static constexpr int ICAP = 256;           // item parameter records on chip per CTA
+  static constexpr int STASH = 64;           // marked vectors a warp keeps on chip per position
+  static constexpr int ICAP = 256;           // item positions on chip per CTA
+  static constexpr int IREC = 64;            // full item records on chip per CTA
   static constexpr int BANDW = 128;          // widest band the warp path resolves
 };
 static_assert(WCfg::MAXCH * WCfg::TPC <= 64, "the marks of a position fit one 64-bit word");
+static_assert(WCfg::STASH == 64, "the stash compaction holds two entries per lane");
 static_assert(WCfg::NTHREADS >= CfgBF16::NTHREADS, "the grouped pipeline runs inside the warp kernel's CTA");
 
 // Work-list entries of deferred positions carry this bit until the CTA
@@ -2078,7 +2151,8 @@ struct WItem {
 struct WStash {
   uint4 c[WCfg::STASH];
   uint4 u[WCfg::STASH];
-  int j[WCfg::STASH];  // vector index in the row copy
+  int j[WCfg::STASH];    // vector index in the row copy
+  float z[WCfg::STASH];  // largest z2' of the vector
 };
 
 // Band members of a position (ids and logits), then the wide finisher's
@@ -2091,23 +2165,46 @@ struct WBand {
   float w[WCfg::BANDW];
 };
 
+// A band wider than 32 of a team's last item, resolved by the whole CTA
+// after the warp pass (cta_finish_wide) instead of by the leader alone.
+struct WPend {
+  int n;     // members (0: nothing pending)
+  int area;  // the WBand holding them
+  ItemParams Q;
+  PosCtx X;
+  ScoreCtx K;
+};
+
 struct WSmem {
   int scan[32];
   int ndef;
+  WPend pend[WCfg::NWARP];
   uint64_t bar[WCfg::NWARP][WCfg::NSLOT];
   float wstat[WCfg::NWARP][2][6];  // per-warp (m, s) of the statistics, by item parity
-  WItem item[WCfg::NWARP];         // the position each warp is working
-  ItemParams items[WCfg::ICAP];    // sampling parameters of the CTA's first ICAP items
+  WItem item[WCfg::NWARP];         // the position each warp is working (items past IREC)
+  WItem irec[WCfg::IREC];           // the CTA's first IREC items
+  int items_pos[WCfg::ICAP];        // positions of the CTA's first ICAP items
+  ReqTable req;                     // sampling parameters of the first kReqCap requests
   WStash stash[WCfg::NWARP];
   WBand band[WCfg::NWARP];
   alignas(128) unsigned char ring[WCfg::NWARP][WCfg::NSLOT][2 * WCfg::CHB];
 };
 
-// The parameters of this CTA's item k (on chip for the first ICAP items).
+// The parameters of this CTA's item k (from shared memory for the first
+// ICAP items of requests below kReqCap).
 __device__ __forceinline__ ItemParams w_params(const SampleParams& P, const WSmem& ws, int k, int first,
                                                int stride) {
-  if (k < WCfg::ICAP) return ws.items[k];
-  return load_params(P, P.work_w[first + k * stride] & ~kDeferBit);
+  const int pos = k < WCfg::ICAP ? ws.items_pos[k] : (P.work_w[first + k * stride] & ~kDeferBit);
+  const int b = pos / P.L;
+  if (b >= kReqCap) return load_params(P, pos);
+  ItemParams q;
+  q.pos = pos;
+  q.T = ws.req.T[b];
+  q.top_k = ws.req.top_k[b];
+  q.top_p = ws.req.top_p[b];
+  q.min_p = ws.req.min_p[b];
+  q.rep = ws.req.rep[b];
+  return q;
 }
 
 template <bool CFG>
@@ -2130,6 +2227,13 @@ __device__ __forceinline__ WItem witem(const SampleParams& P, const ItemParams& 
   I.ok = Q.min_p > 0.0f && !topk_on && (!CFG || I.gc.head == I.gu.head) && I.nch <= WCfg::MAXCH &&
          I.S.nscal <= 32;
   return I;
+}
+
+// This CTA's item k (the first IREC from shared memory).
+template <bool CFG>
+__device__ __forceinline__ WItem w_item(const SampleParams& P, const WSmem& ws, int k, int first, int stride) {
+  if (k < WCfg::IREC) return ws.irec[k];
+  return witem<CFG>(P, w_params(P, ws, k, first, stride));
 }
 
 // Team layout of the CTA: NTEAM teams of T warps; team `team`, rank `r`.
@@ -2158,7 +2262,7 @@ __device__ __forceinline__ bool w_issue(const SampleParams& P, WSmem& ws, int wa
       c.q = c.nch = 0;
       return false;
     }
-    const WItem I = witem<CFG>(P, w_params(P, ws, c.k, first, stride));
+    const WItem I = w_item<CFG>(P, ws, c.k, first, stride);
     c.q = tm.r;
     c.nch = I.ok ? I.nch : 0;
     c.nvi = I.nvi;
@@ -2259,91 +2363,118 @@ __device__ __forceinline__ void band_vector(const PosCtx& X, const Span& S, int 
   }
 }
 
-// Leader warp: a band of 32 < n <= BANDW members.  Exact value, mass and
-// score per member (four per lane), rank by (exact value, id), then top-p /
-// min-p flags from double prefix sums in rank order and the best kept score
-// (ties to the lower rank), as band_finish_warp does for a one-lane band.
+// Leader warp: a band of 32 < n <= BANDW members (four per lane).  Exact
+// value, mass and score (penalty + noise) per member, the four of a lane
+// computed side by side; each member's rank by (exact value, id) and the
+// double sum of the masses ranked above it (exact: at most BANDW floats of
+// nearby exponents) give the top-p / min-p flags with the arithmetic of
+// band_finish_warp's prefix sums; then the best kept score (ties to the lower
+// rank).
 template <bool CFG>
-__device__ __noinline__ void band_finish_wide(const SampleParams& P, const ItemParams Q, const PosCtx X,
-                                              const ScoreCtx K, WBand& B, int n) {
+__device__ __forceinline__ void band_finish_wide(const SampleParams& P, const ItemParams& Q, const PosCtx& X,
+                                                 const ScoreCtx& K, WBand& B, int n) {
   using C = CfgBF16;
   constexpr int PER = WCfg::BANDW / 32;
   const int lane = threadIdx.x & 31;
   unsigned long long key[PER];
-  float e[PER], sc[PER], cw[PER], uw[PER];
+  float pm[PER], sc[PER], cw[PER], uw[PER];
   int id[PER];
 #pragma unroll
   for (int t = 0; t < PER; ++t) {
     const int i = lane + 32 * t;
-    key[t] = 0ull;
-    e[t] = 0.f;
-    sc[t] = kNegInf;
-    id[t] = 0;
-    cw[t] = uw[t] = 0.f;
-    if (i < n) {
-      id[t] = B.id[i];
-      cw[t] = B.c[i];
-      uw[t] = B.u[i];
-      const float vals = exact_val_cu(P, X, cw[t], uw[t]);
-      key[t] = cand_key(vals, id[t]);
-      e[t] = ex2_approx(__fsub_rn(z2_of(X, cw[t], uw[t]), X.zmax));
-      sc[t] = exact_score<C, true>(P, K, id[t], vals);
-    }
+    const int ic = i < n ? i : 0;
+    id[t] = B.id[ic];
+    cw[t] = B.c[ic];
+    uw[t] = B.u[ic];
+  }
+  ScoreIn si[PER];
+#pragma unroll
+  for (int t = 0; t < PER; ++t) si[t] = score_in<true>(P, K, id[t]);
+#pragma unroll
+  for (int t = 0; t < PER; ++t) {
+    const float vals = exact_val_cu(P, X, cw[t], uw[t]);
+    key[t] = cand_key(vals, id[t]);
+    pm[t] = __fmul_rn(ex2_approx(__fsub_rn(z2_of(X, cw[t], uw[t]), X.zmax)), K.r);
+    sc[t] = score_from(K, vals, si[t]);
+    if (!(sc[t] == sc[t])) sc[t] = kNegInf;
   }
   __syncwarp();
-  // keys to shared memory (high word in c, low word in u), then ranks
+  // key (high word in c, low word in u) and mass (w) of every member
 #pragma unroll
   for (int t = 0; t < PER; ++t) {
     const int i = lane + 32 * t;
     if (i < n) {
       B.c[i] = __uint_as_float((uint32_t)(key[t] >> 32));
       B.u[i] = __uint_as_float((uint32_t)key[t]);
+      B.w[i] = pm[t];
     }
   }
   __syncwarp();
   int rank[PER];
+  double above[PER];
 #pragma unroll
-  for (int t = 0; t < PER; ++t) rank[t] = 0;
-  for (int j = 0; j < n; ++j) {
+  for (int t = 0; t < PER; ++t) {
+    rank[t] = 0;
+    above[t] = 0.0;
+  }
+  double above2[PER];
+#pragma unroll
+  for (int t = 0; t < PER; ++t) above2[t] = 0.0;
+  int j = 0;
+  for (; j + 1 < n; j += 2) {
+    const unsigned long long k0 =
+        ((unsigned long long)__float_as_uint(B.c[j]) << 32) | __float_as_uint(B.u[j]);
+    const unsigned long long k1 =
+        ((unsigned long long)__float_as_uint(B.c[j + 1]) << 32) | __float_as_uint(B.u[j + 1]);
+    const double p0j = (double)B.w[j], p1j = (double)B.w[j + 1];
+#pragma unroll
+    for (int t = 0; t < PER; ++t) {
+      const bool u0 = k0 > key[t], u1 = k1 > key[t];
+      rank[t] += (u0 ? 1 : 0) + (u1 ? 1 : 0);
+      above[t] += u0 ? p0j : 0.0;
+      above2[t] += u1 ? p1j : 0.0;
+    }
+  }
+  if (j < n) {
     const unsigned long long kj =
         ((unsigned long long)__float_as_uint(B.c[j]) << 32) | __float_as_uint(B.u[j]);
+    const double pj = (double)B.w[j];
 #pragma unroll
-    for (int t = 0; t < PER; ++t) rank[t] += (kj > key[t]) ? 1 : 0;
+    for (int t = 0; t < PER; ++t) {
+      const bool up = kj > key[t];
+      rank[t] += up ? 1 : 0;
+      above[t] += up ? pj : 0.0;
+    }
   }
-  __syncwarp();
-  // rank order: mass in c, score in u, id in id
+#pragma unroll
+  for (int t = 0; t < PER; ++t) above[t] += above2[t];
+  // the mass of the member ranked first
+  float p0l = 0.f;
+  bool h0 = false;
+#pragma unroll
+  for (int t = 0; t < PER; ++t) {
+    if (lane + 32 * t < n && rank[t] == 0) {
+      p0l = pm[t];
+      h0 = true;
+    }
+  }
+  const unsigned b0 = __ballot_sync(0xffffffffu, h0);
+  const float p0 = __shfl_sync(0xffffffffu, p0l, b0 ? __ffs(b0) - 1 : 0);
+  unsigned long long best = 0ull;
 #pragma unroll
   for (int t = 0; t < PER; ++t) {
     if (lane + 32 * t < n) {
-      B.c[rank[t]] = e[t];
-      B.u[rank[t]] = sc[t];
-      B.w[rank[t]] = __int_as_float(id[t]);
+      const double incl = above[t] + (double)pm[t];
+      bool keep = true;
+      if (Q.top_p < 1.0f) keep = __fsub_rn((float)incl, pm[t]) < Q.top_p;
+      keep = keep && (pm[t] >= __fmul_rn(Q.min_p, p0));
+      if (keep) {
+        const uint32_t ks = sc[t] > kNegInf ? ord_key(sc[t]) : 0u;
+        const unsigned long long rec =
+            ks ? (((unsigned long long)ks << 32) | (uint32_t)(0x7fffffff - rank[t])) : 0ull;
+        best = rec > best ? rec : best;
+      }
     }
-  }
-  __syncwarp();
-  const float p0 = __fmul_rn(B.c[0], K.r);
-  double carry = 0.0;
-  unsigned long long best = 0ull;
-  for (int r0 = 0; r0 < n; r0 += 32) {
-    const int r = r0 + lane;
-    const bool live = r < n;
-    const float p = live ? __fmul_rn(B.c[r], K.r) : 0.f;
-    double incl = (double)p;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const double t = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += t;
-    }
-    incl += carry;
-    carry = __shfl_sync(0xffffffffu, incl, 31);
-    bool keep = live;
-    if (Q.top_p < 1.0f) keep = keep && (__fsub_rn((float)incl, p) < Q.top_p);
-    keep = keep && (p >= __fmul_rn(Q.min_p, p0));
-    float s = keep ? B.u[r] : kNegInf;
-    if (!(s == s)) s = kNegInf;
-    const uint32_t ks = s > kNegInf ? ord_key(s) : 0u;
-    const unsigned long long rec = ks ? (((unsigned long long)ks << 32) | (uint32_t)(0x7fffffff - r)) : 0ull;
-    best = rec > best ? rec : best;
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -2351,11 +2482,10 @@ __device__ __noinline__ void band_finish_wide(const SampleParams& P, const ItemP
     best = x > best ? x : best;
   }
   const int win = best ? 0x7fffffff - (int)(uint32_t)(best & 0xffffffffu) : 0;
-  const int chosen_id = __float_as_int(B.w[win]);
 #pragma unroll
   for (int t = 0; t < PER; ++t) {
     if (lane + 32 * t < n && rank[t] == win) {
-      int chosen = chosen_id;
+      int chosen = id[t];
       if (chosen < 0 || chosen >= P.V) {
         atomicOr(P.status, (unsigned)YAPD_STATUS_INTERNAL);
         chosen = 0;
@@ -2372,16 +2502,25 @@ __device__ __noinline__ void band_finish_wide(const SampleParams& P, const ItemP
 // the chunks this warp has consumed; `ok_wait` turns false when a slot wait
 // expired (the warp then keeps the team's barriers but reads nothing more).
 template <bool CFG>
-__device__ __forceinline__ bool w_position(const SampleParams& P, WSmem& ws, int warp, const WTeam& tm,
-                                           int parity, int n_my, int first, int stride, uint32_t& gcons,
-                                           WCursor& cur, bool& ok_wait) {
+__device__ __forceinline__ bool w_position(const SampleParams& P, WSmem& ws, const WItem& I, int warp,
+                                           const WTeam& tm, int parity, bool last, int n_my, int first,
+                                           int stride, uint32_t& gcons, WCursor& cur, bool& ok_wait) {
   using C = CfgBF16;
   const int lane = threadIdx.x & 31;
-  const WItem& I = ws.item[warp];
   const ItemParams Q = I.Q;
+  if (tm.r == 0 && lane == 0 && P.history_kind != YAPD_HISTORY_NONE && P.history != nullptr && Q.rep != 1.0f) {
+    // the request's history row towards L2 for the finish (whole 16-byte blocks inside the row)
+    const int b = Q.pos / P.L;
+    const bool bits = P.history_kind == YAPD_HISTORY_BITMAP;
+    const uintptr_t h0 = reinterpret_cast<uintptr_t>(P.history) + (uintptr_t)((int64_t)b * P.history_stride * (bits ? 4 : 1));
+    const uintptr_t hb = h0 + (bits ? (uintptr_t)((P.V + 31) / 32) * 4u : (uintptr_t)P.V);
+    const uintptr_t s0 = (h0 + 15) & ~(uintptr_t)15, e0 = hb & ~(uintptr_t)15;
+    if (e0 > s0) prefetch_l2(reinterpret_cast<const void*>(s0), (uint32_t)(e0 - s0));
+  }
   const float kPosInf = __int_as_float(0x7f800000);
   const int leader = tm.team * tm.T;
-  WBand& B = ws.band[tm.T > 1 ? leader + parity : warp];
+  const int area = tm.T > 1 ? leader + parity : warp;
+  WBand& B = ws.band[area];
   WStash& st_ = ws.stash[warp];
   PosCtx X;
   float sA;
@@ -2503,8 +2642,44 @@ __device__ __forceinline__ bool w_position(const SampleParams& P, WSmem& ws, int
       const int y = __shfl_up_sync(0xffffffffu, incl, o);
       if (lane >= o) incl += y;
     }
+    const int tot = __shfl_sync(0xffffffffu, incl, 31);
+    if (nst + tot > WCfg::STASH && nst > 0) {
+      // the running maximum has risen: drop the entries now below it
+      const int ns = min(nst, WCfg::STASH);
+      uint4 ec[2], eu[2];
+      int ej[2];
+      float ez[2];
+      bool keep[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int i = lane + 32 * h;
+        keep[h] = i < ns && st_.z[i] >= thr;
+        if (keep[h]) {
+          ec[h] = st_.c[i];
+          eu[h] = st_.u[i];
+          ej[h] = st_.j[i];
+          ez[h] = st_.z[i];
+        }
+      }
+      const unsigned kb0 = __ballot_sync(0xffffffffu, keep[0]);
+      const unsigned kb1 = __ballot_sync(0xffffffffu, keep[1]);
+      __syncwarp();
+      const unsigned lt = (1u << lane) - 1u;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (keep[h]) {
+          const int d = h == 0 ? __popc(kb0 & lt) : __popc(kb0) + __popc(kb1 & lt);
+          st_.c[d] = ec[h];
+          st_.u[d] = eu[h];
+          st_.j[d] = ej[h];
+          st_.z[d] = ez[h];
+        }
+      }
+      __syncwarp();
+      nst = __popc(kb0) + __popc(kb1);  // entries past STASH stay in the overflow marks
+    }
     int at = nst + incl - cnt;
-    nst += __shfl_sync(0xffffffffu, incl, 31);
+    nst += tot;
     while (mk) {
       const int t = __ffs(mk) - 1;
       mk &= mk - 1u;
@@ -2513,6 +2688,7 @@ __device__ __forceinline__ bool w_position(const SampleParams& P, WSmem& ws, int
         st_.c[at] = lds128(slot + v * 16);
         st_.u[at] = CFG ? lds128(slot + WCfg::CHB + v * 16) : make_uint4(0u, 0u, 0u, 0u);
         st_.j[at] = I.S.j0 + q * WCfg::CHV + v;
+        st_.z[at] = __fadd_rn(vzl[t], rz);
       } else {
         ovf |= 1ull << ((q / tm.T) * WCfg::TPC + t);
       }
@@ -2643,10 +2819,118 @@ __device__ __forceinline__ bool w_position(const SampleParams& P, WSmem& ws, int
     const bool live = lane < n;
     band_finish_warp<C, CFG>(P, Q, X, K, n, live ? B.id[lane] : 0, live ? B.c[lane] : 0.f,
                              live ? B.u[lane] : 0.f);
+  } else if (last) {
+    // the team has no further item: the CTA resolves the band after the warp pass
+    if (lane == 0) {
+      WPend& pd = ws.pend[warp];
+      pd.area = area;
+      pd.Q = Q;
+      pd.X = X;
+      pd.K = K;
+      pd.n = n;
+    }
+    __syncwarp();
   } else {
     band_finish_wide<CFG>(P, Q, X, K, B, n);
   }
   return true;
+}
+
+// Scratch of cta_finish_wide, in the ring (free once the warp pass is over).
+struct WEpi {
+  unsigned long long key[WCfg::BANDW];
+  float pm[WCfg::BANDW];
+  float sc[WCfg::BANDW];
+  unsigned long long best[WCfg::NWARP];
+  float p0;
+  int win;
+};
+static_assert(sizeof(WEpi) <= sizeof(((WSmem*)nullptr)->ring), "the wide-band scratch fits the ring");
+static_assert(WCfg::NTHREADS >= 4 * WCfg::BANDW, "four threads per band member");
+
+// The band recorded in ws.pend[w], by every thread of the CTA: exact value,
+// mass and score per member (one thread each), rank by (exact value, id) and
+// the double sum of the masses ranked above (four threads per member), the
+// top-p / min-p flags and the best kept score (ties to the lower rank) -- the
+// arithmetic of band_finish_wide.
+template <bool CFG>
+__device__ __noinline__ void cta_finish_wide(const SampleParams& P, WSmem& ws, int w) {
+  const WPend& pd = ws.pend[w];
+  const int n = pd.n;
+  const WBand& B = ws.band[pd.area];
+  WEpi& E = *reinterpret_cast<WEpi*>(&ws.ring[0][0][0]);
+  const PosCtx X = pd.X;
+  const ScoreCtx K = pd.K;
+  const ItemParams Q = pd.Q;
+  const int lane = threadIdx.x & 31;
+  const int i = threadIdx.x >> 2, sub = threadIdx.x & 3;
+  const bool own = sub == 0 && i < n;
+  float cw = 0.f, uw = 0.f;
+  int id = 0;
+  if (own) {
+    id = B.id[i];
+    cw = B.c[i];
+    uw = B.u[i];
+    const ScoreIn si = score_in<true>(P, K, id);
+    const float vals = exact_val_cu(P, X, cw, uw);
+    E.key[i] = cand_key(vals, id);
+    E.pm[i] = __fmul_rn(ex2_approx(__fsub_rn(z2_of(X, cw, uw), X.zmax)), K.r);
+    float sc = score_from(K, vals, si);
+    if (!(sc == sc)) sc = kNegInf;
+    E.sc[i] = sc;
+  }
+  __syncthreads();
+  int rk = 0;
+  double ab = 0.0;
+  if (i < n) {
+    const unsigned long long ki = E.key[i];
+    for (int j = sub; j < n; j += 4) {
+      if (E.key[j] > ki) {
+        ++rk;
+        ab += (double)E.pm[j];
+      }
+    }
+  }
+  rk += __shfl_xor_sync(0xffffffffu, rk, 1);
+  rk += __shfl_xor_sync(0xffffffffu, rk, 2);
+  ab += __shfl_xor_sync(0xffffffffu, ab, 1);
+  ab += __shfl_xor_sync(0xffffffffu, ab, 2);
+  if (own && rk == 0) E.p0 = E.pm[i];
+  __syncthreads();
+  unsigned long long rec = 0ull;
+  if (own) {
+    const float p = E.pm[i];
+    const double incl = ab + (double)p;
+    bool keep = true;
+    if (Q.top_p < 1.0f) keep = __fsub_rn((float)incl, p) < Q.top_p;
+    keep = keep && (p >= __fmul_rn(Q.min_p, E.p0));
+    const float sc = E.sc[i];
+    const uint32_t ks = keep && sc > kNegInf ? ord_key(sc) : 0u;
+    rec = ks ? (((unsigned long long)ks << 32) | (uint32_t)(0x7fffffff - rk)) : 0ull;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long x = __shfl_xor_sync(0xffffffffu, rec, o);
+    rec = x > rec ? x : rec;
+  }
+  if (lane == 0) E.best[threadIdx.x >> 5] = rec;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long b = 0ull;
+    for (int q = 0; q < WCfg::NWARP; ++q) b = E.best[q] > b ? E.best[q] : b;
+    E.win = b ? 0x7fffffff - (int)(uint32_t)(b & 0xffffffffu) : 0;
+  }
+  __syncthreads();
+  if (own && rk == E.win) {
+    int chosen = id;
+    if (chosen < 0 || chosen >= P.V) {
+      atomicOr(P.status, (unsigned)YAPD_STATUS_INTERNAL);
+      chosen = 0;
+    }
+    P.sampled[Q.pos] = chosen;
+    if (P.pcu) P.pcu[Q.pos] = pmi_cu<CFG>(X, cw, uw);
+  }
+  __syncthreads();
 }
 
 // bf16 select step: preamble, the warp-per-position pass over this CTA's
@@ -2656,7 +2940,7 @@ __global__ void __launch_bounds__(WCfg::NTHREADS, 1) wsample_kernel(const __grid
   using C = CfgBF16;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   WSmem& ws = *reinterpret_cast<WSmem*>(smem_raw);
-  const int n_items = cta_prepare(P, ws.scan, ws.items, WCfg::ICAP);
+  const int n_items = cta_prepare(P, ws.scan, &ws.req, ws.items_pos, WCfg::ICAP);
   const int first = blockIdx.x, stride = gridDim.x;
   if (first >= n_items) return;
   const int n_my = (n_items - first + stride - 1) / stride;
@@ -2668,11 +2952,15 @@ __global__ void __launch_bounds__(WCfg::NTHREADS, 1) wsample_kernel(const __grid
   tm.T = WCfg::NWARP / tm.NTEAM;
   tm.team = warp / tm.T;
   tm.r = warp % tm.T;
+  // the records of the first IREC items, one thread each
+  for (int k = threadIdx.x; k < min(n_my, WCfg::IREC); k += blockDim.x)
+    ws.irec[k] = witem<CFG>(P, w_params(P, ws, k, first, stride));
   if (lane == 0) {
     for (int s = 0; s < WCfg::NSLOT; ++s) mbar_init(&ws.bar[warp][s], 1);
     fence_mbar_init();
+    ws.pend[warp].n = 0;
   }
-  __syncwarp();
+  __syncthreads();
   WCursor cur;
   cur.k = tm.team - tm.NTEAM;
   cur.q = cur.nch = cur.nvi = 0;
@@ -2686,14 +2974,19 @@ __global__ void __launch_bounds__(WCfg::NTHREADS, 1) wsample_kernel(const __grid
   int parity = 0;
   for (int k = tm.team; k < n_my; k += tm.NTEAM) {
     const int idx = first + k * stride;
-    if (lane == 0) ws.item[warp] = witem<CFG>(P, w_params(P, ws, k, first, stride));
-    __syncwarp();
+    const WItem* Ip = &ws.irec[k < WCfg::IREC ? k : 0];
+    if (k >= WCfg::IREC) {
+      if (lane == 0) ws.item[warp] = witem<CFG>(P, w_params(P, ws, k, first, stride));
+      __syncwarp();
+      Ip = &ws.item[warp];
+    }
     bool done = false;
-    if (ws.item[warp].ok) {
-      done = w_position<CFG>(P, ws, warp, tm, parity, n_my, first, stride, gcons, cur, ok_wait);
+    if (Ip->ok) {
+      done = w_position<CFG>(P, ws, *Ip, warp, tm, parity, k + tm.NTEAM >= n_my, n_my, first, stride, gcons,
+                             cur, ok_wait);
       parity ^= 1;
     }
-    if (!done && tm.r == 0 && lane == 0) P.work_w[idx] = ws.item[warp].Q.pos | kDeferBit;
+    if (!done && tm.r == 0 && lane == 0) P.work_w[idx] = Ip->Q.pos | kDeferBit;
     __syncwarp();
   }
   // copies issued but not consumed (only after an expired wait)
@@ -2705,6 +2998,9 @@ __global__ void __launch_bounds__(WCfg::NTHREADS, 1) wsample_kernel(const __grid
       asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_u32(&ws.bar[warp][s])) : "memory");
   }
   __syncthreads();
+  // wide bands left for the whole CTA (the ring is free now)
+  for (int w = 0; w < WCfg::NWARP; ++w)
+    if (ws.pend[w].n > 0) cta_finish_wide<CFG>(P, ws, w);
   // compact the deferred entries to the front of this CTA's work-list slots
   if (warp == 0) {
     int j = 0;
@@ -2733,6 +3029,7 @@ constexpr size_t smem_bytes() {
   return sizeof(KSmem<C>) + 128;
 }
 
+static_assert(sizeof(WSmem) + 128 <= 227 * 1024, "the warp kernel's shared memory fits one SM");
 constexpr size_t wsmem_bytes() {
   return (sizeof(WSmem) > sizeof(KSmem<CfgBF16>) ? sizeof(WSmem) : sizeof(KSmem<CfgBF16>)) + 128;
 }
@@ -2820,10 +3117,12 @@ static int fill_sampling(SampleParams& P, const yapd_sampling& s, const yapd_noi
 }
 
 template <class C, bool CFG>
-static void launch_one(const SampleParams& P, int occ, int sms, int max_items, cudaStream_t st) {
+static void launch_one(const SampleParams& P0, int occ, int sms, int max_items, cudaStream_t st) {
   int grid = sms * occ;
   if (grid > max_items) grid = max_items;
   if (grid < 1) grid = 1;
+  SampleParams P = P0;
+  P.div_grid = divu_make(grid);
   sample_kernel<C, CFG><<<grid, C::NTHREADS, smem_bytes<C>(), st>>>(P);
 }
 
@@ -2836,8 +3135,10 @@ static int launch_sample(const SampleParams& P, int dtype, int max_items, cudaSt
   const int occ = d->occ[bf ? 1 : 0][cfg ? 1 : 0];
   if (bf && P.fused) {
     // select step: warp-per-position kernel, one CTA per SM
-    if (cfg) wsample_kernel<true><<<d->sms, WCfg::NTHREADS, wsmem_bytes(), st>>>(P);
-    else wsample_kernel<false><<<d->sms, WCfg::NTHREADS, wsmem_bytes(), st>>>(P);
+    SampleParams Pw = P;
+    Pw.div_grid = divu_make(d->sms);
+    if (cfg) wsample_kernel<true><<<d->sms, WCfg::NTHREADS, wsmem_bytes(), st>>>(Pw);
+    else wsample_kernel<false><<<d->sms, WCfg::NTHREADS, wsmem_bytes(), st>>>(Pw);
   } else if (bf) {
     if (cfg) launch_one<CfgBF16, true>(P, occ, d->sms, max_items, st);
     else launch_one<CfgBF16, false>(P, occ, d->sms, max_items, st);
@@ -2931,6 +3232,7 @@ int yapd_select_step(const yapd_select_args* a, void* stream) {
   P.B = a->B;
   P.nb = a->nb;
   P.L = a->L;
+  P.div_L = divu_make(a->L);
   P.V = a->V;
   int rc = fill_sampling(P, a->sampling, a->noise);
   if (rc != YAPD_OK) return rc;
@@ -3016,6 +3318,7 @@ int yapd_sample_rows(const yapd_sample_args* a, void* stream) {
   P.B = a->R;
   P.nb = 1;
   P.L = 1;
+  P.div_L = divu_make(1);
   P.V = a->V;
   int rc = fill_sampling(P, a->sampling, a->noise);
   if (rc != YAPD_OK) return rc;

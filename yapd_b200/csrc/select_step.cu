@@ -2178,6 +2178,7 @@ struct WPend {
 struct WSmem {
   int scan[32];
   int ndef;
+  int nflag;  // items this CTA marked deferred
   WPend pend[WCfg::NWARP];
   uint64_t bar[WCfg::NWARP][WCfg::NSLOT];
   float wstat[WCfg::NWARP][2][6];  // per-warp (m, s) of the statistics, by item parity
@@ -2815,7 +2816,21 @@ __device__ __forceinline__ bool w_position(const SampleParams& P, WSmem& ws, con
   if (tm.r != 0) return true;  // the team's first warp resolves the band
   const int n = B.n;
   if (n <= 0 || n > WCfg::BANDW) return false;
-  if (n <= 32) {
+  if (n == 1) {
+    // a one-member band: min-p keeps it (p >= min_p * p), so does top-p
+    // (nothing above it), and an argmax over one kept member (or over none,
+    // when its score is not a number) picks it
+    if (lane == 0) {
+      int chosen = B.id[0];
+      if (chosen < 0 || chosen >= P.V) {
+        atomicOr(P.status, (unsigned)YAPD_STATUS_INTERNAL);
+        chosen = 0;
+      }
+      P.sampled[Q.pos] = chosen;
+      if (P.pcu) P.pcu[Q.pos] = pmi_cu<CFG>(X, B.c[0], B.u[0]);
+    }
+    __syncwarp();
+  } else if (n <= 32) {
     const bool live = lane < n;
     band_finish_warp<C, CFG>(P, Q, X, K, n, live ? B.id[lane] : 0, live ? B.c[lane] : 0.f,
                              live ? B.u[lane] : 0.f);
@@ -2960,6 +2975,7 @@ __global__ void __launch_bounds__(WCfg::NTHREADS, 1) wsample_kernel(const __grid
     fence_mbar_init();
     ws.pend[warp].n = 0;
   }
+  if (threadIdx.x == 0) ws.nflag = 0;
   __syncthreads();
   WCursor cur;
   cur.k = tm.team - tm.NTEAM;
@@ -2986,7 +3002,10 @@ __global__ void __launch_bounds__(WCfg::NTHREADS, 1) wsample_kernel(const __grid
                              cur, ok_wait);
       parity ^= 1;
     }
-    if (!done && tm.r == 0 && lane == 0) P.work_w[idx] = Ip->Q.pos | kDeferBit;
+    if (!done && tm.r == 0 && lane == 0) {
+      P.work_w[idx] = Ip->Q.pos | kDeferBit;
+      atomicAdd(&ws.nflag, 1);
+    }
     __syncwarp();
   }
   // copies issued but not consumed (only after an expired wait)
@@ -3001,6 +3020,7 @@ __global__ void __launch_bounds__(WCfg::NTHREADS, 1) wsample_kernel(const __grid
   // wide bands left for the whole CTA (the ring is free now)
   for (int w = 0; w < WCfg::NWARP; ++w)
     if (ws.pend[w].n > 0) cta_finish_wide<CFG>(P, ws, w);
+  if (ws.nflag == 0) return;  // nothing deferred: no grouped pass
   // compact the deferred entries to the front of this CTA's work-list slots
   if (warp == 0) {
     int j = 0;
@@ -3150,6 +3170,7 @@ static int launch_sample(const SampleParams& P, int dtype, int max_items, cudaSt
 }
 
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
 
 }  // namespace yapd
 

@@ -2561,68 +2561,78 @@ __device__ __forceinline__ bool w_position(const SampleParams& P, WSmem& ws, con
     ++gcons;
     const int nv = min(WCfg::CHV, I.nvi - q * WCfg::CHV);
     const unsigned char* slot = ws.ring[warp][s];
-    float vzl[WCfg::TPC];
-#pragma unroll
-    for (int t = 0; t < WCfg::TPC; ++t) {
-      const int v = lane + 32 * t;
-      vzl[t] = kNegInf;
-      if (v < nv) {
-        const uint4 a = lds128(slot + v * 16);
+    if (first_vec) {
+      // references: the maxima of this lane's first vector
+      first_vec = false;
+      if (lane < nv) {
+        const uint4 a = lds128(slot + lane * 16);
         uint4 b = a;
-        if (CFG) b = lds128(slot + WCfg::CHB + v * 16);
+        if (CFG) b = lds128(slot + WCfg::CHB + lane * 16);
         const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
         const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
         const uint32_t ac = bmax2(bmax2(a.x, a.y), bmax2(a.z, a.w));
-        cm2 = bmax2(cm2, ac);
-        uint32_t au = 0u;
+        rc = __fmul_rn(finite_or0(fmaxf(bf16lo(ac), bf16hi(ac))), kLog2e);
         if (CFG) {
-          au = bmax2(bmax2(b.x, b.y), bmax2(b.z, b.w));
-          um2 = bmax2(um2, au);
+          const uint32_t au = bmax2(bmax2(b.x, b.y), bmax2(b.z, b.w));
+          ru = __fmul_rn(finite_or0(fmaxf(bf16lo(au), bf16hi(au))), kLog2e);
         }
-        if (t == 0 && first_vec) {
-          // references: this lane's first vector's maxima
-          rc = __fmul_rn(finite_or0(fmaxf(bf16lo(ac), bf16hi(ac))), kLog2e);
-          ru = CFG ? __fmul_rn(finite_or0(fmaxf(bf16lo(au), bf16hi(au))), kLog2e) : 0.f;
-          float zm = kNegInf;
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const unsigned long long cx = f2_bf16(aw[k]);
-            const unsigned long long zx =
-                CFG ? f2_fma(cx, A2p, f2_fma(f2_bf16(bw[k]), nB2p, zero)) : f2_fma(cx, A2p, zero);
-            float lo, hi;
-            f2_unpack(zx, lo, hi);
-            zm = fmax3(zm, lo, hi);
-          }
-          rz = finite_or0(zm);
-          nrcp = f2_pack(-rc, -rc);
-          nrup = f2_pack(-ru, -ru);
-          nrzp = f2_pack(-rz, -rz);
-        }
-        float m = kNegInf;
+        float zm = kNegInf;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const unsigned long long cx = f2_bf16(aw[k]);
-          unsigned long long dx;
+          const unsigned long long zx =
+              CFG ? f2_fma(cx, A2p, f2_fma(f2_bf16(bw[k]), nB2p, zero)) : f2_fma(cx, A2p, zero);
           float lo, hi;
-          if (CFG) {
-            const unsigned long long ux = f2_bf16(bw[k]);
-            dx = f2_fma(cx, A2p, f2_fma(ux, nB2p, nrzp));
-            f2_unpack(f2_fma(ux, L2p, nrup), lo, hi);
-            sup = f2_add(sup, f2_pack(ex2_approx(lo), ex2_approx(hi)));
-          } else {
-            dx = f2_fma(cx, A2p, nrzp);
-          }
-          f2_unpack(f2_fma(cx, L2p, nrcp), lo, hi);
-          scp = f2_add(scp, f2_pack(ex2_approx(lo), ex2_approx(hi)));
-          f2_unpack(dx, lo, hi);
-          sp = f2_add(sp, f2_pack(ex2_approx(lo), ex2_approx(hi)));
-          m = fmax3(m, lo, hi);
+          f2_unpack(zx, lo, hi);
+          zm = fmax3(zm, lo, hi);
         }
-        vzl[t] = m;
-        dm = fmaxf(dm, m);
+        rz = finite_or0(zm);
       }
+      nrcp = f2_pack(-rc, -rc);
+      nrup = f2_pack(-ru, -ru);
+      nrzp = f2_pack(-rz, -rz);
     }
-    first_vec = false;
+    // one 16-byte vector pair: maxima, the three sums, the vector's largest z2'
+    auto vec = [&](int v) -> float {
+      const uint4 a = lds128(slot + v * 16);
+      uint4 b = a;
+      if (CFG) b = lds128(slot + WCfg::CHB + v * 16);
+      const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+      const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+      cm2 = bmax2(cm2, bmax2(bmax2(a.x, a.y), bmax2(a.z, a.w)));
+      if (CFG) um2 = bmax2(um2, bmax2(bmax2(b.x, b.y), bmax2(b.z, b.w)));
+      float m = kNegInf;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const unsigned long long cx = f2_bf16(aw[k]);
+        unsigned long long dx;
+        float lo, hi;
+        if (CFG) {
+          const unsigned long long ux = f2_bf16(bw[k]);
+          dx = f2_fma(cx, A2p, f2_fma(ux, nB2p, nrzp));
+          f2_unpack(f2_fma(ux, L2p, nrup), lo, hi);
+          sup = f2_add(sup, f2_pack(ex2_approx(lo), ex2_approx(hi)));
+        } else {
+          dx = f2_fma(cx, A2p, nrzp);
+        }
+        f2_unpack(f2_fma(cx, L2p, nrcp), lo, hi);
+        scp = f2_add(scp, f2_pack(ex2_approx(lo), ex2_approx(hi)));
+        f2_unpack(dx, lo, hi);
+        sp = f2_add(sp, f2_pack(ex2_approx(lo), ex2_approx(hi)));
+        m = fmax3(m, lo, hi);
+      }
+      dm = fmaxf(dm, m);
+      return m;
+    };
+    float vzl[WCfg::TPC];
+    if (nv == WCfg::CHV) {
+      // a full chunk: straight-line code over the lane's four vectors
+#pragma unroll
+      for (int t = 0; t < WCfg::TPC; ++t) vzl[t] = vec(lane + 32 * t);
+    } else {
+#pragma unroll
+      for (int t = 0; t < WCfg::TPC; ++t) vzl[t] = lane + 32 * t < nv ? vec(lane + 32 * t) : kNegInf;
+    }
     // marks: vectors whose largest z2' reaches the running maximum + log2(min_p)
     float cmx = vzl[0];
 #pragma unroll
@@ -3098,6 +3108,11 @@ static int device_info(DevInfo** out) {
     if (rc == YAPD_OK) rc = prepare_kernel<CfgF32, false>(&d.occ[0][0]);
     if (rc == YAPD_OK) rc = prepare_wkernel<true>();
     if (rc == YAPD_OK) rc = prepare_wkernel<false>();
+    // the state update runs between two sample kernels: the same shared-memory
+    // carveout spares the SMs a reconfiguration at each boundary
+    if (rc == YAPD_OK && cudaFuncSetAttribute(unmask_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                              (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess)
+      rc = YAPD_ERR_LAUNCH;
     if (rc != YAPD_OK) return rc;
     d.init = true;
   }

@@ -406,7 +406,7 @@ def run_ours(args, ws, rank, local):
             },
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
-                         "kernel": "sample_kernel", "kernel_ms_per_launch": sum(kern_ms) / K,
+                         "kernel": "wsample_kernel", "kernel_ms_per_launch": sum(kern_ms) / K,
                          "bytes_per_launch": sum(byt) / K},
             "e2e": {"value": e2e_rows / (e2e_ms * 1e-3), "unit": "rows/s",
                     "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"]},

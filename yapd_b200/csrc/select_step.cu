@@ -313,31 +313,37 @@ __device__ __forceinline__ uint32_t rank_key(float f) {
   return (f != f) ? 0xffffffffu : ord_key(f);
 }
 
-// Whether position p is sampled this step (masked in a denoising request).
-__device__ __forceinline__ bool pos_active(const UnmaskParams& U, int dense, int p) {
-  return dense || (U.is_commit[p / U.L] == 0 && U.xt[p] == U.mask_id);
-}
-
 // Block-state update of request b by one warp: server/engine.py:559-612.
-// Only positions sampled this step (pos_active) read `sampled` and `pcu`.
+// Only the positions sampled this step (every position in dense mode, else
+// the masked positions of a denoising request) use `sampled` and `pcu`.
 __device__ __forceinline__ void unmask_request(const UnmaskParams& U, int dense, int b) {
   const int lane = threadIdx.x & 31;
   const int L = U.L, K = U.K;
   const bool in = lane < L;
   const int p = b * L + lane;
-  const int64_t x = in ? U.xt[p] : 0;
-  const bool is_mask = in && x == U.mask_id;
-  const bool commit = U.is_commit[b] != 0;
-  const bool denoise = !commit;
+  // every load that does not depend on another goes out first (lanes past L
+  // read the request's first position and ignore it)
+  const int pc = in ? p : b * L;
+  const int64_t xr = U.xt[pc];
+  const uint8_t cm = U.is_commit[b];
   const int64_t ks = U.k_step[b];
+  const int sraw = U.sampled[pc];   // -1 where not sampled this step
+  const float2 pr = U.pcu[pc];      // read only where sampled
+  const int64_t x = in ? xr : 0;
+  const bool is_mask = in && x == U.mask_id;
+  const bool commit = cm != 0;
+  const bool denoise = !commit;
   int kc = (int)(ks < (int64_t)(K - 1) ? ks : (int64_t)(K - 1));
   if (kc < 0) kc = 0;
   // PMI of the sampled token (server/engine.py:553-558, calibration.py:58-60)
   // and the position noise on masked positions (server/engine.py:559-561)
+  float gn = 0.f;
+  if (is_mask && U.pos_noise)
+    gn = (U.noise_kind == YAPD_NOISE_EXPLICIT) ? U.gumbel_pos[p]
+                                                : philox_position_gumbel(U.seed, U.offset, (uint32_t)p);
   float pm = 0.f;
-  const int smp = (in && pos_active(U, dense, p)) ? U.sampled[p] : -1;
+  const int smp = (in && (dense || (!commit && x == U.mask_id))) ? sraw : -1;
   if (smp >= 0) {
-    const float2 pr = U.pcu[p];
     const float lpl = __fmul_rn(U.pmi_lambda, __ldg(U.log_prior + smp));
     pm = __fsub_rn(logf(fmaxf(pr.x, 1e-8f)), lpl);
     if (U.nb == 2) {
@@ -345,14 +351,7 @@ __device__ __forceinline__ void unmask_request(const UnmaskParams& U, int dense,
       pm = __fsub_rn(__fmul_rn(U.cfg_1pw, pm), __fmul_rn(U.cfg_w, pmi_u));
     }
   }
-  if (is_mask) {
-    if (U.pos_noise) {
-      const float gn = (U.noise_kind == YAPD_NOISE_EXPLICIT)
-                           ? U.gumbel_pos[p]
-                           : philox_position_gumbel(U.seed, U.offset, (uint32_t)p);
-      pm = __fadd_rn(pm, gn);
-    }
-  }
+  if (is_mask && U.pos_noise) pm = __fadd_rn(pm, gn);
   const unsigned mbal = __ballot_sync(0xffffffffu, is_mask);
   const int m = __popc(mbal);
   // ascending sort of masked PMI (+inf elsewhere), engine.py:566
@@ -508,25 +507,34 @@ __device__ int cta_prepare(const SampleParams& P, int* scan, ReqTable* rt = null
     base += q < w ? c : 0;
     tot += c;
   }
-  const unsigned lt = (1u << lane) - 1u;
+  // this CTA's entries: global indices me + k*grid (the k-th item) and, for
+  // the output initialisation, positions me + j*grid; both stride by grid,
+  // so each round of 32 meets few of them (warp-uniform loops)
+  int nxt = base <= me ? me : me + divu(base - me + grid - 1, P.div_grid) * grid;
+  int np = w0 <= me ? me : me + divu(w0 - me + grid - 1, P.div_grid) * grid;
   for (int c0 = w0; c0 < w1; c0 += kR * 32) {
     if (!one_chunk) chunk(c0, masks, false);
 #pragma unroll
     for (int r = 0; r < kR; ++r) {
-      const int p = c0 + r * 32 + lane;
-      const bool a = (masks[r] >> lane) & 1u;
-      const int idx = base + __popc(masks[r] & lt);
-      const int qi = divu(idx, P.div_grid);
-      if (a && idx - qi * grid == me) {
-        P.work_w[idx] = p;
-        // the CTA's item qi
-        if (qi < cap) items_pos[qi] = p;
+      const int p0 = c0 + r * 32;
+      const int cr = __popc(masks[r]);
+      while (nxt < base + cr) {
+        const int ln = (int)__fns(masks[r], 0u, nxt - base + 1);
+        if (lane == ln) {
+          P.work_w[nxt] = p0 + lane;
+          const int qi = divu(nxt - me, P.div_grid);
+          if (qi < cap) items_pos[qi] = p0 + lane;
+        }
+        nxt += grid;
       }
-      if (!a && p < w1 && p - divu(p, P.div_grid) * grid == me) {
-        P.sampled[p] = -1;
-        U.pmi[p] = __int_as_float(0x7fc00000);
+      while (np < min(p0 + 32, w1)) {
+        if (lane == np - p0 && !((masks[r] >> lane) & 1u)) {
+          P.sampled[np] = -1;
+          U.pmi[np] = __int_as_float(0x7fc00000);
+        }
+        np += grid;
       }
-      base += __popc(masks[r]);
+      base += cr;
     }
   }
   __syncthreads();
@@ -2255,7 +2263,7 @@ struct WCursor {
 // Issue the warp's next chunk into its slot; false at the end of the stream.
 template <bool CFG>
 __device__ __forceinline__ bool w_issue(const SampleParams& P, WSmem& ws, int warp, const WTeam& tm, int n_my,
-                                        int first, int stride, WCursor& c) {
+                                        int first, int stride, WCursor& c, bool direct = false) {
   while (c.q >= c.nch) {
     c.k += tm.NTEAM;
     if (c.k >= n_my) {
@@ -2263,7 +2271,8 @@ __device__ __forceinline__ bool w_issue(const SampleParams& P, WSmem& ws, int wa
       c.q = c.nch = 0;
       return false;
     }
-    const WItem I = w_item<CFG>(P, ws, c.k, first, stride);
+    // (`direct`: before the item records exist)
+    const WItem I = direct ? witem<CFG>(P, w_params(P, ws, c.k, first, stride)) : w_item<CFG>(P, ws, c.k, first, stride);
     c.q = tm.r;
     c.nch = I.ok ? I.nch : 0;
     c.nvi = I.nvi;
@@ -2977,24 +2986,24 @@ __global__ void __launch_bounds__(WCfg::NTHREADS, 1) wsample_kernel(const __grid
   tm.T = WCfg::NWARP / tm.NTEAM;
   tm.team = warp / tm.T;
   tm.r = warp % tm.T;
-  // the records of the first IREC items, one thread each
-  for (int k = threadIdx.x; k < min(n_my, WCfg::IREC); k += blockDim.x)
-    ws.irec[k] = witem<CFG>(P, w_params(P, ws, k, first, stride));
-  if (lane == 0) {
-    for (int s = 0; s < WCfg::NSLOT; ++s) mbar_init(&ws.bar[warp][s], 1);
-    fence_mbar_init();
-    ws.pend[warp].n = 0;
-  }
-  if (threadIdx.x == 0) ws.nflag = 0;
-  __syncthreads();
+  // first copies of each warp (lane 0, its own barriers), then the records of
+  // the first IREC items, one thread each
   WCursor cur;
   cur.k = tm.team - tm.NTEAM;
   cur.q = cur.nch = cur.nvi = 0;
   cur.c = cur.u = nullptr;
   cur.gi = 0;
-  if (lane == 0)
+  if (lane == 0) {
+    for (int s = 0; s < WCfg::NSLOT; ++s) mbar_init(&ws.bar[warp][s], 1);
+    fence_mbar_init();
+    ws.pend[warp].n = 0;
     for (int s = 0; s < WCfg::NSLOT; ++s)
-      if (!w_issue<CFG>(P, ws, warp, tm, n_my, first, stride, cur)) break;
+      if (!w_issue<CFG>(P, ws, warp, tm, n_my, first, stride, cur, true)) break;
+  }
+  for (int k = threadIdx.x; k < min(n_my, WCfg::IREC); k += blockDim.x)
+    ws.irec[k] = witem<CFG>(P, w_params(P, ws, k, first, stride));
+  if (threadIdx.x == 0) ws.nflag = 0;
+  __syncthreads();
   uint32_t gcons = 0;
   bool ok_wait = true;
   int parity = 0;

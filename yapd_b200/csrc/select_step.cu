@@ -225,6 +225,7 @@ template <class C>
 struct Smem;
 template <class C>
 struct KSmem;
+constexpr int kHistBins = 512;  // bins of the histogram bracket
 
 template <class C>
 __device__ __forceinline__ float load_elem_global(const char* row, int v) {
@@ -879,41 +880,106 @@ __device__ __forceinline__ int block_pick(const Pick& bp, bool turbo, Smem<C>& s
   return 0x7fffffff - (int)(uint32_t)w2;
 }
 
-// Cold argmax from the staged rows (rolled loop): elements with z2 >= H are
-// kept (min-p test included); elements with band_lo <= z2 < H are kept iff
-// their composite (exact value, -id) key is >= Xcomp.
+// Gumbel noise of tokens v4 .. v4+3 (v4 a multiple of 4): one Philox block,
+// whose four words are the four tokens' words, or the explicit tensor.
+__device__ __forceinline__ void noise4(const SampleParams& P, const ScoreCtx& K, int v4, float (&g)[4]) {
+  if (P.noise_kind == YAPD_NOISE_EXPLICIT) {
+    const float* row = P.gumbel_tok + (int64_t)K.b * P.gt_stride_req + (int64_t)K.l * P.gt_stride_pos;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) g[i] = v4 + i < P.V ? __ldg(row + v4 + i) : 0.f;
+    return;
+  }
+  const Philox4 r = philox4x32_10((uint32_t)v4 >> 2, (uint32_t)K.pos, (uint32_t)P.offset,
+                                  (uint32_t)(P.offset >> 32) & 0x7fffffffu, (uint32_t)P.seed,
+                                  (uint32_t)(P.seed >> 32));
+  g[0] = gumbel_from_uniform(uniform_from_word(r.x));
+  g[1] = gumbel_from_uniform(uniform_from_word(r.y));
+  g[2] = gumbel_from_uniform(uniform_from_word(r.z));
+  g[3] = gumbel_from_uniform(uniform_from_word(r.w));
+}
+
+// History bits of tokens v4 .. v4+3 (bit i: token v4 + i).
+__device__ __forceinline__ unsigned hist4(const SampleParams& P, int b, int v4) {
+  if (P.history_kind == YAPD_HISTORY_BITMAP) {
+    const uint32_t* h = reinterpret_cast<const uint32_t*>(P.history) + (int64_t)b * P.history_stride;
+    return (__ldg(h + (v4 >> 5)) >> (v4 & 31)) & 15u;
+  }
+  const uint8_t* h = reinterpret_cast<const uint8_t*>(P.history) + (int64_t)b * P.history_stride;
+  unsigned m = 0u;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) m |= (v4 + i < P.V && __ldg(h + v4 + i) != 0) ? (1u << i) : 0u;
+  return m;
+}
+
+// Cold argmax from the staged rows: elements with z2 >= H are kept (min-p
+// test included); elements with band_lo <= z2 < H are kept iff their
+// composite (exact value, -id) key is >= Xcomp.  Pass 1 runs over groups of
+// four tokens per thread (one Philox block and one history word each) with
+// approximate values and exact noise, keeping the tokens within a margin of
+// the thread's best; pass 2 rescores those exactly (or every token, when a
+// thread's list overflowed) and scans the boundary band.
 template <class C>
 __device__ __noinline__ int argmax_smem(const SampleParams& P, const PosCtx X, const RowRef<C> R, float H,
                                         float band_lo, unsigned long long Xcomp, const ScoreCtx& K, Pick bp, Smem<C>& sm) {
   csync<C>();  // out-of-line reductions use scratch slots 2/3
   int slot = 2;
   const int V = P.V;
+  constexpr int NC = 4;
   float best = kNegInf;
-  for (int v = gtid<C>(); v < V; v += C::NT) {
-    const float z = z2_smem<C>(X, R, v);
-    if (!(z >= H)) continue;
-    if (K.minp_on && !(__fmul_rn(ex2_approx(__fsub_rn(z, X.zmax)), K.r) >= K.minp_thr)) continue;
-    best = fmaxf(best, approx_score<C>(P, X, K, v, z));
+  int cv[NC];
+  int nc = 0;
+  bool ovf = false;
+  for (int v4 = 4 * gtid<C>(); v4 < V; v4 += 4 * C::NT) {
+    float g[4] = {0.f, 0.f, 0.f, 0.f};
+    if (K.noisy) noise4(P, K, v4, g);
+    const unsigned hb = K.pen_on ? hist4(P, K.b, v4) : 0u;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int v = v4 + i;
+      if (v >= V) break;
+      const float z = z2_smem<C>(X, R, v);
+      if (!(z >= H)) continue;
+      if (K.minp_on && !(__fmul_rn(ex2_approx(__fsub_rn(z, X.zmax)), K.r) >= K.minp_thr)) continue;
+      float va = __fmaf_rn(z, kLn2, X.Kval);
+      if ((hb >> i) & 1u) va = va > 0.f ? __fmul_rn(va, K.rrep) : __fmul_rn(va, K.rep);
+      const float sc = K.noisy ? __fadd_rn(va, g[i]) : va;
+      // (the bound x - margin(x) rises with x: a token within the final
+      // margin was within the margin of the running best when it came)
+      if (!(sc >= best - score_margin(best))) continue;
+      best = fmaxf(best, sc);
+      if (nc < NC) cv[nc++] = v;
+      else ovf = true;
+    }
   }
   const float gbest = red_max1<C>(best, sm, slot);
   const float thr = gbest > kNegInf ? gbest - score_margin(gbest) : kBig;
-  for (int v = gtid<C>(); v < V; v += C::NT) {
-    const float z = z2_smem<C>(X, R, v);
-    const bool in_main = z >= H;
-    const bool in_band = z >= band_lo && z < H;
-    if (!in_main && !in_band) continue;
-    if (K.minp_on && !(__fmul_rn(ex2_approx(__fsub_rn(z, X.zmax)), K.r) >= K.minp_thr)) continue;
+  const bool all = csync_or<C>(ovf);
+  auto rescore = [&](int v, float z) {
     float vals;
+    const bool in_main = z >= H;
     if (in_main) {
-      if (!(approx_score<C>(P, X, K, v, z) >= thr)) continue;
+      if (!(approx_score<C>(P, X, K, v, z) >= thr)) return;
       vals = exact_val<C>(P, X, R, v);
     } else {
       vals = exact_val<C>(P, X, R, v);
-      if (cand_key(vals, v) < Xcomp) continue;
+      if (cand_key(vals, v) < Xcomp) return;
     }
     const float es = exact_score<C>(P, K, v, vals);
     const Pick cand{es, vals, v};
     if (es == es && es > kNegInf && pick_better(cand, bp, K.turbo)) bp = cand;
+  };
+  if (!all) {
+    for (int q = 0; q < nc; ++q) rescore(cv[q], z2_smem<C>(X, R, cv[q]));
+  }
+  if (all || band_lo < H) {
+    for (int v = gtid<C>(); v < V; v += C::NT) {
+      const float z = z2_smem<C>(X, R, v);
+      const bool in_main = z >= H;
+      const bool in_band = z >= band_lo && z < H;
+      if (!(in_band || (all && in_main))) continue;
+      if (K.minp_on && !(__fmul_rn(ex2_approx(__fsub_rn(z, X.zmax)), K.r) >= K.minp_thr)) continue;
+      rescore(v, z);
+    }
   }
   return block_pick<C>(bp, K.turbo, sm, slot);
 }
@@ -1224,6 +1290,113 @@ __device__ __noinline__ int top1_smem(const SampleParams& P, const PosCtx X, con
 }
 
 // Top-k / top-p (and min-p) selection from the staged rows.
+// Histogram bracket: the same contract as bracket_smem (lo, hi around the
+// point where the count (or mass) of {z2 >= t} crosses the target), from
+// passes that bin z2 into kHistBins equal bins below zmax + 1 (counts and
+// masses by shared-memory atomics) and refine inside the crossing bins; false
+// when the target lies below the binned range (the caller then probes).
+template <class C>
+__device__ __noinline__ bool bracket_hist(const PosCtx X, const RowRef<C> R, int V, bool by_mass, float tgt_lo,
+                                          float tgt_hi, float floor_t, float& lo, float& hi, Smem<C>& sm) {
+  constexpr int NB = kHistBins, PER = NB / 32;
+  constexpr int kTarget = C::BAND / 2;
+  const int tid = gtid<C>(), lane = threadIdx.x & 31;
+  float top = __fadd_rn(X.zmax, 1.0f);
+  float base = fmaxf(floor_t, __fsub_rn(X.zmax, 63.0f));
+  float above_c = 0.f, above_m = 0.f;  // count / mass of {z2 >= top}
+  bool ok = false;
+  for (int pass = 0; pass < 3; ++pass) {
+    if (!(top > base)) break;
+    const float w = __fdiv_rn(__fsub_rn(top, base), (float)NB);
+    const float iw = __fdiv_rn(1.0f, w);
+    for (int i = tid; i < NB; i += C::NT) {
+      sm.hc[i] = 0;
+      sm.hm[i] = 0.f;
+    }
+    csync<C>();
+    for (int v = tid; v < V; v += C::NT) {
+      const float z = z2_smem<C>(X, R, v);
+      if (z >= base && z < top) {
+        const int bi = min(max((int)__fmul_rn(__fsub_rn(z, base), iw), 0), NB - 1);
+        atomicAdd(&sm.hc[bi], 1);
+        if (by_mass) atomicAdd(&sm.hm[bi], ex2_approx(__fsub_rn(z, X.zmax)));
+      }
+    }
+    csync<C>();
+    // lane s of the group's first warp scans bins NB-1-s*PER downwards; the
+    // running totals G(j) = F(base + j*w) grow towards lower bins
+    if (tid < 32) {
+      float segc = 0.f, segm = 0.f;
+#pragma unroll
+      for (int k = 0; k < PER; ++k) {
+        const int bi = NB - 1 - (lane * PER + k);
+        segc += (float)sm.hc[bi];
+        segm += sm.hm[bi];
+      }
+      float pc = segc, pm = segm;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float yc = __shfl_up_sync(0xffffffffu, pc, o);
+        const float ym = __shfl_up_sync(0xffffffffu, pm, o);
+        if (lane >= o) {
+          pc += yc;
+          pm += ym;
+        }
+      }
+      float gc = above_c + pc - segc, gm = above_m + pm - segm;  // G at the top of this segment
+      int jlo = -1, jx = -1;
+      float gclo = 0.f, gcx = 0.f, gmx = 0.f;
+#pragma unroll
+      for (int k = 0; k < PER; ++k) {
+        const int bi = NB - 1 - (lane * PER + k);
+        const float gc0 = gc, gm0 = gm;  // G(bi + 1)
+        gc += (float)sm.hc[bi];
+        gm += sm.hm[bi];
+        const float F = by_mass ? gm : gc;
+        if (jx < 0 && F >= tgt_lo) {
+          jx = bi;
+          gcx = gc0;
+          gmx = gm0;
+        }
+        if (jlo < 0 && F >= tgt_hi) {
+          jlo = bi;
+          gclo = gc;
+        }
+      }
+      // the first lane (highest bins) holding each crossing
+      const unsigned blo = __ballot_sync(0xffffffffu, jlo >= 0), bx = __ballot_sync(0xffffffffu, jx >= 0);
+      if (lane == 0) sm.misc[4] = blo ? 1 : 0;
+      if (blo) {
+        const int sl = __ffs(blo) - 1, sx = __ffs(bx) - 1;
+        const int jl = __shfl_sync(0xffffffffu, jlo, sl);
+        const float cl = __shfl_sync(0xffffffffu, gclo, sl);
+        const int jh = __shfl_sync(0xffffffffu, jx, sx) + 1;
+        const float ch = __shfl_sync(0xffffffffu, gcx, sx), mh = __shfl_sync(0xffffffffu, gmx, sx);
+        if (lane == 0) {
+          sm.red8[0] = __fadd_rn(base, __fmul_rn((float)jl, w));
+          sm.red8[1] = jh >= NB ? top : __fadd_rn(base, __fmul_rn((float)jh, w));
+          sm.red8[2] = __fsub_rn(cl, ch);
+          sm.red8[3] = ch;
+          sm.red8[4] = mh;
+        }
+      }
+    }
+    csync<C>();
+    if (!sm.misc[4]) break;  // the target lies below the binned range
+    ok = true;
+    lo = sm.red8[0];
+    hi = sm.red8[1];
+    const float between = sm.red8[2];
+    above_c = sm.red8[3];
+    above_m = sm.red8[4];
+    csync<C>();  // every read of the record precedes the next pass's writes
+    if (between <= (float)kTarget || hi - lo <= 8.f * zmargin(hi)) break;
+    base = lo;
+    top = hi;
+  }
+  return ok;
+}
+
 template <class C>
 __device__ __noinline__ int select_cold(const SampleParams& P, const PosCtx X, const RowRef<C> R, ScoreCtx K,
                                         int topk_raw, bool topk_on, bool topp_on, float top_p, float min_p, Smem<C>& sm) {
@@ -1241,7 +1414,8 @@ __device__ __noinline__ int select_cold(const SampleParams& P, const PosCtx X, c
   bool done = false;
   if (topk_on) {
     float lo, hi;
-    bracket_smem<C>(X, R, V, false, (float)topk_raw, (float)topk_raw, -kBig, (float)V, lo, hi, sm);
+    if (!bracket_hist<C>(X, R, V, false, (float)topk_raw, (float)topk_raw, -kBig, lo, hi, sm))
+      bracket_smem<C>(X, R, V, false, (float)topk_raw, (float)topk_raw, -kBig, (float)V, lo, hi, sm);
     csync<C>();
     const float blo = __fsub_rn(lo, zmargin(lo)), bhi = __fadd_rn(hi, zmargin(hi));
     bk = band_smem<C>(P, X, R, blo, bhi, sm);
@@ -1274,7 +1448,8 @@ __device__ __noinline__ int select_cold(const SampleParams& P, const PosCtx X, c
     const float tgt = __fmul_rn(top_p, Sn);
     if (topp_on && !(topk_on && bk.m_above < __fmul_rn(tgt, 1.00001f))) {
       float lo, hi;
-      bracket_smem<C>(X, R, V, true, __fmul_rn(tgt, 0.99999f), __fmul_rn(tgt, 1.00001f), Hk, cnt_k, lo, hi, sm);
+      if (!bracket_hist<C>(X, R, V, true, __fmul_rn(tgt, 0.99999f), __fmul_rn(tgt, 1.00001f), Hk, lo, hi, sm))
+        bracket_smem<C>(X, R, V, true, __fmul_rn(tgt, 0.99999f), __fmul_rn(tgt, 1.00001f), Hk, cnt_k, lo, hi, sm);
     csync<C>();
       const float blo = fmaxf(__fsub_rn(lo, zmargin(lo)), Hk), bhi = __fadd_rn(hi, zmargin(hi));
       const Band bp = band_smem<C>(P, X, R, blo, bhi, sm);
@@ -1319,6 +1494,8 @@ struct Smem {
   float2 cpc[32];             // PMI inputs of the first 32 band members
   float cscore[32];           // their exact scores (penalty + noise)
   unsigned char cflag[C::BAND];
+  int hc[kHistBins];          // bracket histogram: counts ...
+  float hm[kHistBins];        // ... and masses 2^(z2 - zmax) per bin
 };
 
 template <class C>
@@ -3067,6 +3244,8 @@ template <class C>
 constexpr size_t smem_bytes() {
   return sizeof(KSmem<C>) + 128;
 }
+static_assert(smem_bytes<CfgBF16>() <= 227 * 1024 && smem_bytes<CfgF32>() <= 227 * 1024,
+              "the grouped pipeline's shared memory fits one SM");
 
 static_assert(sizeof(WSmem) + 128 <= 227 * 1024, "the warp kernel's shared memory fits one SM");
 constexpr size_t wsmem_bytes() {

@@ -663,6 +663,29 @@ __device__ __forceinline__ float z2_smem(const PosCtx& X, const RowRef<C>& R, in
   return z2_of(X, c, u);
 }
 
+template <class C, bool CFG>
+__device__ __forceinline__ Span make_span(const RowRef<C>& R, int V);
+
+// Every element of the staged rows with its z2 (z2_smem's value): the 16-byte
+// vectors first (one thread per vector), then the elements of the partial
+// vectors at the row ends.
+template <class C, class F>
+__device__ __forceinline__ void for_each_z(const PosCtx& X, const RowRef<C>& R, int V, F&& f) {
+  const int tid = gtid<C>();
+  const Span S = X.cfg ? make_span<C, true>(R, V) : make_span<C, false>(R, V);
+  for (int j = S.j0 + tid; j < S.j1; j += C::NT) {
+    const uint4 a = lds128(R.sc + j * 16);
+    const uint4 b = X.cfg ? lds128(R.su + j * 16) : a;
+    const int v0 = j * C::W - S.head;
+#pragma unroll
+    for (int i = 0; i < C::W; ++i) f(v0 + i, z2_of(X, velem<C>(a, i), X.cfg ? velem<C>(b, i) : 0.f));
+  }
+  for (int e = tid; e < S.nscal; e += C::NT) {
+    const int v = scalar_v(S, e);
+    f(v, z2_smem<C>(X, R, v));
+  }
+}
+
 // ---------------------------------------------------------------- reductions
 
 template <class C>
@@ -930,16 +953,27 @@ __device__ __noinline__ int argmax_smem(const SampleParams& P, const PosCtx X, c
   int nc = 0;
   bool ovf = false;
   for (int v4 = 4 * gtid<C>(); v4 < V; v4 += 4 * C::NT) {
+    // the four tokens' z2 and filters first: no noise for a group none of
+    // whose tokens is kept
+    float zz[4];
+    unsigned keep = 0u;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int v = v4 + i;
+      zz[i] = v < V ? z2_smem<C>(X, R, v) : kNegInf;
+      bool in = v < V && zz[i] >= H;
+      if (in && K.minp_on) in = __fmul_rn(ex2_approx(__fsub_rn(zz[i], X.zmax)), K.r) >= K.minp_thr;
+      keep |= in ? (1u << i) : 0u;
+    }
+    if (!keep) continue;
     float g[4] = {0.f, 0.f, 0.f, 0.f};
     if (K.noisy) noise4(P, K, v4, g);
     const unsigned hb = K.pen_on ? hist4(P, K.b, v4) : 0u;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int v = v4 + i;
-      if (v >= V) break;
-      const float z = z2_smem<C>(X, R, v);
-      if (!(z >= H)) continue;
-      if (K.minp_on && !(__fmul_rn(ex2_approx(__fsub_rn(z, X.zmax)), K.r) >= K.minp_thr)) continue;
+      if (!((keep >> i) & 1u)) continue;
+      const float z = zz[i];
       float va = __fmaf_rn(z, kLn2, X.Kval);
       if ((hb >> i) & 1u) va = va > 0.f ? __fmul_rn(va, K.rrep) : __fmul_rn(va, K.rep);
       const float sc = K.noisy ? __fadd_rn(va, g[i]) : va;
@@ -972,14 +1006,13 @@ __device__ __noinline__ int argmax_smem(const SampleParams& P, const PosCtx X, c
     for (int q = 0; q < nc; ++q) rescore(cv[q], z2_smem<C>(X, R, cv[q]));
   }
   if (all || band_lo < H) {
-    for (int v = gtid<C>(); v < V; v += C::NT) {
-      const float z = z2_smem<C>(X, R, v);
+    for_each_z<C>(X, R, V, [&](int v, float z) {
       const bool in_main = z >= H;
       const bool in_band = z >= band_lo && z < H;
-      if (!(in_band || (all && in_main))) continue;
-      if (K.minp_on && !(__fmul_rn(ex2_approx(__fsub_rn(z, X.zmax)), K.r) >= K.minp_thr)) continue;
+      if (!(in_band || (all && in_main))) return;
+      if (K.minp_on && !(__fmul_rn(ex2_approx(__fsub_rn(z, X.zmax)), K.r) >= K.minp_thr)) return;
       rescore(v, z);
-    }
+    });
   }
   return block_pick<C>(bp, K.turbo, sm, slot);
 }
@@ -1030,24 +1063,6 @@ __device__ __forceinline__ void rank_sort(int n, Smem<C>& sm) {
   csync<C>();
 }
 
-__device__ __forceinline__ void band_push(unsigned long long* cand, float* cande, int* counter, bool in,
-                                          unsigned long long key_if_in, float e_if_in, int cap) {
-  const int lane = threadIdx.x & 31;
-  const unsigned bal = __ballot_sync(0xffffffffu, in);
-  if (bal) {
-    int base = 0;
-    if (lane == 0) base = atomicAdd(counter, __popc(bal));
-    base = __shfl_sync(0xffffffffu, base, 0);
-    if (in) {
-      const int at = base + __popc(bal & ((1u << lane) - 1u));
-      if (at < cap) {
-        cand[at] = key_if_in;
-        cande[at] = e_if_in;
-      }
-    }
-  }
-}
-
 // Cold band from the staged rows: {lo_z <= z2 < hi_z}, with count and mass above hi_z.
 template <class C>
 __device__ __noinline__ Band band_smem(const SampleParams& P, const PosCtx X, const RowRef<C> R, float lo_z,
@@ -1059,22 +1074,18 @@ __device__ __noinline__ Band band_smem(const SampleParams& P, const PosCtx X, co
   if (gtid<C>() == 0) sm.misc[0] = 0;
   csync<C>();
   float na = 0.f, ma = 0.f;
-  for (int v0 = 0; v0 < V; v0 += C::NT) {
-    const int v = v0 + gtid<C>();
-    float z = kNegInf;
-    if (v < V) z = z2_smem<C>(X, R, v);
-    const bool above = v < V && z >= hi_z;
-    na += above ? 1.f : 0.f;
-    ma += above ? ex2_approx(__fsub_rn(z, X.zmax)) : 0.f;
-    const bool in = v < V && z >= lo_z && z < hi_z;
-    unsigned long long key = 0ull;
-    float e = 0.f;
-    if (in) {
-      key = cand_key(exact_val<C>(P, X, R, v), v);
-      e = ex2_approx(__fsub_rn(z, X.zmax));
+  for_each_z<C>(X, R, V, [&](int v, float z) {
+    if (z >= hi_z) {
+      na += 1.f;
+      ma += ex2_approx(__fsub_rn(z, X.zmax));
+    } else if (z >= lo_z) {
+      const int at = atomicAdd(&sm.misc[0], 1);
+      if (at < C::BAND) {
+        sm.cand[at] = cand_key(exact_val<C>(P, X, R, v), v);
+        sm.cande[at] = ex2_approx(__fsub_rn(z, X.zmax));
+      }
     }
-    band_push(sm.cand, sm.cande, &sm.misc[0], in, key, e, C::BAND);
-  }
+  });
   float acc[8] = {na, ma, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   block_sum8<C>(acc, sm, slot);
   Band bd;
@@ -1314,14 +1325,13 @@ __device__ __noinline__ bool bracket_hist(const PosCtx X, const RowRef<C> R, int
       sm.hm[i] = 0.f;
     }
     csync<C>();
-    for (int v = tid; v < V; v += C::NT) {
-      const float z = z2_smem<C>(X, R, v);
+    for_each_z<C>(X, R, V, [&](int, float z) {
       if (z >= base && z < top) {
         const int bi = min(max((int)__fmul_rn(__fsub_rn(z, base), iw), 0), NB - 1);
         atomicAdd(&sm.hc[bi], 1);
         if (by_mass) atomicAdd(&sm.hm[bi], ex2_approx(__fsub_rn(z, X.zmax)));
       }
-    }
+    });
     csync<C>();
     // lane s of the group's first warp scans bins NB-1-s*PER downwards; the
     // running totals G(j) = F(base + j*w) grow towards lower bins

@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the block-diffusion select step: logit rows/sec at V = 8194.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 1|3]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 1|2|3|4]
 
 One *step* is one select step (m8than/yapd ``server/engine.py:533-612``) over one
 GPU's batch: configuration 1 by default (64 requests x 2 CFG rows x 32 positions
@@ -11,6 +11,11 @@ the block state (masked positions, step counter, commit flag) evolves through
 the kernel's own outputs and is reset at each block start.  A logit row is
 counted when the step must read it (masked position of a non-commit request),
 the metric of the reference's tick.
+
+Configuration 4 puts the speech LM head in front of the step: each step first
+multiplies the hidden states (512 requests x 2 x 32 rows of 1024, bf16) by the
+head weight (8194 x 1024) with cuBLAS into a bf16 logits buffer (the unfused
+form, ``server/engine.py:517-520``), then runs the select step on it.
 
 Under ``torchrun`` each rank runs its own request shard (weak scaling, no
 per-step collective); ranks gather their committed tokens with one NCCL
@@ -53,7 +58,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=8000)
     ap.add_argument("--warmup", type=int, default=16)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3])
+    ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3, 4])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=16)
@@ -134,11 +139,27 @@ class ClockSampler:
 # ------------------------------------------------------------------ workload
 
 def config_name(cfg: int) -> str:
-    return {1: "config1", 2: "config2", 3: "config3"}[cfg]
+    return {1: "config1", 2: "config2", 3: "config3", 4: "config4"}[cfg]
+
+
+N_HIDDEN = 3  # rotating hidden-state buffers of config 4 (3 x 64 MB > L2)
 
 
 def make_inputs(cfg: int, rank: int, device):
-    """The per-GPU shard: config defaults, Philox noise (production mode)."""
+    """The per-GPU shard: config defaults, Philox noise (production mode).
+
+    Configuration 4 returns one logits buffer and a ``gemm`` dict holding the
+    device operands of the head GEMM that fills it every step."""
+    if cfg == 4:
+        inp = WL.make_config(4, seed=100 + rank, explicit_noise=False, lmhead_logits=False)
+        g = torch.Generator(device=device).manual_seed(7 + 131 * rank)
+        hid = [inp.meta["hidden"].to(device)]
+        for _ in range(N_HIDDEN - 1):
+            hid.append(torch.randn(hid[0].shape, generator=g, device=device).to(torch.bfloat16))
+        gemm = {"hidden": hid, "weight": inp.meta["weight"].to(device),
+                "ev": None}
+        logits = torch.empty(inp.logits.shape, dtype=torch.bfloat16, device=device)
+        return inp, [logits], gemm
     inp = WL.make_config(cfg, seed=100 + rank, explicit_noise=False)
     g = torch.Generator(device=device).manual_seed(7 + 131 * rank)
     bufs = [inp.logits.to(device)]
@@ -147,14 +168,14 @@ def make_inputs(cfg: int, rank: int, device):
         idx = torch.randint(0, inp.V, (*inp.logits.shape[:2], 3), generator=g, device=device)
         x.scatter_add_(2, idx, torch.full(idx.shape, 8.0, device=device))
         bufs.append(x.to(inp.logits.dtype))
-    return inp, bufs
+    return inp, bufs, None
 
 
 class Runner:
     """Eight captured graphs, one per diffusion step of a block."""
 
-    def __init__(self, inp, bufs, device):
-        self.inp, self.bufs, self.dev = inp, bufs, device
+    def __init__(self, inp, bufs, device, gemm=None):
+        self.inp, self.bufs, self.dev, self.gemm = inp, bufs, device, gemm
         B, L = inp.B, inp.L
         self.xt0 = torch.full((B, L), inp.mask_id, dtype=torch.int64, device=device)
         self.k0 = torch.zeros(B, dtype=torch.int64, device=device)
@@ -178,7 +199,9 @@ class Runner:
         self.K = inp.num_steps
         self.ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                    for _ in range(self.K)]
-        for a, b in self.ev:  # torch creates the CUDA events lazily, on first record
+        self.gev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                    for _ in range(self.K)] if gemm else None
+        for a, b in self.ev + (self.gev or []):  # torch creates the CUDA events lazily
             a.record()
             b.record()
         torch.cuda.synchronize()
@@ -189,9 +212,19 @@ class Runner:
             self.xt.copy_(self.xt0)
             self.k.copy_(self.k0)
             self.c.copy_(self.c0)
+        if self.gemm:
+            if prof:
+                record_event(self.gev[k][0])
+            self.head_gemm(self.gemm["hidden"][k % len(self.gemm["hidden"])], self.bufs[0])
+            if prof:
+                record_event(self.gev[k][1])
         S.select_step(self.bufs[k % len(self.bufs)], self.xt, self.k, self.c, self.lp, self.sched,
                       self.q, seed=1234, offset=k, out=self.out,
                       prof_events=self.ev[k] if prof else None, **self.kw)
+
+    def head_gemm(self, hidden, logits):
+        """logits = hidden @ weight.T (cuBLAS bf16, fp32 accumulation)."""
+        torch.mm(hidden, self.gemm["weight"].t(), out=logits.view(-1, logits.shape[-1]))
 
     def rows_per_step(self):
         """Sampled positions per step index, from one eager block."""
@@ -230,6 +263,23 @@ class Runner:
         torch.cuda.synchronize()
 
 
+def record_event(ev):
+    """Record a timing event on the current stream; inside a graph capture as
+    an event-record node (a plain record there only orders the capture)."""
+    from cuda.bindings import runtime as rt
+    st = torch.cuda.current_stream()
+    err, cap = rt.cudaStreamIsCapturing(rt.cudaStream_t(st.cuda_stream))
+    if int(err) != 0:
+        raise RuntimeError(f"cudaStreamIsCapturing failed: {err}")
+    if cap == rt.cudaStreamCaptureStatus.cudaStreamCaptureStatusActive:
+        err, = rt.cudaEventRecordWithFlags(rt.cudaEvent_t(ev.cuda_event), rt.cudaStream_t(st.cuda_stream),
+                                           rt.cudaEventRecordExternal)
+        if int(err) != 0:
+            raise RuntimeError(f"cudaEventRecordWithFlags failed: {err}")
+    else:
+        ev.record(st)
+
+
 def event_ms(e0, e1) -> float:
     """Elapsed time between two events recorded by the library (inside a graph,
     so torch's own bookkeeping does not know them)."""
@@ -266,6 +316,13 @@ def committed_traffic(cfg: int):
 
 # ------------------------------------------------------------ CPU baselines
 
+def cpu_head(inp):
+    """Configuration 4: the head GEMM on the host cores, as the reference's
+    speech head runs before its select step."""
+    if inp.meta.get("config") == 4:
+        inp.logits = WL.lmhead_logits_of(inp.meta["hidden"], inp.meta["weight"]).view(inp.logits.shape)
+
+
 def cpu_sample(cfg: int, seconds: float, B_s: int = 2):
     """The CPU oracle (the reference algorithm, torch CPU, all host cores) on a
     bounded sample of the same workload: B_s requests, all positions masked."""
@@ -276,6 +333,7 @@ def cpu_sample(cfg: int, seconds: float, B_s: int = 2):
     O.select_step(inp, noise="philox", seed=1, offset=0)
     n, t0 = 0, time.perf_counter()
     while True:
+        cpu_head(inp)
         O.select_step(inp, noise="philox", seed=1, offset=n)
         n += 1
         el = time.perf_counter() - t0
@@ -283,7 +341,8 @@ def cpu_sample(cfg: int, seconds: float, B_s: int = 2):
             break
     return {"value": rows * n / el, "unit": "rows/s", "cores": torch.get_num_threads(),
             "kind": "port", "sample": f"{config_name(cfg)} shape with B={B_s} requests, all "
-            f"{inp.L} positions masked, {n} steps in {el:.1f} s (torch CPU oracle)"}, el / n, rows
+            f"{inp.L} positions masked, {n} steps in {el:.1f} s (torch CPU oracle"
+            f"{', after the head GEMM' if cfg == 4 else ''})"}, el / n, rows
 
 
 # ----------------------------------------------------------------- main arms
@@ -297,15 +356,18 @@ def run_reference(args, ws, rank):
     inp = WL.make_config(args.config, seed=999, B=B_s, explicit_noise=False)
     rows = 2 * inp.B * inp.L
     for i in range(args.warmup):
+        cpu_head(inp)
         O.select_step(inp, noise="philox", seed=1, offset=i)
     t0 = time.perf_counter()
     for i in range(args.steps):
+        cpu_head(inp)
         O.select_step(inp, noise="philox", seed=1, offset=i)
     el = time.perf_counter() - t0
     v = rows * args.steps / el
     cb = {"value": v, "unit": "rows/s", "cores": torch.get_num_threads(), "kind": "port",
           "sample": f"{config_name(args.config)} shape with B={B_s} requests per step, all positions "
-                    f"masked (torch CPU oracle of server/engine.py:533-612)"}
+                    f"masked (torch CPU oracle of server/engine.py:533-612"
+                    f"{', after the head GEMM' if args.config == 4 else ''})"}
     line = {"metric": METRIC, "value": v, "unit": "rows/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -321,8 +383,8 @@ def run_ours(args, ws, rank, local):
     dist = dist_init(ws, local)
     dev = torch.device("cuda", local)
     cfg = args.config
-    inp, bufs = make_inputs(cfg, rank, dev)
-    R = Runner(inp, bufs, dev)
+    inp, bufs, gemm = make_inputs(cfg, rank, dev)
+    R = Runner(inp, bufs, dev, gemm)
     positions = R.rows_per_step()
     R.capture()
     K = R.K
@@ -355,6 +417,7 @@ def run_ours(args, ws, rank, local):
         R.pgraphs[k].replay()
     torch.cuda.synchronize()
     kern_ms = [event_ms(*R.ev[k]) for k in range(K)]
+    gemm_ms = [event_ms(*R.gev[k]) for k in range(K)] if gemm else None
     my_rows = sum(2 * positions[(args.warmup + i) % K] for i in range(args.steps))
     byt = [algorithmic_bytes(inp, positions[k]) for k in range(K)]
     achieved = sum(byt) / (sum(kern_ms) * 1e-3) / 1e9
@@ -414,6 +477,18 @@ def run_ours(args, ws, rank, local):
             "clocks": ck,
             "cpu_baseline": cpu,
         }
+        if gemm:
+            h = gemm["hidden"][0]
+            flop = 2.0 * h.shape[0] * h.shape[1] * inp.V
+            gm = sum(gemm_ms) / K
+            line["config"].update({
+                "workload": f"config4 (unfused): cuBLAS bf16 head GEMM [{h.shape[0]} x {h.shape[1]}] x "
+                            f"[{inp.V} x {h.shape[1]}]^T -> bf16 logits, then the select step; "
+                            f"{inp.B} requests x 2 CFG rows x {inp.L} positions, {K}-step blocks",
+                "gemm_ms_per_step": gm, "gemm_tflops": flop / (gm * 1e-3) / 1e12,
+                "l2": f"{N_HIDDEN} rotating hidden-state buffers ({N_HIDDEN * h.numel() * 2 / 1e6:.0f} MB) "
+                      f"and a {inp.logits.numel() * 2 / 1e6:.0f} MB logits buffer > L2"})
+            line["gpu_launches"] = (LAUNCHES_PER_STEP + 1) * args.steps
         print(json.dumps(line), flush=True)
     if dist:
         del R
@@ -425,7 +500,11 @@ def run_e2e(R, inp, dev, steps):
     logits and block state host->device and reads the new state back (the one
     device->host sync of the engine tick, server/engine.py:635-636)."""
     K = R.K
-    pin = [b.cpu().pin_memory() for b in R.bufs[:2]]
+    if R.gemm:
+        pin = [h.cpu().pin_memory() for h in R.gemm["hidden"][:2]]
+        dhid = torch.empty_like(R.gemm["hidden"][0])
+    else:
+        pin = [b.cpu().pin_memory() for b in R.bufs[:2]]
     dlog = torch.empty_like(R.bufs[0])
     hx = R.xt0.cpu().pin_memory()
     hk = R.k0.cpu().pin_memory()
@@ -448,7 +527,11 @@ def run_e2e(R, inp, dev, steps):
             hk.zero_()
             hc.zero_()
         rows = 2 * int(((hx == inp.mask_id) & ~hc[:, None]).sum())
-        dlog.copy_(pin[i % 2], non_blocking=True)
+        if R.gemm:
+            dhid.copy_(pin[i % 2], non_blocking=True)
+            R.head_gemm(dhid, dlog)
+        else:
+            dlog.copy_(pin[i % 2], non_blocking=True)
         dx.copy_(hx, non_blocking=True)
         dk.copy_(hk, non_blocking=True)
         dc.copy_(hc, non_blocking=True)
@@ -476,7 +559,7 @@ def run_e2e(R, inp, dev, steps):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
-    h2d = dlog.numel() * dlog.element_size() + hx.numel() * 8 + hk.numel() * 8 + hc.numel()
+    h2d = pin[0].numel() * pin[0].element_size() + hx.numel() * 8 + hk.numel() * 8 + hc.numel()
     d2h = ox.numel() * 8 + ok_.numel() * 8 + oc.numel() + on.numel() * 4 + oe.numel()
     return {"ms": ms, "rows": rows, "h2d": h2d, "d2h": d2h}
 

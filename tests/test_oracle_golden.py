@@ -105,3 +105,17 @@ def test_philox_known_answers():
     for ctr, key, want in cases:
         out = philox4x32_10(np.array([ctr], dtype=np.uint32), key)
         assert tuple(int(x) for x in out[0]) == want
+
+
+def test_lmhead_workload_shapes():
+    # configuration 4: the logits are the bf16 rounding of the fp32 head GEMM
+    from yapd_b200 import workloads as WL
+    inp = WL.make_config(4, seed=1, B=2)
+    h, w = inp.meta["hidden"], inp.meta["weight"]
+    assert h.shape == (2 * 2 * 32, WL.LMHEAD_HIDDEN) and w.shape == (WL.V_SPEECH, WL.LMHEAD_HIDDEN)
+    assert inp.logits.shape == (4, 32, WL.V_SPEECH) and inp.logits.dtype == torch.bfloat16
+    ref = (h.float() @ w.float().T).to(torch.bfloat16).view(4, 32, -1)
+    assert torch.equal(inp.logits, ref)
+    lazy = WL.make_config(4, seed=1, B=2, lmhead_logits=False)
+    assert lazy.logits.shape == inp.logits.shape and lazy.logits.stride() == (0, 0, 0)
+    assert torch.equal(lazy.meta["hidden"], h)

@@ -196,3 +196,12 @@ def test_min_p_wide_bands_many_items():
     inp.logits = (torch.randn(inp.logits.shape, generator=g) * 1.1).to(inp.logits.dtype)
     inp = _uniform(inp, temperature=0.8, top_k=0, top_p=0.95, min_p=0.05, rep=1.2)
     check(inp, dense=True)
+
+
+@pytest.mark.parametrize("noise,masked", [("explicit", "ragged"), ("philox", "all")])
+def test_lmhead_logits_config4(noise, masked):
+    # configuration 4's logits come from a speech head (hidden ~ N(0,1) times a
+    # N(0, 0.02) weight): flat rows (std 0.64) whose min-p bands hold hundreds
+    # of tokens, so every position takes the wide-band path
+    inp = make_config(4, seed=21, B=4, masked=masked, explicit_noise=(noise == "explicit"))
+    check(inp, noise=noise, seed=5, offset=2, dense=(masked == "all"))

@@ -2327,6 +2327,8 @@ struct WCfg {
 };
 static_assert(WCfg::MAXCH * WCfg::TPC <= 64, "the marks of a position fit one 64-bit word");
 static_assert(WCfg::STASH == 64, "the stash compaction holds two entries per lane");
+static_assert((WCfg::BANDW & (WCfg::BANDW - 1)) == 0 && WCfg::BANDW >= 64,
+              "the band list doubles as a ring of 64 entries or more (a power of two)");
 static_assert(WCfg::NTHREADS >= CfgBF16::NTHREADS, "the grouped pipeline runs inside the warp kernel's CTA");
 
 // Work-list entries of deferred positions carry this bit until the CTA
@@ -2537,27 +2539,239 @@ __device__ __forceinline__ void team_sync(const WTeam& tm) {
   else __syncwarp();
 }
 
-__device__ __forceinline__ void band_push(WBand& B, int id, float c, float u) {
-  const int at = atomicAdd(&B.n, 1);
-  if (at < WCfg::BANDW) {
-    B.id[at] = id;
-    B.c[at] = c;
-    B.u[at] = u;
+// Where a warp finds its share of the band {z2 >= lo_z} after the stream:
+// its stash entries and the marked vectors the stash could not take (or,
+// when the running margins were too thin, all of its vectors), and the
+// scalar element of the lane.
+struct BandScan {
+  float lo_z;
+  int nst;
+  unsigned long long ovf;
+  bool marks;  // the marks cover the band
+  bool has_scalar;
+  float xsc, xsu;
+  int r, T;
+};
+
+// f(id, c, u) for every member (z2 >= lo_z) of the lane's share of the band.
+template <bool CFG, class F>
+__device__ __forceinline__ void for_band_members(const PosCtx& X, const WItem& I, const WStash& st,
+                                                 const BandScan& bs, F&& f) {
+  using C = CfgBF16;
+  const int lane = threadIdx.x & 31;
+  auto vec = [&](int j, const uint4& a, const uint4& b) {
+    const int v0 = j * C::W - I.S.head;
+#pragma unroll
+    for (int i = 0; i < C::W; ++i) {
+      const float c = velem<C>(a, i);
+      const float u = CFG ? velem<C>(b, i) : 0.f;
+      if (z2_of(X, c, u) >= bs.lo_z) f(v0 + i, c, u);
+    }
+  };
+  if (bs.marks) {
+    for (int i = lane; i < min(bs.nst, WCfg::STASH); i += 32) vec(st.j[i], st.c[i], st.u[i]);
+    unsigned long long o = bs.ovf;
+    while (o) {
+      const int bit = __ffsll((long long)o) - 1;
+      o &= o - 1ull;
+      const int q = bs.r + bs.T * (bit / WCfg::TPC);
+      const int j = I.S.j0 + lane + 32 * (bit % WCfg::TPC) + WCfg::CHV * q;
+      const uint4 a = ldg128(I.gc.src + j * 16);
+      vec(j, a, CFG ? ldg128(I.gu.src + j * 16) : a);
+    }
+  } else {
+    for (int q = bs.r; q < I.nch; q += bs.T) {
+      const int nv = min(WCfg::CHV, I.nvi - q * WCfg::CHV);
+      for (int v = lane; v < nv; v += 32) {
+        const int j = I.S.j0 + q * WCfg::CHV + v;
+        const uint4 a = ldg128(I.gc.src + j * 16);
+        vec(j, a, CFG ? ldg128(I.gu.src + j * 16) : a);
+      }
+    }
   }
+  if (bs.has_scalar && z2_of(X, bs.xsc, CFG ? bs.xsu : 0.f) >= bs.lo_z) f(scalar_v(I.S, lane), bs.xsc, bs.xsu);
 }
 
-// The band members of 16-byte vector j (row copy index) into B.
-template <bool CFG>
-__device__ __forceinline__ void band_vector(const PosCtx& X, const Span& S, int j, const uint4& a, const uint4& b,
-                                            float lo_z, WBand& B) {
+// The same share walked by the whole warp in lockstep: f(m, id, c, u) is
+// called by every lane for each element slot, m telling whether the lane's
+// element there is a member, so that f may use warp collectives.
+template <bool CFG, class F>
+__device__ __forceinline__ void for_band_members_sync(const PosCtx& X, const WItem& I, const WStash& st,
+                                                      const BandScan& bs, F&& f) {
   using C = CfgBF16;
-  const int v0 = j * C::W - S.head;
+  const int lane = threadIdx.x & 31;
+  auto vec = [&](bool has, int j, const uint4& a, const uint4& b) {
+    const int v0 = j * C::W - I.S.head;
+#pragma unroll 1
+    for (int i = 0; i < C::W; ++i) {
+      const float c = velem<C>(a, i);
+      const float u = CFG ? velem<C>(b, i) : 0.f;
+      f(has && z2_of(X, c, u) >= bs.lo_z, v0 + i, c, u);
+    }
+  };
+  const uint4 zero4 = make_uint4(0u, 0u, 0u, 0u);
+  if (bs.marks) {
+    const int ns = min(bs.nst, WCfg::STASH);
+    for (int base = 0; base < ns; base += 32) {
+      const int i = base + lane;
+      const bool has = i < ns;
+      vec(has, has ? st.j[i] : 0, has ? st.c[i] : zero4, has ? st.u[i] : zero4);
+    }
+    unsigned long long o = bs.ovf;
+    int rounds = __popcll(o);
 #pragma unroll
-  for (int i = 0; i < C::W; ++i) {
-    const float c = velem<C>(a, i);
-    const float u = CFG ? velem<C>(b, i) : 0.f;
-    if (z2_of(X, c, u) >= lo_z) band_push(B, v0 + i, c, u);
+    for (int s = 16; s > 0; s >>= 1) rounds = max(rounds, __shfl_xor_sync(0xffffffffu, rounds, s));
+    for (int it = 0; it < rounds; ++it) {
+      const bool has = o != 0ull;
+      int j = 0;
+      uint4 a = zero4, b = zero4;
+      if (has) {
+        const int bit = __ffsll((long long)o) - 1;
+        o &= o - 1ull;
+        const int q = bs.r + bs.T * (bit / WCfg::TPC);
+        j = I.S.j0 + lane + 32 * (bit % WCfg::TPC) + WCfg::CHV * q;
+        a = ldg128(I.gc.src + j * 16);
+        b = CFG ? ldg128(I.gu.src + j * 16) : a;
+      }
+      vec(has, j, a, b);
+    }
+  } else {
+    for (int q = bs.r; q < I.nch; q += bs.T) {
+      const int nv = min(WCfg::CHV, I.nvi - q * WCfg::CHV);
+      for (int v0 = 0; v0 < nv; v0 += 32) {
+        const bool has = v0 + lane < nv;
+        const int j = I.S.j0 + q * WCfg::CHV + v0 + lane;
+        uint4 a = zero4, b = zero4;
+        if (has) {
+          a = ldg128(I.gc.src + j * 16);
+          b = CFG ? ldg128(I.gu.src + j * 16) : a;
+        }
+        vec(has, j, a, b);
+      }
+    }
   }
+  f(bs.has_scalar && z2_of(X, bs.xsc, CFG ? bs.xsu : 0.f) >= bs.lo_z, scalar_v(I.S, lane), bs.xsc, bs.xsu);
+}
+
+// A kept member's (score key, (exact value, -id) key); score key 0 when the
+// score is not a number above -inf.  Out of line: one copy of the Philox
+// rounds for the whole wide path.
+struct WideCand {
+  uint32_t ks;
+  unsigned long long kk;
+};
+template <bool CFG>
+__device__ __forceinline__ WideCand wide_score(const SampleParams& P, const PosCtx& X, const ScoreCtx& K, int id,
+                                               float c, float u) {
+  const float vals = exact_val_cu(P, X, c, u);
+  const float sc = score_from(K, vals, score_in<false>(P, K, id));
+  WideCand w;
+  w.ks = (sc == sc && sc > kNegInf) ? ord_key(sc) : 0u;
+  w.kk = cand_key(vals, id);
+  return w;
+}
+
+// The sample of a min-p band too wide for the list, by one warp over the
+// members (for_band_members), given the lane's band mass and its member of
+// largest z2 from the collection.  Every token ranked above a member has an
+// exact value at least the member's, so it lies in the band too: when the
+// band's mass is below top_p (less a margin far above the rounding of either
+// side's sums) top-p drops no member, and the sample is the best score
+// (penalty + noise) among the members min-p keeps, p >= min_p * p0, ties to
+// the larger (exact value, -id) key; with nothing kept (scores not numbers)
+// the top member is taken -- what band_finish_warp's sort and prefix sums
+// give.  p0 is the p of the member of largest z2 (ties to the lower id), the
+// top member by (exact value, -id) but where the two orders differ by a
+// rounding, which moves the min-p bound by as much.  Returns false, having
+// written nothing, when top-p may cut the band.
+template <bool CFG>
+__device__ __forceinline__ bool wide_minp_pick(const SampleParams& P, const ItemParams Q, const PosCtx X,
+                                            const ScoreCtx K, const WItem I, const WStash& st,
+                                            const BandScan scan, WBand& B, float bmass, float tz, int tid,
+                                            float tc, float tu) {
+  const int lane = threadIdx.x & 31;
+  if (Q.top_p < 1.0f && !(__fmul_rn(warp_sum(bmass), K.r) < __fsub_rn(Q.top_p, 1e-3f))) return false;
+  float wz = tz;
+  int wid = tid;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float yz = __shfl_xor_sync(0xffffffffu, wz, o);
+    const int yi = __shfl_xor_sync(0xffffffffu, wid, o);
+    if (yz > wz || (yz == wz && yi < wid)) {
+      wz = yz;
+      wid = yi;
+    }
+  }
+  const int tl = __ffs(__ballot_sync(0xffffffffu, tz == wz && tid == wid)) - 1;
+  const float p0 = __fmul_rn(ex2_approx(__fsub_rn(wz, X.zmax)), K.r);
+  const float thr = __fmul_rn(Q.min_p, p0);
+  uint32_t bs = 0u;
+  unsigned long long bk = 0ull;
+  float bc = 0.f, bu = 0.f;
+  // the kept members go through a ring in B (its list is of no use for a
+  // band this wide) and are scored 32 at a time, one per lane
+  auto score = [&](int slot) {
+    const int id = B.id[slot];
+    const float c = B.c[slot], u = B.u[slot];
+    const WideCand w = wide_score<CFG>(P, X, K, id, c, u);
+    if (w.ks > bs || (w.ks == bs && w.kk > bk)) {
+      bs = w.ks;
+      bk = w.kk;
+      bc = c;
+      bu = u;
+    }
+  };
+  int head = 0, tail = 0;  // warp-uniform
+  for_band_members_sync<CFG>(X, I, st, scan, [&](bool m, int id, float c, float u) {
+    const bool keep = m && __fmul_rn(ex2_approx(__fsub_rn(z2_of(X, c, u), X.zmax)), K.r) >= thr;
+    const unsigned bal = __ballot_sync(0xffffffffu, keep);
+    if (bal == 0u) return;
+    if (keep) {
+      const int at = (tail + __popc(bal & ((1u << lane) - 1u))) & (WCfg::BANDW - 1);
+      B.id[at] = id;
+      B.c[at] = c;
+      B.u[at] = u;
+    }
+    tail += __popc(bal);
+    if (tail - head >= 32) {
+      __syncwarp();
+      score((head + lane) & (WCfg::BANDW - 1));
+      head += 32;
+      __syncwarp();
+    }
+  });
+  __syncwarp();
+  if (lane < tail - head) score((head + lane) & (WCfg::BANDW - 1));
+  uint32_t ws = bs;
+  unsigned long long wk = bk;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint32_t ys = __shfl_xor_sync(0xffffffffu, ws, o);
+    const unsigned long long yk = __shfl_xor_sync(0xffffffffu, wk, o);
+    if (ys > ws || (ys == ws && yk > wk)) {
+      ws = ys;
+      wk = yk;
+    }
+  }
+  const bool any = ws != 0u;
+  const bool mine = any ? (bs == ws && bk == wk) : (lane == tl);
+  const unsigned who = __ballot_sync(0xffffffffu, mine);
+  if (who == 0u) {
+    if (lane == 0) {
+      atomicOr(P.status, (unsigned)YAPD_STATUS_INTERNAL);
+      P.sampled[Q.pos] = 0;
+    }
+  } else if (lane == __ffs(who) - 1) {
+    int chosen = any ? cand_id(wk) : wid;
+    if (chosen < 0 || chosen >= P.V) {
+      atomicOr(P.status, (unsigned)YAPD_STATUS_INTERNAL);
+      chosen = 0;
+    }
+    P.sampled[Q.pos] = chosen;
+    if (P.pcu) P.pcu[Q.pos] = any ? pmi_cu<CFG>(X, bc, bu) : pmi_cu<CFG>(X, tc, tu);
+  }
+  __syncwarp();
+  return true;
 }
 
 // Leader warp: a band of 32 < n <= BANDW members (four per lane).  Exact
@@ -2992,35 +3206,35 @@ __device__ __forceinline__ bool w_position(const SampleParams& P, WSmem& ws, con
   const float lo_z = __fsub_rn(zm, zmargin(zm));
   const float zmp = __fadd_rn(m3[2], lg_minp);
   const float need = __fadd_rn(zmargin(zmp), __fadd_rn(1e-3f, __fmul_rn(4e-6f, __fadd_rn(fabsf(X.K2), fabsf(zmp)))));
-  if (mg_min >= need) {
-    for (int i = lane; i < min(nst, WCfg::STASH); i += 32)
-      band_vector<CFG>(X, I.S, st_.j[i], st_.c[i], st_.u[i], lo_z, B);
-    while (ovf) {
-      const int bit = __ffsll((long long)ovf) - 1;
-      ovf &= ovf - 1ull;
-      const int q = tm.r + tm.T * (bit / WCfg::TPC);
-      const int v = lane + 32 * (bit % WCfg::TPC) + WCfg::CHV * q;
-      const int j = I.S.j0 + v;
-      const uint4 a = ldg128(I.gc.src + j * 16);
-      const uint4 b = CFG ? ldg128(I.gu.src + j * 16) : a;
-      band_vector<CFG>(X, I.S, j, a, b, lo_z, B);
+  const BandScan bs{lo_z, nst, ovf, mg_min >= need, has_scalar, xsc, xsu, tm.r, tm.T};
+  // collection; alongside, the lane's band mass 2^(z2 - zmax) and its
+  // member of largest z2 (ties to the lower id), which a band too wide for
+  // the list needs
+  float bmass = 0.f, tz = kNegInf, tc = 0.f, tu = 0.f;
+  int tid = 0x7fffffff;
+  for_band_members<CFG>(X, I, st_, bs, [&](int id, float c, float u) {
+    const int at = atomicAdd(&B.n, 1);
+    if (at < WCfg::BANDW) {
+      B.id[at] = id;
+      B.c[at] = c;
+      B.u[at] = u;
     }
-  } else {
-    // the running margins were too thin for this warp: test all its vectors
-    for (int q = tm.r; q < I.nch; q += tm.T) {
-      const int nv = min(WCfg::CHV, I.nvi - q * WCfg::CHV);
-      for (int v = lane; v < nv; v += 32) {
-        const int j = I.S.j0 + q * WCfg::CHV + v;
-        const uint4 a = ldg128(I.gc.src + j * 16);
-        const uint4 b = CFG ? ldg128(I.gu.src + j * 16) : a;
-        band_vector<CFG>(X, I.S, j, a, b, lo_z, B);
-      }
+    const float z = z2_of(X, c, u);
+    bmass += ex2_approx(__fsub_rn(z, X.zmax));
+    if (z > tz || (z == tz && id < tid)) {
+      tz = z;
+      tid = id;
+      tc = c;
+      tu = u;
     }
-  }
-  if (has_scalar && z2_of(X, xsc, CFG ? xsu : 0.f) >= lo_z) band_push(B, scalar_v(I.S, lane), xsc, xsu);
+  });
   team_sync(tm);
   if (tm.r != 0) return true;  // the team's first warp resolves the band
   const int n = B.n;
+  // a band too wide for the list, in a one-warp team: resolved here when
+  // top-p cannot cut it
+  if (n > WCfg::BANDW && tm.T == 1 && wide_minp_pick<CFG>(P, Q, X, K, I, st_, bs, B, bmass, tz, tid, tc, tu))
+    return true;
   if (n <= 0 || n > WCfg::BANDW) return false;
   if (n == 1) {
     // a one-member band: min-p keeps it (p >= min_p * p), so does top-p

@@ -177,13 +177,20 @@ def make_block_state(gen: torch.Generator, B: int, L: int, K: int, mask_id: int,
 def make_config(config: int, seed: int = 0, *, B: int | None = None, L: int | None = None,
                 V: int = V_SPEECH, dtype=None, explicit_noise: bool = True,
                 masked: str = "all", k_step: int | None = None,
-                commit_frac: float = 0.0) -> StepInputs:
+                commit_frac: float = 0.0, lmhead_logits: bool = True) -> StepInputs:
     """Inputs for benchmark configurations 0-3.
 
     * 0: B=1, L=16, fp32, uniform parameters (the CPU parity case).
     * 1: B=64, L=32, bf16, uniform parameters.
     * 2: B=256, L=32, fp32, ragged masks and per-request parameters.
     * 3: B=256 per GPU, L=32, bf16, config-2 parameters.
+    * 4: B=512, L=32, bf16 logits of a speech LM head: hidden states
+      ``(B*2*L, 1024)`` ~ N(0, 1) times a head weight ``(V, 1024)`` ~ N(0, 0.02)
+      (both bf16, fp32 accumulation, rounded to bf16), config-1 parameters.
+      ``meta["hidden"]`` and ``meta["weight"]`` hold the two operands;
+      ``lmhead_logits=False`` skips the host GEMM (``logits`` is then a
+      zero-stride view of the right shape, for callers that run the GEMM on
+      the device).
 
     ``masked``: "all" (a block's first step) or "ragged" (U{1..L} masked
     positions per request).  ``B``, ``L``, ``V`` and ``dtype`` override the
@@ -191,7 +198,8 @@ def make_config(config: int, seed: int = 0, *, B: int | None = None, L: int | No
     """
     gen = torch.Generator().manual_seed(int(seed) * 1000003 + config)
     defaults = {0: (1, 16, torch.float32, 4), 1: (64, 32, torch.bfloat16, 8),
-                2: (256, 32, torch.float32, 8), 3: (256, 32, torch.bfloat16, 8)}
+                2: (256, 32, torch.float32, 8), 3: (256, 32, torch.bfloat16, 8),
+                4: (512, 32, torch.bfloat16, 8)}
     B0, L0, dt0, K = defaults[config]
     B = B0 if B is None else B
     L = L0 if L is None else L
@@ -199,9 +207,18 @@ def make_config(config: int, seed: int = 0, *, B: int | None = None, L: int | No
     nb = 2
     cfg_scale = 0.5
     pmi_lambda = 0.5
-    logits = make_logits(gen, B * nb, L, V, dtype=dtype)
+    meta = {"config": config, "seed": seed}
+    if config == 4:
+        hidden, weight = make_lmhead(gen, B * nb * L, V)
+        meta.update(hidden=hidden, weight=weight)
+        if lmhead_logits:
+            logits = lmhead_logits_of(hidden, weight).view(B * nb, L, V).to(dtype)
+        else:
+            logits = torch.zeros((1, 1, 1), dtype=dtype).expand(B * nb, L, V)
+    else:
+        logits = make_logits(gen, B * nb, L, V, dtype=dtype)
     log_prior = make_log_prior(gen, V)
-    if config in (0, 1):
+    if config in (0, 1, 4):
         temperature = torch.full((B,), 0.8)
         top_k = torch.zeros(B, dtype=torch.int32)
         top_p = torch.full((B,), 0.95)
@@ -240,7 +257,24 @@ def make_config(config: int, seed: int = 0, *, B: int | None = None, L: int | No
         rep_penalty=rep.float(), history=history, cfg_scale=cfg_scale, pmi_lambda=pmi_lambda,
         pos_noise=True, use_quantile=True, num_steps=K, nb=nb,
         mask_id=MASK_ID if V == V_SPEECH else V, stop_id=STOP_ID if V > STOP_ID else V - 1,
-        gumbel_tok=gtok, gumbel_pos=gpos, meta={"config": config, "seed": seed})
+        gumbel_tok=gtok, gumbel_pos=gpos, meta=meta)
+
+
+LMHEAD_HIDDEN = 1024
+
+
+def make_lmhead(gen: torch.Generator, rows: int, V: int, H: int = LMHEAD_HIDDEN):
+    """Speech-head operands: hidden ``(rows, H)`` ~ N(0, 1) and weight
+    ``(V, H)`` ~ N(0, 0.02), both bf16 (the config-4 distributions)."""
+    hidden = torch.randn(rows, H, generator=gen).to(torch.bfloat16)
+    weight = (torch.randn(V, H, generator=gen) * 0.02).to(torch.bfloat16)
+    return hidden, weight
+
+
+def lmhead_logits_of(hidden: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """``hidden @ weight.T`` accumulated in fp32, rounded to bf16 (the
+    speech head of ``server/engine.py:517-520``)."""
+    return (hidden.float() @ weight.float().T).to(torch.bfloat16)
 
 
 def gumbel_from_uniform(u: torch.Tensor) -> torch.Tensor:

@@ -143,6 +143,7 @@ def config_name(cfg: int) -> str:
 
 
 N_HIDDEN = 3  # rotating hidden-state buffers of config 4 (3 x 64 MB > L2)
+LOGIT_PAD = 8200  # config 4 logits row length: V = 8194 rounded up to 8 (16 bytes)
 
 
 def make_inputs(cfg: int, rank: int, device):
@@ -156,9 +157,15 @@ def make_inputs(cfg: int, rank: int, device):
         hid = [inp.meta["hidden"].to(device)]
         for _ in range(N_HIDDEN - 1):
             hid.append(torch.randn(hid[0].shape, generator=g, device=device).to(torch.bfloat16))
-        gemm = {"hidden": hid, "weight": inp.meta["weight"].to(device),
-                "ev": None}
-        logits = torch.empty(inp.logits.shape, dtype=torch.bfloat16, device=device)
+        # the head weight padded to LOGIT_PAD rows: the GEMM writes 16-byte
+        # aligned logits rows (cuBLAS takes its fast path; the select step
+        # reads the first V columns of each row through its row stride)
+        w = inp.meta["weight"].to(device)
+        wp = torch.zeros(LOGIT_PAD, w.shape[1], dtype=w.dtype, device=device)
+        wp[: w.shape[0]] = w
+        out = torch.empty(hid[0].shape[0], LOGIT_PAD, dtype=torch.bfloat16, device=device)
+        gemm = {"hidden": hid, "weight": wp, "out": out}
+        logits = out.view(inp.logits.shape[0], inp.logits.shape[1], LOGIT_PAD)[:, :, : inp.V]
         return inp, [logits], gemm
     inp = WL.make_config(cfg, seed=100 + rank, explicit_noise=False)
     g = torch.Generator(device=device).manual_seed(7 + 131 * rank)
@@ -215,16 +222,18 @@ class Runner:
         if self.gemm:
             if prof:
                 record_event(self.gev[k][0])
-            self.head_gemm(self.gemm["hidden"][k % len(self.gemm["hidden"])], self.bufs[0])
+            self.head_gemm(self.gemm["hidden"][k % len(self.gemm["hidden"])])
             if prof:
                 record_event(self.gev[k][1])
         S.select_step(self.bufs[k % len(self.bufs)], self.xt, self.k, self.c, self.lp, self.sched,
                       self.q, seed=1234, offset=k, out=self.out,
                       prof_events=self.ev[k] if prof else None, **self.kw)
 
-    def head_gemm(self, hidden, logits):
-        """logits = hidden @ weight.T (cuBLAS bf16, fp32 accumulation)."""
-        torch.mm(hidden, self.gemm["weight"].t(), out=logits.view(-1, logits.shape[-1]))
+    def head_gemm(self, hidden):
+        """logits = hidden @ weight.T (cuBLAS bf16, fp32 accumulation) into the
+        padded buffer; returns the (B*2, L, V) logits view."""
+        torch.mm(hidden, self.gemm["weight"].t(), out=self.gemm["out"])
+        return self.bufs[0]
 
     def rows_per_step(self):
         """Sampled positions per step index, from one eager block."""
@@ -479,11 +488,12 @@ def run_ours(args, ws, rank, local):
         }
         if gemm:
             h = gemm["hidden"][0]
-            flop = 2.0 * h.shape[0] * h.shape[1] * inp.V
+            flop = 2.0 * h.shape[0] * h.shape[1] * inp.V  # useful flops (V columns)
             gm = sum(gemm_ms) / K
             line["config"].update({
                 "workload": f"config4 (unfused): cuBLAS bf16 head GEMM [{h.shape[0]} x {h.shape[1]}] x "
-                            f"[{inp.V} x {h.shape[1]}]^T -> bf16 logits, then the select step; "
+                            f"[{inp.V} x {h.shape[1]}]^T (weight zero-padded to {LOGIT_PAD} rows) -> "
+                            f"bf16 logits rows of stride {LOGIT_PAD}, then the select step; "
                             f"{inp.B} requests x 2 CFG rows x {inp.L} positions, {K}-step blocks",
                 "gemm_ms_per_step": gm, "gemm_tflops": flop / (gm * 1e-3) / 1e12,
                 "l2": f"{N_HIDDEN} rotating hidden-state buffers ({N_HIDDEN * h.numel() * 2 / 1e6:.0f} MB) "
@@ -505,7 +515,7 @@ def run_e2e(R, inp, dev, steps):
         dhid = torch.empty_like(R.gemm["hidden"][0])
     else:
         pin = [b.cpu().pin_memory() for b in R.bufs[:2]]
-    dlog = torch.empty_like(R.bufs[0])
+    dlog = None if R.gemm else torch.empty(R.bufs[0].shape, dtype=R.bufs[0].dtype, device=dev)
     hx = R.xt0.cpu().pin_memory()
     hk = R.k0.cpu().pin_memory()
     hc = R.c0.cpu().pin_memory()
@@ -529,13 +539,14 @@ def run_e2e(R, inp, dev, steps):
         rows = 2 * int(((hx == inp.mask_id) & ~hc[:, None]).sum())
         if R.gemm:
             dhid.copy_(pin[i % 2], non_blocking=True)
-            R.head_gemm(dhid, dlog)
+            logits = R.head_gemm(dhid)
         else:
             dlog.copy_(pin[i % 2], non_blocking=True)
+            logits = dlog
         dx.copy_(hx, non_blocking=True)
         dk.copy_(hk, non_blocking=True)
         dc.copy_(hc, non_blocking=True)
-        S.select_step(dlog, dx, dk, dc, R.lp, R.sched, R.q, seed=99, offset=k, out=out, **R.kw)
+        S.select_step(logits, dx, dk, dc, R.lp, R.sched, R.q, seed=99, offset=k, out=out, **R.kw)
         ox.copy_(dx, non_blocking=True)
         ok_.copy_(dk, non_blocking=True)
         oc.copy_(dc, non_blocking=True)

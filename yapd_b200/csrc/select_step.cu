@@ -2955,6 +2955,7 @@ __device__ __forceinline__ bool w_position(const SampleParams& P, WSmem& ws, con
   float dm = kNegInf, W = kNegInf, mg_min = kBig;
   unsigned long long ovf = 0ull;  // marked vectors the stash could not take
   int nst = 0;                    // stash entries (warp-uniform)
+  bool sfull = false;             // a compaction freed little: the stash stays as it is
   bool first_vec = true;
   for (int q = tm.r; q < I.nch; q += tm.T) {
     // after an expired wait nothing more is read (the chunks still count as
@@ -3064,7 +3065,7 @@ __device__ __forceinline__ bool w_position(const SampleParams& P, WSmem& ws, con
       if (lane >= o) incl += y;
     }
     const int tot = __shfl_sync(0xffffffffu, incl, 31);
-    if (nst + tot > WCfg::STASH && nst > 0) {
+    if (nst + tot > WCfg::STASH && nst > 0 && !sfull) {
       // the running maximum has risen: drop the entries now below it
       const int ns = min(nst, WCfg::STASH);
       uint4 ec[2], eu[2];
@@ -3098,6 +3099,8 @@ __device__ __forceinline__ bool w_position(const SampleParams& P, WSmem& ws, con
       }
       __syncwarp();
       nst = __popc(kb0) + __popc(kb1);  // entries past STASH stay in the overflow marks
+      // (a wide band: compacting again would free as little)
+      sfull = nst > WCfg::STASH - WCfg::STASH / 4;
     }
     int at = nst + incl - cnt;
     nst += tot;

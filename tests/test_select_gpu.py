@@ -205,3 +205,15 @@ def test_lmhead_logits_config4(noise, masked):
     # of tokens, so every position takes the wide-band path
     inp = make_config(4, seed=21, B=4, masked=masked, explicit_noise=(noise == "explicit"))
     check(inp, noise=noise, seed=5, offset=2, dense=(masked == "all"))
+
+
+@pytest.mark.parametrize("top_p,min_p,noise", [(0.95, 0.05, "explicit"), (0.95, 0.05, "philox"),
+                                               (1.0, 0.02, "explicit"), (0.3, 0.05, "explicit")])
+def test_lmhead_wide_bands_one_warp_teams(top_p, min_p, noise):
+    # 2560 positions, so every CTA holds more items than warps and each
+    # position has a warp of its own: bands of hundreds of members take the
+    # warp's wide min-p path when top-p cannot cut them (0.95, 1.0) and are
+    # deferred when it can (0.3)
+    inp = make_config(4, seed=31, B=80, masked="all", explicit_noise=(noise == "explicit"))
+    inp = _uniform(inp, temperature=0.8, top_k=0, top_p=top_p, min_p=min_p, rep=1.2)
+    check(inp, noise=noise, seed=11, offset=4, dense=True)

@@ -56,8 +56,8 @@ struct KCfg {
   // ahead of the barrier (a parity wait would then pass at once).
   static_assert(NSTAGE % NG == 0, "the groups must divide the stages");
 };
-using CfgBF16 = KCfg<128, 3, 8, 2, 6>;
-using CfgF32 = KCfg<96, 3, 4, 4, 3>;
+using CfgBF16 = KCfg<224, 2, 8, 2, 6>;
+using CfgF32 = KCfg<480, 1, 4, 4, 3>;
 
 // Thread index within its group, and the group index.
 template <class C>

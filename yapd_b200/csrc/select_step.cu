@@ -946,6 +946,8 @@ __device__ __noinline__ int argmax_smem(const SampleParams& P, const PosCtx X, c
                                         float band_lo, unsigned long long Xcomp, const ScoreCtx& K, Pick bp, Smem<C>& sm) {
   csync<C>();  // out-of-line reductions use scratch slots 2/3
   int slot = 2;
+  // nothing outside the band can be kept: the band's pick stands
+  if (H >= kBig && !(band_lo < H)) return block_pick<C>(bp, K.turbo, sm, slot);
   const int V = P.V;
   constexpr int NC = 4;
   float best = kNegInf;
@@ -1428,8 +1430,16 @@ __device__ __noinline__ int select_cold(const SampleParams& P, const PosCtx X, c
       bracket_smem<C>(X, R, V, false, (float)topk_raw, (float)topk_raw, -kBig, (float)V, lo, hi, sm);
     csync<C>();
     const float blo = __fsub_rn(lo, zmargin(lo)), bhi = __fadd_rn(hi, zmargin(hi));
-    bk = band_smem<C>(P, X, R, blo, bhi, sm);
+    // a small k: the whole top-k set (everything from the boundary band up)
+    // in the sorted list when it fits, so that top-k, top-p and min-p are
+    // all decided on it and no pass over the row is left for the sample
+    const bool whole = topk_raw <= C::BAND - 16;
+    bk = band_smem<C>(P, X, R, blo, whole ? kBig : bhi, sm);
     csync<C>();
+    if (whole && bk.overflow) {
+      bk = band_smem<C>(P, X, R, blo, bhi, sm);
+      csync<C>();
+    }
     if (bk.overflow) {
       float Sk;
       Xcomp = overflow_resolve<C>(P, X, R, blo, bhi, bk.n_above, bk.m_above, true, topk_raw,

@@ -903,24 +903,6 @@ __device__ __forceinline__ int block_pick(const Pick& bp, bool turbo, Smem<C>& s
   return 0x7fffffff - (int)(uint32_t)w2;
 }
 
-// Gumbel noise of tokens v4 .. v4+3 (v4 a multiple of 4): one Philox block,
-// whose four words are the four tokens' words, or the explicit tensor.
-__device__ __forceinline__ void noise4(const SampleParams& P, const ScoreCtx& K, int v4, float (&g)[4]) {
-  if (P.noise_kind == YAPD_NOISE_EXPLICIT) {
-    const float* row = P.gumbel_tok + (int64_t)K.b * P.gt_stride_req + (int64_t)K.l * P.gt_stride_pos;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) g[i] = v4 + i < P.V ? __ldg(row + v4 + i) : 0.f;
-    return;
-  }
-  const Philox4 r = philox4x32_10((uint32_t)v4 >> 2, (uint32_t)K.pos, (uint32_t)P.offset,
-                                  (uint32_t)(P.offset >> 32) & 0x7fffffffu, (uint32_t)P.seed,
-                                  (uint32_t)(P.seed >> 32));
-  g[0] = gumbel_from_uniform(uniform_from_word(r.x));
-  g[1] = gumbel_from_uniform(uniform_from_word(r.y));
-  g[2] = gumbel_from_uniform(uniform_from_word(r.z));
-  g[3] = gumbel_from_uniform(uniform_from_word(r.w));
-}
-
 // History bits of tokens v4 .. v4+3 (bit i: token v4 + i).
 __device__ __forceinline__ unsigned hist4(const SampleParams& P, int b, int v4) {
   if (P.history_kind == YAPD_HISTORY_BITMAP) {
@@ -932,6 +914,33 @@ __device__ __forceinline__ unsigned hist4(const SampleParams& P, int b, int v4) 
 #pragma unroll
   for (int i = 0; i < 4; ++i) m |= (v4 + i < P.V && __ldg(h + v4 + i) != 0) ? (1u << i) : 0u;
   return m;
+}
+
+// The Gumbel noise of the tokens v4 + i with bit i of `keep` set (v4 a
+// multiple of 4): one Philox block, the logarithms only for those tokens
+// (one at a time, so a warp pays for the most any lane keeps, not for four).
+__device__ __forceinline__ void noise4_kept(const SampleParams& P, const ScoreCtx& K, int v4, unsigned keep,
+                                            float (&g)[4]) {
+  if (P.noise_kind == YAPD_NOISE_EXPLICIT) {
+    const float* row = P.gumbel_tok + (int64_t)K.b * P.gt_stride_req + (int64_t)K.l * P.gt_stride_pos;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) g[i] = ((keep >> i) & 1u) ? __ldg(row + v4 + i) : 0.f;
+    return;
+  }
+  const Philox4 r = philox4x32_10((uint32_t)v4 >> 2, (uint32_t)K.pos, (uint32_t)P.offset,
+                                  (uint32_t)(P.offset >> 32) & 0x7fffffffu, (uint32_t)P.seed,
+                                  (uint32_t)(P.seed >> 32));
+  g[0] = g[1] = g[2] = g[3] = 0.f;
+  while (keep) {
+    const int i = __ffs(keep) - 1;
+    keep &= keep - 1u;
+    const uint32_t w = i == 0 ? r.x : i == 1 ? r.y : i == 2 ? r.z : r.w;
+    const float gi = gumbel_from_uniform(uniform_from_word(w));
+    g[0] = i == 0 ? gi : g[0];
+    g[1] = i == 1 ? gi : g[1];
+    g[2] = i == 2 ? gi : g[2];
+    g[3] = i == 3 ? gi : g[3];
+  }
 }
 
 // Cold argmax from the staged rows: elements with z2 >= H are kept (min-p
@@ -969,7 +978,7 @@ __device__ __noinline__ int argmax_smem(const SampleParams& P, const PosCtx X, c
     }
     if (!keep) continue;
     float g[4] = {0.f, 0.f, 0.f, 0.f};
-    if (K.noisy) noise4(P, K, v4, g);
+    if (K.noisy) noise4_kept(P, K, v4, keep, g);
     const unsigned hb = K.pen_on ? hist4(P, K.b, v4) : 0u;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {

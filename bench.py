@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the block-diffusion select step: logit rows/sec at V = 8194.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 1|2|3|4]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 1|2|3|4|5]
 
 One *step* is one select step (m8than/yapd ``server/engine.py:533-612``) over one
 GPU's batch: configuration 1 by default (64 requests x 2 CFG rows x 32 positions
@@ -16,6 +16,11 @@ Configuration 4 puts the speech LM head in front of the step: each step first
 multiplies the hidden states (512 requests x 2 x 32 rows of 1024, bf16) by the
 head weight (8194 x 1024) with cuBLAS into a bf16 logits buffer (the unfused
 form, ``server/engine.py:517-520``), then runs the select step on it.
+
+Configuration 5 ("turbo") times the Turbo engine's autoregressive sampler
+(``server/engine_ar.py:220-243``) through ``sample_rows``: 256 active rows x
+V = 6563 fp32 logits, the engine defaults T 0.8, top-k 1000, top-p 0.95,
+repetition penalty 1.2 (``server/engine_ar.py:140-146``); one step = one call.
 
 Under ``torchrun`` each rank runs its own request shard (weak scaling, no
 per-step collective); ranks gather their committed tokens with one NCCL
@@ -58,7 +63,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=8000)
     ap.add_argument("--warmup", type=int, default=16)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3, 4])
+    ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3, 4, 5])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=16)
@@ -139,7 +144,7 @@ class ClockSampler:
 # ------------------------------------------------------------------ workload
 
 def config_name(cfg: int) -> str:
-    return {1: "config1", 2: "config2", 3: "config3", 4: "config4"}[cfg]
+    return {1: "config1", 2: "config2", 3: "config3", 4: "config4", 5: "turbo"}[cfg]
 
 
 N_HIDDEN = 3  # rotating hidden-state buffers of config 4 (3 x 64 MB > L2)
@@ -359,6 +364,8 @@ def cpu_sample(cfg: int, seconds: float, B_s: int = 2):
 def run_reference(args, ws, rank):
     if ws > 1 and rank != 0:
         return
+    if args.config == 5:
+        return run_reference_turbo(args)
     B_s = 4
     from oracle import select_oracle as O
     torch.set_num_threads(os.cpu_count() or 1)
@@ -575,11 +582,204 @@ def run_e2e(R, inp, dev, steps):
     return {"ms": ms, "rows": rows, "h2d": h2d, "d2h": d2h}
 
 
+TURBO_ROWS, TURBO_V, TURBO_BUFS = 256, 6563, 24  # 24 x 6.7 MB of logits > L2
+TURBO_METRIC = "logit rows/sec at V=6563 (Turbo sampler)"
+
+
+def turbo_inputs(seed: int, R: int = TURBO_ROWS):
+    """Turbo rows: logits ~ N(0, 2) with three tokens per row +8 (as the
+    block configurations), a 2% bool history, the engine's default parameters."""
+    g = torch.Generator().manual_seed(seed)
+    logits = WL.make_logits(g, R, 1, TURBO_V).view(R, TURBO_V)
+    seen = torch.rand(R, TURBO_V, generator=g) < 0.02
+    prm = dict(temperature=torch.full((R,), 0.8), top_k=torch.full((R,), 1000, dtype=torch.int32),
+               top_p=torch.full((R,), 0.95), min_p=torch.zeros(R), rep_penalty=torch.full((R,), 1.2))
+    return logits, seen, prm
+
+
+def turbo_oracle_step(logits, seen, prm, i: int):
+    """One Turbo step on the host (the oracle's chain of server/engine_ar.py:220-243)."""
+    from oracle import select_oracle as O
+    R = logits.shape[0]
+    G = O.gumbel_from_uniform(torch.rand(R, TURBO_V, generator=torch.Generator().manual_seed(i)))
+    return O.sample_tokens(logits, prm["temperature"], prm["top_k"], prm["top_p"], prm["min_p"],
+                           prm["rep_penalty"], seen, G, zero_temp="unscaled")
+
+
+def run_turbo(args, ws, rank, local):
+    """Configuration 5 on each rank (weak scaling): sample_rows over the
+    engine's active rows, one call (one kernel launch) per step."""
+    dist = dist_init(ws, local)
+    dev = torch.device("cuda", local)
+    logits, seen, prm = turbo_inputs(100 + rank)
+    gd = torch.Generator(device=dev).manual_seed(7 + rank)
+    bufs = [logits.to(dev)] + [torch.randn(logits.shape, generator=gd, device=dev) * 2.0
+                               for _ in range(TURBO_BUFS - 1)]
+    kw = {k: v.to(dev) for k, v in prm.items()}
+    seen_d = seen.to(dev)
+    out = torch.empty(TURBO_ROWS, dtype=torch.int32, device=dev)
+
+    def call(i, x):
+        S.sample_rows(x, seen=seen_d, seed=1234, offset=i, out=out, zero_temp_greedy=False, **kw)
+
+    for i in range(3):
+        call(i, bufs[i])
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        call(0, bufs[0])
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(TURBO_BUFS):
+            call(i, bufs[i])
+    reps = max(1, args.steps // TURBO_BUFS)
+    steps = reps * TURBO_BUFS
+    for _ in range(max(1, -(-args.warmup // TURBO_BUFS))):
+        g.replay()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    ck = clocks.stop()
+    # kernel time per launch: events around single calls (one launch each)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(TURBO_BUFS)]
+    for i in range(TURBO_BUFS):
+        ev[i][0].record()
+        call(i, bufs[i])
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    kern_ms = sum(a.elapsed_time(b) for a, b in ev) / TURBO_BUFS
+    if dist:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+    rows_all = float(TURBO_ROWS * steps * ws)
+    value = rows_all / (ms * 1e-3)
+    # end to end: logits from pinned host memory, sampled ids back, every step
+    pin = [b.cpu().pin_memory() for b in bufs[:2]]
+    dl = torch.empty_like(bufs[0])
+    ho = torch.empty(TURBO_ROWS, dtype=torch.int32).pin_memory()
+    n_e2e = max(2, args.e2e_steps)
+
+    def tick(i):
+        dl.copy_(pin[i % 2], non_blocking=True)
+        call(i, dl)
+        ho.copy_(out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for i in range(2):
+        tick(i)
+    e0.record()
+    for i in range(n_e2e):
+        tick(i)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t[0])
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        cpu = turbo_cpu(args.cpu_seconds)
+    if rank == 0:
+        peak, peak_kind = roofline_peak()
+        # logits in, sampled ids out (the bool history is read per candidate only)
+        byt = TURBO_ROWS * TURBO_V * 4 + TURBO_ROWS * 4
+        ach = byt / (kern_ms * 1e-3) / 1e9
+        line = {
+            "metric": TURBO_METRIC, "value": value, "unit": "rows/s",
+            "n_gpus": ws, "steps": steps, "warmup": args.warmup, "ms_per_step": ms / steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": f"turbo: sample_rows over {TURBO_ROWS} rows x V={TURBO_V} fp32, T 0.8, "
+                                   f"top-k 1000, top-p 0.95, rep 1.2 (server/engine_ar.py:220-243)",
+                       "global_batch": TURBO_ROWS * ws, "parallelism": f"request-sharded x{ws}",
+                       "l2": f"{TURBO_BUFS} rotating logits buffers "
+                             f"({TURBO_BUFS * bufs[0].numel() * 4 / 1e6:.0f} MB) > L2",
+                       "noise": "in-kernel Philox4x32-10 Gumbel"},
+            "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
+                         "frac": ach / peak, "traffic": None, "peak_kind": peak_kind,
+                         "kernel": "sample_kernel", "kernel_ms_per_launch": kern_ms,
+                         "bytes_per_launch": byt},
+            "e2e": {"value": TURBO_ROWS * ws * n_e2e / (e2e_ms * 1e-3), "unit": "rows/s",
+                    "h2d_bytes_per_step": bufs[0].numel() * 4, "d2h_bytes_per_step": TURBO_ROWS * 4},
+            "gpu_launches": steps, "clocks": ck, "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if dist:
+        del g
+        dist.destroy_process_group()
+
+
+def turbo_cpu(seconds: float, R: int = 16):
+    """The Turbo chain on the host cores (oracle port) on a bounded sample."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    logits, seen, prm = turbo_inputs(999, R)
+    turbo_oracle_step(logits, seen, prm, 0)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        turbo_oracle_step(logits, seen, prm, n)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return {"value": R * n / el, "unit": "rows/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{R} Turbo rows per call, {n} calls in {el:.1f} s (torch CPU oracle of "
+                      f"server/engine_ar.py:220-243)"}
+
+
+def run_reference_turbo(args, R: int = 16):
+    """The reference arm of configuration 5: the Turbo chain on the host cores
+    (oracle port), R rows per step."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    logits, seen, prm = turbo_inputs(999, R)
+    for i in range(args.warmup):
+        turbo_oracle_step(logits, seen, prm, i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        turbo_oracle_step(logits, seen, prm, i)
+    el = time.perf_counter() - t0
+    v = R * args.steps / el
+    cb = {"value": v, "unit": "rows/s", "cores": torch.get_num_threads(), "kind": "port",
+          "sample": f"{R} Turbo rows per step (torch CPU oracle of server/engine_ar.py:220-243)"}
+    print(json.dumps({"metric": TURBO_METRIC, "value": v, "unit": "rows/s",
+                      "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+                      "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+                      "config": {"workload": f"turbo (CPU sample, {R} rows)", "parallelism": "host cores"},
+                      "cpu_baseline": cb,
+                      "e2e": {"value": v, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+          flush=True)
+
+
 def main():
     args = parse()
     ws, rank, local = dist_env()
     if args.impl == "reference":
         run_reference(args, ws, rank)
+        return
+    if args.config == 5:
+        run_turbo(args, ws, rank, local)
         return
     run_ours(args, ws, rank, local)
 

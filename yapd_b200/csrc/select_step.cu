@@ -58,6 +58,10 @@ struct KCfg {
 };
 using CfgBF16 = KCfg<224, 2, 8, 2, 6>;
 using CfgF32 = KCfg<480, 1, 4, 4, 3>;
+// fp32 rows without CFG (the Turbo sampler, yapd_sample_rows): one row per
+// group, two groups per CTA; a call holds few rows per SM, so two rows in
+// flight beat one wider group
+using CfgF32R = KCfg<224, 2, 4, 4, 2>;
 
 // Thread index within its group, and the group index.
 template <class C>
@@ -3490,7 +3494,8 @@ template <class C>
 constexpr size_t smem_bytes() {
   return sizeof(KSmem<C>) + 128;
 }
-static_assert(smem_bytes<CfgBF16>() <= 227 * 1024 && smem_bytes<CfgF32>() <= 227 * 1024,
+static_assert(smem_bytes<CfgBF16>() <= 227 * 1024 && smem_bytes<CfgF32>() <= 227 * 1024 &&
+                  smem_bytes<CfgF32R>() <= 227 * 1024,
               "the grouped pipeline's shared memory fits one SM");
 
 static_assert(sizeof(WSmem) + 128 <= 227 * 1024, "the warp kernel's shared memory fits one SM");
@@ -3539,7 +3544,7 @@ static int device_info(DevInfo** out) {
     int rc = prepare_kernel<CfgBF16, true>(&d.occ[1][1]);
     if (rc == YAPD_OK) rc = prepare_kernel<CfgBF16, false>(&d.occ[1][0]);
     if (rc == YAPD_OK) rc = prepare_kernel<CfgF32, true>(&d.occ[0][1]);
-    if (rc == YAPD_OK) rc = prepare_kernel<CfgF32, false>(&d.occ[0][0]);
+    if (rc == YAPD_OK) rc = prepare_kernel<CfgF32R, false>(&d.occ[0][0]);
     if (rc == YAPD_OK) rc = prepare_wkernel<true>();
     if (rc == YAPD_OK) rc = prepare_wkernel<false>();
     // the state update runs between two sample kernels: the same shared-memory
@@ -3613,7 +3618,7 @@ static int launch_sample(const SampleParams& P, int dtype, int max_items, cudaSt
     else launch_one<CfgBF16, false>(P, occ, d->sms, max_items, st);
   } else {
     if (cfg) launch_one<CfgF32, true>(P, occ, d->sms, max_items, st);
-    else launch_one<CfgF32, false>(P, occ, d->sms, max_items, st);
+    else launch_one<CfgF32R, false>(P, occ, d->sms, max_items, st);
   }
   return cudaGetLastError() == cudaSuccess ? YAPD_OK : YAPD_ERR_LAUNCH;
 }

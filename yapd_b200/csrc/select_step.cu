@@ -856,7 +856,14 @@ struct ScoreCtx {
   bool pen_on, noisy, turbo, minp_on;
   float rep, rrep;
   float r, minp_thr;  // min-p: keep iff 2^(z2-zmax) * r >= minp_thr
+  const uint32_t* hbits;  // the request's history bitmap in shared memory, or null (global)
 };
+
+// Whether token v is in the request's history, from the shared-memory copy
+// of its bitmap when the caller staged one.
+__device__ __forceinline__ bool hist_bit_k(const SampleParams& P, const ScoreCtx& K, int v) {
+  return K.hbits ? ((K.hbits[v >> 5] >> (v & 31)) & 1u) != 0u : hist_bit(P, K.b, v);
+}
 
 // The memory-borne inputs of a token's score (history bit, noise), fetched
 // ahead of the arithmetic so that their latency overlaps other work.
@@ -867,7 +874,7 @@ struct ScoreIn {
 template <bool INL = false>
 __device__ __forceinline__ ScoreIn score_in(const SampleParams& P, const ScoreCtx& K, int v) {
   ScoreIn r;
-  r.hb = K.pen_on ? hist_bit(P, K.b, v) : false;
+  r.hb = K.pen_on ? hist_bit_k(P, K, v) : false;
   r.nz = K.noisy ? noise_at<INL>(P, K.b, K.pos, K.l, v) : 0.f;
   return r;
 }
@@ -887,7 +894,7 @@ template <class C>
 __device__ __forceinline__ float approx_score(const SampleParams& P, const PosCtx& X, const ScoreCtx& K, int v,
                                               float z) {
   float va = __fmaf_rn(z, kLn2, X.Kval);
-  if (K.pen_on && hist_bit(P, K.b, v)) va = va > 0.f ? __fmul_rn(va, K.rrep) : __fmul_rn(va, K.rep);
+  if (K.pen_on && hist_bit_k(P, K, v)) va = va > 0.f ? __fmul_rn(va, K.rrep) : __fmul_rn(va, K.rep);
   return K.noisy ? __fadd_rn(va, noise_at(P, K.b, K.pos, K.l, v)) : va;
 }
 
@@ -1527,8 +1534,15 @@ struct Smem {
   float2 cpc[32];             // PMI inputs of the first 32 band members
   float cscore[32];           // their exact scores (penalty + noise)
   unsigned char cflag[C::BAND];
-  int hc[kHistBins];          // bracket histogram: counts ...
-  float hm[kHistBins];        // ... and masses 2^(z2 - zmax) per bin
+  alignas(16) int hc[kHistBins];    // bracket histogram: counts ...
+  union {
+    alignas(16) float hm[kHistBins];     // ... and masses 2^(z2 - zmax) per bin (select_cold)
+    alignas(16) uint32_t hq[kHistBins];  // ... or fixed-point masses (histogram select)
+  };
+  int hsi[8];                 // histogram select: the scan's crossings ...
+  float hsf[8];               // ... and its mass bounds
+  uint32_t hbits[(YAPD_MAX_V + 31) / 32];  // the position's history bitmap (histogram select)
+  int klist[C::NT];           // histogram select: ids of the tokens above band P (kept)
 };
 
 template <class C>
@@ -1930,6 +1944,7 @@ __device__ __forceinline__ void stats_rest(const SampleParams& P, const ItemPara
   K.rrep = K.pen_on ? __fdiv_rn(1.0f, Q.rep) : 1.0f;
   K.r = __fdiv_rn(1.0f, X.S);
   K.minp_thr = 0.f;
+  K.hbits = nullptr;
 }
 
 // The min-p band's ids, from the vectors pass 2 marked (and every scalar
@@ -1971,6 +1986,671 @@ __device__ __forceinline__ int band_collect(const PosCtx& X, const RowRef<C>& R,
   return h.n;
 }
 
+// ------------------------------------------------------------ histogram select
+//
+// Positions filtered by top-k and / or top-p (min-p off) take three passes
+// over their staged rows:
+//   1. the exact maxima of c, u and z2' = A2*c - B2*u;
+//   2. the sums of exp(c - max c), exp(u - max u) and 2^d, d = z2 - zmax,
+//      against those maxima, and a histogram of d by depth below zmax
+//      (kHistBins bins of 1/kHistPerUnit log2 unit: counts and fixed-point
+//      masses 2^d by shared-memory integer atomics).  One warp scans it for
+//      the bin where the count from the top reaches k, and the bins where the
+//      mass from the top reaches top_p times the bounds of S_k (the top-k
+//      mass) that bin gives, and lays out the bands;
+//   3. one collection pass: tokens of the crossing bins, widened by the float
+//      margin, go to the band lists with their exact values and masses;
+//      tokens above the top band (all kept) go to the kept list with their
+//      masses summed; tokens between the bands are not visited (their count
+//      and mass come from the histogram).
+// The kept tokens are then scored exactly (penalty, Philox noise), one per
+// thread; the bands are resolved as select_cold resolves its bands (rank by
+// (exact value, id), the top-k cut and S_k, top-p flags from double prefix
+// sums), their kept members are scored, and the best score wins.  On a
+// failed precondition (non-finite row, a crossing below the binned range, a
+// band larger than the list, a crossing the histogram misplaced) the function
+// writes nothing and returns false; the caller then takes the general cold
+// path.
+
+constexpr int kHistPerUnit = 8;  // kHistBins / kHistPerUnit = 64 log2 units of depth
+
+// Group maxima of three values (one barrier).
+template <class C>
+__device__ __forceinline__ void red_max3(float& a, float& b, float& c, Smem<C>& sm, int& slot) {
+  a = warp_max(a);
+  b = warp_max(b);
+  c = warp_max(c);
+  float* s = sm.red8 + slot * 8 * C::NW;
+  slot ^= 1;
+  if ((threadIdx.x & 31) == 0) {
+    s[gtid<C>() >> 5] = a;
+    s[C::NW + (gtid<C>() >> 5)] = b;
+    s[2 * C::NW + (gtid<C>() >> 5)] = c;
+  }
+  csync<C>();
+  float ra = s[0], rb = s[C::NW], rc = s[2 * C::NW];
+#pragma unroll
+  for (int q = 1; q < C::NW; ++q) {
+    ra = fmaxf(ra, s[q]);
+    rb = fmaxf(rb, s[C::NW + q]);
+    rc = fmaxf(rc, s[2 * C::NW + q]);
+  }
+  a = ra;
+  b = rb;
+  c = rc;
+}
+
+// Pass 1: this thread's maxima of c, u and z2' = A2*c - B2*u (NaN ignored).
+template <class C, bool CFG>
+__device__ __forceinline__ void hpass_max(const PosCtx& X, const RowRef<C>& R, const Span& S, float& mc, float& mu,
+                                          float& zm) {
+  const int tid = gtid<C>();
+  const float A2 = X.A2, nB2 = -X.B2;
+  float z0 = kNegInf, z1 = kNegInf;
+  if constexpr (C::BF16) {
+    uint32_t c2 = 0xff80ff80u, u2 = 0xff80ff80u;
+    const unsigned long long A2p = f2_pack(A2, A2), nB2p = f2_pack(nB2, nB2), zp = f2_pack(0.f, 0.f);
+#pragma unroll 2
+    for (int j = S.j0 + tid; j < S.j1; j += C::NT) {
+      const uint4 a = lds128(R.sc + j * 16);
+      c2 = bmax2(c2, bmax2(bmax2(a.x, a.y), bmax2(a.z, a.w)));
+      const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+      uint32_t qw[4] = {0u, 0u, 0u, 0u};
+      if (CFG) {
+        const uint4 q = lds128(R.su + j * 16);
+        u2 = bmax2(u2, bmax2(bmax2(q.x, q.y), bmax2(q.z, q.w)));
+        qw[0] = q.x;
+        qw[1] = q.y;
+        qw[2] = q.z;
+        qw[3] = q.w;
+      }
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const unsigned long long cx = f2_bf16(aw[t]);
+        const unsigned long long zx = CFG ? f2_fma(cx, A2p, f2_fma(f2_bf16(qw[t]), nB2p, zp)) : f2_fma(cx, A2p, zp);
+        float lo, hi;
+        f2_unpack(zx, lo, hi);
+        if (t & 1) z1 = fmax3(z1, lo, hi);
+        else z0 = fmax3(z0, lo, hi);
+      }
+    }
+    mc = fmaxf(bf16lo(c2), bf16hi(c2));
+    mu = CFG ? fmaxf(bf16lo(u2), bf16hi(u2)) : kNegInf;
+  } else {
+    float c0 = kNegInf, u0 = kNegInf;
+#pragma unroll 2
+    for (int j = S.j0 + tid; j < S.j1; j += C::NT) {
+      const uint4 a = lds128(R.sc + j * 16);
+      const float cv[4] = {__uint_as_float(a.x), __uint_as_float(a.y), __uint_as_float(a.z), __uint_as_float(a.w)};
+      c0 = fmax3(c0, cv[0], cv[1]);
+      c0 = fmax3(c0, cv[2], cv[3]);
+      float zz[4];
+      if (CFG) {
+        const uint4 q = lds128(R.su + j * 16);
+        const float uv[4] = {__uint_as_float(q.x), __uint_as_float(q.y), __uint_as_float(q.z), __uint_as_float(q.w)};
+        u0 = fmax3(u0, uv[0], uv[1]);
+        u0 = fmax3(u0, uv[2], uv[3]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) zz[i] = __fmaf_rn(cv[i], A2, __fmul_rn(uv[i], nB2));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) zz[i] = __fmul_rn(cv[i], A2);
+      }
+      z0 = fmax3(z0, zz[0], zz[1]);
+      z1 = fmax3(z1, zz[2], zz[3]);
+    }
+    mc = c0;
+    mu = CFG ? u0 : kNegInf;
+  }
+  for (int e = tid; e < S.nscal; e += C::NT) {
+    const int v = scalar_v(S, e);
+    const float c = load_elem_smem<C>(R.sc, R.gc, v);
+    mc = fmaxf(mc, c);
+    float z;
+    if (CFG) {
+      const float u = load_elem_smem<C>(R.su, R.gu, v);
+      mu = fmaxf(mu, u);
+      z = __fmaf_rn(c, A2, __fmul_rn(u, nB2));
+    } else {
+      z = __fmul_rn(c, A2);
+    }
+    z0 = fmaxf(z0, z);
+  }
+  zm = fmaxf(z0, z1);
+}
+
+// d = z2 - zmax of one token (the histogram select's key), from its logits.
+template <bool CFG>
+__device__ __forceinline__ float hdepth(const PosCtx& X, float K2mz, float c, float u) {
+  return CFG ? __fmaf_rn(c, X.A2, __fmaf_rn(u, -X.B2, K2mz)) : __fmaf_rn(c, X.A2, K2mz);
+}
+
+// Histogram bin of a depth d <= 0: j = rint(-kHistPerUnit * d), so bin j
+// holds d in (-(j + 1/2) / kHistPerUnit, -(j - 1/2) / kHistPerUnit]; -1 past
+// the binned range (and for non-finite d).  Rounding by the 1.5 * 2^23 shift
+// keeps the float-to-integer conversion off the conversion pipe.
+__device__ __forceinline__ int hist_bin(float d) {
+  const int j = __float_as_int(__fadd_rn(__fmul_rn(d, -(float)kHistPerUnit), 12582912.0f)) - 0x4B400000;
+  return j < kHistBins ? max(j, 0) : -1;
+}
+
+// A token's mass 2^d in the histogram's fixed point: rint(e * 2^(16 + o))
+// with o = j / kHistPerUnit its octave of depth, so that every member of a
+// bin weighs about 2^16 units (the scale is an exponent add, exact).  Shared
+// memory has no native float atomic add; two integer atomics per token cost
+// a third of one float atomic.
+__device__ __forceinline__ uint32_t hist_q(float e, int j) {
+  const float t = __int_as_float(__float_as_int(e) + ((16 + j / kHistPerUnit) << 23));
+  return (uint32_t)(__float_as_int(__fadd_rn(t, 12582912.0f)) - 0x4B400000);
+}
+__device__ __forceinline__ float hist_mass(uint32_t q, int j) {
+  return __fmul_rn((float)q, __int_as_float((127 - 16 - j / kHistPerUnit) << 23));
+}
+
+template <class C>
+__device__ __forceinline__ void hist_add(Smem<C>& sm, float d, float e) {
+  const int j = hist_bin(d);
+  if (j >= 0) {
+    atomicAdd(&sm.hc[j], 1);
+    atomicAdd(&sm.hq[j], hist_q(e, j));
+  }
+}
+
+// Pass 2: sums against the group maxima and the depth histogram.
+template <class C, bool CFG>
+__device__ __forceinline__ void hpass_sums(const PosCtx& X, const RowRef<C>& R, const Span& S, float K2mz,
+                                           float& sc, float& su, float& s, Smem<C>& sm) {
+  const int tid = gtid<C>();
+  const float nmcL = -__fmul_rn(X.mc, kLog2e), nmuL = CFG ? -__fmul_rn(X.mu, kLog2e) : 0.f;
+  float sc0 = 0.f, sc1 = 0.f, su0 = 0.f, su1 = 0.f, s0 = 0.f, s1 = 0.f;
+  if constexpr (C::BF16) {
+    const unsigned long long L2p = f2_pack(kLog2e, kLog2e), A2p = f2_pack(X.A2, X.A2),
+                             nB2p = f2_pack(-X.B2, -X.B2), Kp = f2_pack(K2mz, K2mz);
+    const unsigned long long nmcLp = f2_pack(nmcL, nmcL), nmuLp = f2_pack(nmuL, nmuL);
+    unsigned long long scp = f2_pack(0.f, 0.f), sup = scp, sp = scp;
+    for (int j = S.j0 + tid; j < S.j1; j += C::NT) {
+      const uint4 a = lds128(R.sc + j * 16);
+      uint4 q = a;
+      if (CFG) q = lds128(R.su + j * 16);
+      const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+      const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const unsigned long long cx = f2_bf16(aw[t]);
+        unsigned long long dx;
+        float lo, hi;
+        if (CFG) {
+          const unsigned long long ux = f2_bf16(qw[t]);
+          dx = f2_fma(cx, A2p, f2_fma(ux, nB2p, Kp));
+          f2_unpack(f2_fma(ux, L2p, nmuLp), lo, hi);
+          sup = f2_add(sup, f2_pack(ex2_approx(lo), ex2_approx(hi)));
+        } else {
+          dx = f2_fma(cx, A2p, Kp);
+        }
+        f2_unpack(f2_fma(cx, L2p, nmcLp), lo, hi);
+        scp = f2_add(scp, f2_pack(ex2_approx(lo), ex2_approx(hi)));
+        f2_unpack(dx, lo, hi);
+        const float elo = ex2_approx(lo), ehi = ex2_approx(hi);
+        sp = f2_add(sp, f2_pack(elo, ehi));
+        hist_add<C>(sm, lo, elo);
+        hist_add<C>(sm, hi, ehi);
+      }
+    }
+    f2_unpack(scp, sc0, sc1);
+    f2_unpack(sup, su0, su1);
+    f2_unpack(sp, s0, s1);
+  } else {
+    for (int j = S.j0 + tid; j < S.j1; j += C::NT) {
+      const uint4 a = lds128(R.sc + j * 16);
+      uint4 q = a;
+      if (CFG) q = lds128(R.su + j * 16);
+#pragma unroll
+      for (int i = 0; i < C::W; ++i) {
+        const float c = velem<C>(a, i);
+        const float u = CFG ? velem<C>(q, i) : 0.f;
+        const float d = hdepth<CFG>(X, K2mz, c, u);
+        const float e = ex2_approx(d);
+        if (i & 1) {
+          sc1 += ex2_approx(__fmaf_rn(c, kLog2e, nmcL));
+          if (CFG) su1 += ex2_approx(__fmaf_rn(u, kLog2e, nmuL));
+          s1 += e;
+        } else {
+          sc0 += ex2_approx(__fmaf_rn(c, kLog2e, nmcL));
+          if (CFG) su0 += ex2_approx(__fmaf_rn(u, kLog2e, nmuL));
+          s0 += e;
+        }
+        hist_add<C>(sm, d, e);
+      }
+    }
+  }
+  for (int e = tid; e < S.nscal; e += C::NT) {
+    const int v = scalar_v(S, e);
+    const float c = load_elem_smem<C>(R.sc, R.gc, v);
+    const float u = CFG ? load_elem_smem<C>(R.su, R.gu, v) : 0.f;
+    sc0 += ex2_approx(__fmaf_rn(c, kLog2e, nmcL));
+    if (CFG) su0 += ex2_approx(__fmaf_rn(u, kLog2e, nmuL));
+    const float d = hdepth<CFG>(X, K2mz, c, u);
+    const float ed = ex2_approx(d);
+    s0 += ed;
+    hist_add<C>(sm, d, ed);
+  }
+  sc = sc0 + sc1;
+  su = su0 + su1;
+  s = s0 + s1;
+}
+
+// The scan (the group's first warp; lane l owns bins [l*PER, l*PER + PER),
+// bin 0 the top).  Finds the bin jk where the count from the top reaches k,
+// the bins jp1 <= jp2 where the mass from the top reaches the lower / upper
+// top-p target (top_p times the bounds of S_k that bin jk gives, or times
+// S_all), and lays out the bands: band P = bins [ja, jb] (the top-p
+// crossing, merged with jk when they touch; jk alone without top-p) and, when
+// jk lies further down, band K = bin jk with the bins between them summed.
+// sm.hsi: [0] ok, [1] ja, [2] jb, [3] jk, [4] sep, [5] count between;
+// sm.hsf: [0] mass between.
+template <class C>
+__device__ __forceinline__ void hist_scan(Smem<C>& sm, bool topk_on, int k, bool topp_on, float top_p, float S_all) {
+  constexpr int PER = kHistBins / 32;
+  const int lane = threadIdx.x & 31;
+  int cnt[PER];
+  float ms[PER];
+#pragma unroll
+  for (int q = 0; q < PER / 4; ++q) {
+    const int4 c4 = reinterpret_cast<const int4*>(sm.hc + lane * PER)[q];
+    const uint4 m4 = reinterpret_cast<const uint4*>(sm.hq + lane * PER)[q];
+    cnt[4 * q] = c4.x;
+    cnt[4 * q + 1] = c4.y;
+    cnt[4 * q + 2] = c4.z;
+    cnt[4 * q + 3] = c4.w;
+    const int j0 = lane * PER + 4 * q;
+    ms[4 * q] = hist_mass(m4.x, j0);
+    ms[4 * q + 1] = hist_mass(m4.y, j0 + 1);
+    ms[4 * q + 2] = hist_mass(m4.z, j0 + 2);
+    ms[4 * q + 3] = hist_mass(m4.w, j0 + 3);
+  }
+  int segc = 0;
+  float segm = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    segc += cnt[i];
+    segm += ms[i];
+  }
+  int pc = segc;
+  float pm = segm;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int yc = __shfl_up_sync(0xffffffffu, pc, o);
+    const float ym = __shfl_up_sync(0xffffffffu, pm, o);
+    if (lane >= o) {
+      pc += yc;
+      pm += ym;
+    }
+  }
+  const int basec = pc - segc;
+  const float basem = __fsub_rn(pm, segm);
+  bool ok = true;
+  int jk = -1;
+  float slo = S_all, shi = S_all;
+  if (topk_on) {
+    int c = basec, my = -1;
+    float m = basem, mex = 0.f, minc = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int c2 = c + cnt[i];
+      const float m2 = m + ms[i];
+      if (my < 0 && c2 >= k) {
+        my = lane * PER + i;
+        mex = m;
+        minc = m2;
+      }
+      c = c2;
+      m = m2;
+    }
+    const unsigned bk = __ballot_sync(0xffffffffu, my >= 0);
+    if (!bk) {
+      ok = false;  // the k-th token lies below the binned range
+    } else {
+      const int sl = __ffs(bk) - 1;
+      jk = __shfl_sync(0xffffffffu, my, sl);
+      slo = __shfl_sync(0xffffffffu, mex, sl);
+      shi = __shfl_sync(0xffffffffu, minc, sl);
+    }
+  }
+  int ja = jk, jb = jk;
+  if (ok && topp_on) {
+    // the fixed-point masses are exact to about 2^-16 per token: 1e-4 slack
+    const float tlo = __fmul_rn(__fmul_rn(top_p, slo), 0.9999f);
+    const float thi = __fmul_rn(__fmul_rn(top_p, shi), 1.0001f);
+    int a1 = -1, a2 = -1;
+    float m = basem;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const float m2 = m + ms[i];
+      if (a1 < 0 && m2 >= tlo) a1 = lane * PER + i;
+      if (a2 < 0 && m2 >= thi) a2 = lane * PER + i;
+      m = m2;
+    }
+    const unsigned b1 = __ballot_sync(0xffffffffu, a1 >= 0), b2 = __ballot_sync(0xffffffffu, a2 >= 0);
+    if (!b1) {
+      ok = false;
+    } else {
+      ja = __shfl_sync(0xffffffffu, a1, __ffs(b1) - 1);
+      jb = b2 ? __shfl_sync(0xffffffffu, a2, __ffs(b2) - 1) : -1;
+      if (topk_on) {
+        // the top-p cut never lies below the k-th token
+        if (jb < 0 || jb > jk) jb = jk;
+        if (ja > jk) ja = jk;
+      } else if (jb < 0) {
+        ok = false;
+      }
+    }
+  }
+  const bool sep = ok && topp_on && topk_on && jk > jb + 1;
+  if (ok && topp_on && topk_on && !sep) jb = jk;
+  // tokens of the bins strictly between band P and band K
+  int nbt = 0;
+  float mbt = 0.f;
+  if (sep) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int j = lane * PER + i;
+      const bool in = j > jb && j < jk;
+      nbt += in ? cnt[i] : 0;
+      mbt += in ? ms[i] : 0.f;
+    }
+    nbt = warp_sum_i(nbt);
+    mbt = warp_sum(mbt);
+  }
+  if (lane == 0) {
+    sm.hsi[0] = ok ? 1 : 0;
+    sm.hsi[1] = ja;
+    sm.hsi[2] = jb;
+    sm.hsi[3] = jk;
+    sm.hsi[4] = sep ? 1 : 0;
+    sm.hsi[5] = nbt;
+    sm.hsf[0] = mbt;
+    sm.misc[0] = 0;  // band and kept-list counters of pass 3
+    sm.misc[1] = 0;
+    sm.misc[2] = 0;
+  }
+}
+
+template <class C, bool CFG>
+__device__ __noinline__ bool select_hist(const SampleParams& P, const ItemParams Q, const RowRef<C> R, const Span S,
+                                         Smem<C>& sm) {
+  csync<C>();  // out-of-line reductions use scratch slots 2/3
+  int slot = 2;
+  const int tid = gtid<C>();
+  const int V = P.V;
+  const float kPosInf = __int_as_float(0x7f800000);
+  const bool topk_on = Q.top_k > 0 && Q.top_k < V;
+  const bool topp_on = Q.top_p < 1.0f;
+  PosCtx X;
+  float sA;
+  item_ctx<CFG>(P, Q, X, sA);
+  for (int i = tid; i < kHistBins; i += C::NT) {
+    sm.hc[i] = 0;
+    sm.hq[i] = 0u;
+  }
+  // the request's history bitmap, read once into shared memory (the kept
+  // tokens' penalty tests then cost no global round trip)
+  const bool stage_hist = P.history_kind == YAPD_HISTORY_BITMAP && P.history != nullptr && Q.rep != 1.0f;
+  if (stage_hist) {
+    const uint32_t* h = reinterpret_cast<const uint32_t*>(P.history) + (int64_t)(Q.pos / P.L) * P.history_stride;
+    for (int i = tid; i < (V + 31) / 32; i += C::NT) sm.hbits[i] = __ldg(h + i);
+  }
+  // ---- pass 1: group maxima ----
+  float mc, mu, zm;
+  hpass_max<C, CFG>(X, R, S, mc, mu, zm);
+  red_max3<C>(mc, mu, zm, sm, slot);
+  if (!(mc > kNegInf && mc < kPosInf) || (CFG && !(mu > kNegInf && mu < kPosInf)) ||
+      !(zm > kNegInf && zm < kPosInf))
+    return false;
+  // ---- pass 2: sums and the depth histogram ----
+  X.mc = mc;
+  X.mu = CFG ? mu : 0.f;
+  X.K2 = CFG ? __fmaf_rn(-mc, X.A2, __fmul_rn(mu, X.B2)) : __fmul_rn(-mc, X.A2);
+  const float zmax = __fadd_rn(zm, X.K2);
+  const float K2mz = __fsub_rn(X.K2, zmax);
+  float sums[8];
+  hpass_sums<C, CFG>(X, R, S, K2mz, sums[0], sums[1], sums[2], sm);
+#pragma unroll
+  for (int j = 3; j < 8; ++j) sums[j] = 0.f;
+  block_sum8<C>(sums, sm, slot);
+  {
+    const float m3[3] = {mc, CFG ? mu : kNegInf, zm};
+    const float s3[3] = {sums[0], sums[1], sums[2]};
+    stats_core<CFG>(m3, s3, X);
+  }
+  if (!(X.Sc == X.Sc) || !(X.Sc > 0.f) || (CFG && !(X.Su == X.Su && X.Su > 0.f)) || !(X.S == X.S) ||
+      !(X.S > 0.f))
+    return false;
+  ScoreCtx K;
+  stats_rest<CFG>(P, Q, sA, X, K);
+  if (stage_hist) K.hbits = sm.hbits;
+  // ---- the scan ----
+  if (tid < 32) hist_scan<C>(sm, topk_on, Q.top_k, topp_on, Q.top_p, X.S);
+  csync<C>();
+  if (!sm.hsi[0]) return false;
+  const int ja = sm.hsi[1], jb = sm.hsi[2], jk = sm.hsi[3];
+  const bool sep = sm.hsi[4] != 0;
+  const float n_bins_between = (float)sm.hsi[5];
+  const float m_bins_between = sm.hsf[0];
+  // bin edges in d, widened by the float margin of z2 against the exact values
+  auto edge = [&](float jh, bool upper) {
+    const float d = __fmul_rn(-jh, 1.0f / (float)kHistPerUnit);
+    const float m = zmargin(__fadd_rn(zmax, d));
+    return upper ? __fadd_rn(d, m) : __fsub_rn(d, m);
+  };
+  const float dH = edge((float)ja - 0.5f, true);     // above band P: kept
+  const float dPl = edge((float)jb + 0.5f, false);   // band P: [dPl, dH)
+  const float dKh = sep ? edge((float)jk - 0.5f, true) : dPl;
+  const float dKl = sep ? edge((float)jk + 0.5f, false) : dPl;  // band K: [dKl, dKh)
+  // ---- pass 3: the bands, the kept set's candidates ----
+  // (tokens between the bands are not visited: their count and mass come from
+  // the histogram, less the band members that sit in those bins)
+  float n_above = 0.f, m_above = 0.f, m_bandP = 0.f, n_corr = 0.f, m_corr = 0.f;
+  auto visit = [&](int v) {
+    const float c = load_elem_smem<C>(R.sc, R.gc, v);
+    const float u = CFG ? load_elem_smem<C>(R.su, R.gu, v) : 0.f;
+    const float d = hdepth<CFG>(X, K2mz, c, u);
+    const float e = ex2_approx(d);
+    if (d >= dH) {
+      // kept: scored after the pass, one token per thread
+      n_above += 1.f;
+      m_above += e;
+      const int at = atomicAdd(&sm.misc[2], 1);
+      if (at < C::NT) sm.klist[at] = v;
+      return;
+    }
+    const bool inP = d >= dPl;
+    if (!inP && !(d >= dKl && d < dKh)) return;
+    if (sep) {
+      // members in the bins strictly between the bands
+      const int j = hist_bin(d);
+      if (j > jb && j < jk) {
+        n_corr += 1.f;
+        m_corr += e;
+      }
+    }
+    if (inP) {
+      m_bandP += e;
+      const int at = atomicAdd(&sm.misc[0], 1);
+      if (at < C::BAND) {
+        sm.cand[at] = cand_key(exact_val_cu(P, X, c, u), v);
+        sm.cande[at] = e;
+      }
+    } else {
+      const int at = atomicAdd(&sm.misc[1], 1);
+      const int idx = C::BAND - 1 - at;
+      if (idx >= 0) {
+        sm.cand[idx] = cand_key(exact_val_cu(P, X, c, u), v);
+        sm.cande[idx] = e;
+      }
+    }
+  };
+  // d in band K <=> |d - cK| < hK (never true without band K)
+  const float cK = __fmul_rn(0.5f, __fadd_rn(dKl, dKh)), hK = sep ? __fmul_rn(0.5f, __fsub_rn(dKh, dKl)) : -1.f;
+  auto wanted = [&](float d) { return d >= dPl || fabsf(__fsub_rn(d, cK)) <= hK; };
+  if constexpr (C::BF16) {
+    const unsigned long long A2p = f2_pack(X.A2, X.A2), nB2p = f2_pack(-X.B2, -X.B2), Kp = f2_pack(K2mz, K2mz);
+    const float dLow = sep ? dKl : dPl;
+    for (int j = S.j0 + tid; j < S.j1; j += C::NT) {
+      const uint4 a = lds128(R.sc + j * 16);
+      uint4 q = a;
+      if (CFG) q = lds128(R.su + j * 16);
+      const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+      const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+      float dd[8];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const unsigned long long cx = f2_bf16(aw[t]);
+        const unsigned long long dx = CFG ? f2_fma(cx, A2p, f2_fma(f2_bf16(qw[t]), nB2p, Kp)) : f2_fma(cx, A2p, Kp);
+        f2_unpack(dx, dd[2 * t], dd[2 * t + 1]);
+      }
+      const float vm = fmaxf(fmax3(fmax3(dd[0], dd[1], dd[2]), dd[3], dd[4]), fmax3(dd[5], dd[6], dd[7]));
+      if (!(vm >= dLow)) continue;
+      uint32_t m = 0u;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) m |= (wanted(dd[i]) ? 1u : 0u) << i;
+      const int v0 = j * C::W - S.head;
+      while (m) {
+        const int i = __ffs(m) - 1;
+        m &= m - 1u;
+        visit(v0 + i);
+      }
+    }
+  } else {
+    for (int j = S.j0 + tid; j < S.j1; j += C::NT) {
+      const uint4 a = lds128(R.sc + j * 16);
+      uint4 q = a;
+      if (CFG) q = lds128(R.su + j * 16);
+      uint32_t m = 0u;
+#pragma unroll
+      for (int i = 0; i < C::W; ++i) {
+        const float d = hdepth<CFG>(X, K2mz, velem<C>(a, i), CFG ? velem<C>(q, i) : 0.f);
+        m |= (wanted(d) ? 1u : 0u) << i;
+      }
+      const int v0 = j * C::W - S.head;
+      while (m) {
+        const int i = __ffs(m) - 1;
+        m &= m - 1u;
+        visit(v0 + i);
+      }
+    }
+  }
+  for (int e = tid; e < S.nscal; e += C::NT) {
+    const int v = scalar_v(S, e);
+    const float c = load_elem_smem<C>(R.sc, R.gc, v);
+    const float u = CFG ? load_elem_smem<C>(R.su, R.gu, v) : 0.f;
+    if (wanted(hdepth<CFG>(X, K2mz, c, u))) visit(v);
+  }
+  float acc[8] = {n_above, m_above, m_bandP, n_corr, m_corr, 0.f, 0.f, 0.f};
+  block_sum8<C>(acc, sm, slot);
+  n_above = acc[0];
+  m_above = acc[1];
+  m_bandP = acc[2];
+  const float n_between = n_bins_between - acc[3];
+  const float m_between = __fsub_rn(m_bins_between, acc[4]);
+  const int nP = sm.misc[0], nK = sm.misc[1], nA = sm.misc[2];
+  if (nP + nK > C::BAND || nP == 0 || (sep && nK == 0)) return false;
+  // exact scores of the kept tokens above the bands (they do not depend on
+  // the band resolution below)
+  Pick bp{kNegInf, kNegInf, 0x7fffffff};
+  auto score_tok = [&](int v) {
+    const float vals = exact_val<C>(P, X, R, v);
+    const float es = exact_score<C>(P, K, v, vals);
+    const Pick cand{es, vals, v};
+    if (es == es && es > kNegInf && pick_better(cand, bp, K.turbo)) bp = cand;
+  };
+  if (nA <= C::NT) {
+    for (int q = tid; q < nA; q += C::NT) score_tok(sm.klist[q]);
+  } else {
+    // more kept tokens than the list holds: every thread scores its own
+    for (int j = S.j0 + tid; j < S.j1; j += C::NT) {
+      const int v0 = j * C::W - S.head;
+#pragma unroll 1
+      for (int i = 0; i < C::W; ++i) {
+        const int v = v0 + i;
+        const float c = load_elem_smem<C>(R.sc, R.gc, v);
+        const float u = CFG ? load_elem_smem<C>(R.su, R.gu, v) : 0.f;
+        if (hdepth<CFG>(X, K2mz, c, u) >= dH) score_tok(v);
+      }
+    }
+    for (int e = tid; e < S.nscal; e += C::NT) {
+      const int v = scalar_v(S, e);
+      const float c = load_elem_smem<C>(R.sc, R.gc, v);
+      const float u = CFG ? load_elem_smem<C>(R.su, R.gu, v) : 0.f;
+      if (hdepth<CFG>(X, K2mz, c, u) >= dH) score_tok(v);
+    }
+  }
+  // ---- exact resolution of the bands ----
+  float Sk = X.S;
+  int k_left = 0;
+  bool use_k = false;
+  if (sep) {
+    // S_k: everything above band K plus its first k - n_above members by (exact value, id)
+    const int kl = Q.top_k - (int)(n_above + (float)nP + n_between);
+    if (kl < 1 || kl > nK) return false;
+    float part = 0.f;
+    for (int q = tid; q < nK; q += C::NT) {
+      const unsigned long long key = sm.cand[C::BAND - 1 - q];
+      int rank = 0;
+      for (int j2 = 0; j2 < nK; ++j2) rank += (sm.cand[C::BAND - 1 - j2] > key) ? 1 : 0;
+      if (rank < kl) part += sm.cande[C::BAND - 1 - q];
+    }
+    Sk = __fadd_rn(__fadd_rn(__fadd_rn(m_above, m_bandP), fmaxf(m_between, 0.f)), block_sum1<C>(part, sm, slot));
+  } else if (topk_on) {
+    k_left = Q.top_k - (int)n_above;
+    if (k_left < 1 || k_left > nP) return false;
+    use_k = true;
+  }
+  rank_sort<C>(nP, sm);
+  if (use_k) {
+    float part = 0.f;
+    for (int q = tid; q < nP && q < k_left; q += C::NT) part += sm.cande[q];
+    Sk = __fadd_rn(m_above, block_sum1<C>(part, sm, slot));
+  }
+  K.r = __fdiv_rn(1.0f, Sk);
+  Band bd;
+  bd.n = nP;
+  bd.H = 0.f;
+  bd.n_above = n_above;
+  bd.m_above = m_above;
+  bd.overflow = false;
+  band_flags<C>(bd, use_k, k_left, topp_on, Q.top_p, K.r, false, 0.f, sm);
+  if (topp_on) {
+    // the top-p crossing must lie inside band P: its first member kept and,
+    // when tokens below the band belong to the top-k set, the band's mass
+    // reaching top_p (every token below it then dropped)
+    const bool below = sep || !topk_on;
+    const bool bad = !sm.cflag[0];
+    if (!bad && below && tid < 32) {
+      double t = 0.0;
+      for (int q = tid; q < nP; q += 32) t += (double)__fmul_rn(sm.cande[q], K.r);
+      t = warp_sum_d(t) + (double)m_above * (double)K.r;
+      if (tid == 0) sm.hsi[6] = ((float)t >= Q.top_p) ? 0 : 1;
+    }
+    csync<C>();
+    if (bad || (below && sm.hsi[6])) return false;
+  }
+  // ---- the best kept score: flagged band members and the kept tokens ----
+  {
+    const Pick b2 = band_pick<C>(P, K, nP, sm);
+    if (pick_better(b2, bp, K.turbo)) bp = b2;
+  }
+  int chosen = block_pick<C>(bp, K.turbo, sm, slot);
+  if (chosen < 0) chosen = top1_smem<C>(P, X, R, sm);
+  if (tid == 0) {
+    if (chosen < 0 || chosen >= V) {
+      atomicOr(P.status, (unsigned)YAPD_STATUS_INTERNAL);
+      chosen = 0;
+    }
+    write_choice<C, CFG>(P, R, Q.pos, chosen, X.mc, X.Sc, X.mu, X.Su);
+  }
+  return true;
+}
+
 // One position worked by a group: statistics, group merge, and either the
 // whole token choice with the outputs, or (a min-p band of at most 32
 // members) the hand-off record for the group's tail warp.
@@ -1996,6 +2676,9 @@ __device__ __forceinline__ void compute_item(const SampleParams& P, KSmem<C>& ks
     h.n = 0;
     h.handed = 0;
   }
+  // top-k / top-p without min-p: the histogram select (three passes)
+  if ((topk_on || topp_on) && !minp_on && !(topp_on && !(Q.top_p > 0.0f)))
+    if (select_hist<C, CFG>(P, Q, R, S, sm)) return;
 
   // ---- pass 1: this thread's maxima ----
   float mc_t, mu_t, nu_t;

@@ -3,14 +3,25 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 1|2|3|4|5]
 
-One *step* is one select step (m8than/yapd ``server/engine.py:533-612``) over one
-GPU's batch: configuration 1 by default (64 requests x 2 CFG rows x 32 positions
-x V = 8194 bf16 logits, T 0.8, top-p 0.95, min-p 0.05, repetition penalty 1.2
-over a 256-token history, Philox Gumbel noise), run as 8-step diffusion blocks:
-the block state (masked positions, step counter, commit flag) evolves through
-the kernel's own outputs and is reset at each block start.  A logit row is
-counted when the step must read it (masked position of a non-commit request),
-the metric of the reference's tick.
+One *step* is one select step (m8than/yapd ``server/engine.py:533-622``) over one
+GPU's batch.  The default is configuration 3, the metric's 1/2/4/8-GPU
+workload: 256 requests per GPU x 2 CFG rows x 32 positions x V = 8194 bf16
+logits with per-request parameters (T in [0.5, 1.2], top-k in {0, 50, 200,
+1000}, top-p in [0.8, 1], repetition penalty in [1, 1.5] over histories of
+0-2048 tokens), Philox Gumbel noise.  Configuration 1 is 64 requests with
+uniform parameters (T 0.8, top-p 0.95, min-p 0.05, penalty 1.2), configuration
+2 is configuration 3 with fp32 logits.
+
+The batch runs as the engine runs it, continuous batching through the
+engine's own buffers: each request's tokens live in a token buffer, every step
+samples the masked positions of the requests that are denoising, unmasks,
+writes the block back and moves the requests that were committing to their
+next block (the library does all of it in its two kernels).  The requests start
+staggered (configurations 2 and 3: U{1..32} masked positions and a random step
+counter each), so the batch stays ragged.  A logit row is counted when the step
+must read it (masked position of a non-commit request), the metric of the
+reference's tick; the line also carries the dense figure (every position
+sampled, as the reference's tick reads all of them).
 
 Configuration 4 puts the speech LM head in front of the step: each step first
 multiplies the hidden states (512 requests x 2 x 32 rows of 1024, bf16) by the
@@ -63,7 +74,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=8000)
     ap.add_argument("--warmup", type=int, default=16)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3, 4, 5])
+    ap.add_argument("--config", type=int, default=3, choices=[1, 2, 3, 4, 5])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=16)
@@ -172,7 +183,8 @@ def make_inputs(cfg: int, rank: int, device):
         gemm = {"hidden": hid, "weight": wp, "out": out}
         logits = out.view(inp.logits.shape[0], inp.logits.shape[1], LOGIT_PAD)[:, :, : inp.V]
         return inp, [logits], gemm
-    inp = WL.make_config(cfg, seed=100 + rank, explicit_noise=False)
+    inp = WL.make_config(cfg, seed=100 + rank, explicit_noise=False,
+                         masked="ragged" if cfg in (2, 3) else "all")
     g = torch.Generator(device=device).manual_seed(7 + 131 * rank)
     bufs = [inp.logits.to(device)]
     for _ in range(N_BUFFERS - 1):
@@ -184,19 +196,41 @@ def make_inputs(cfg: int, rank: int, device):
 
 
 class Runner:
-    """Eight captured graphs, one per diffusion step of a block."""
+    """Continuous batching through the engine buffers, as FlashEngine runs it
+    (``server/engine.py:491-622``): each request's tokens live in ``xt_full``;
+    a step gathers every request's current block in the kernels, samples its
+    masked positions (non-commit requests), unmasks, writes the block back and
+    moves the requests that were committing to their next, fully masked block.
+    The requests start staggered (configurations 2 and 3: U{1..32} masked
+    positions and a random step counter each), so the batch stays ragged.
+    ``G`` graphs (Philox offsets 0..G-1, rotating logits buffers) are replayed
+    in turn; a device counter accumulates the sampled positions."""
 
-    def __init__(self, inp, bufs, device, gemm=None):
+    G = 8
+
+    def __init__(self, inp, bufs, device, total_steps: int, gemm=None):
         self.inp, self.bufs, self.dev, self.gemm = inp, bufs, device, gemm
         B, L = inp.B, inp.L
-        self.xt0 = torch.full((B, L), inp.mask_id, dtype=torch.int64, device=device)
-        self.k0 = torch.zeros(B, dtype=torch.int64, device=device)
-        self.c0 = torch.zeros(B, dtype=torch.bool, device=device)
-        self.xt = self.xt0.clone()
-        self.k = self.k0.clone()
-        self.c = self.c0.clone()
+        # enough blocks that no request reaches the end of its buffer: a block
+        # takes at most K denoising ticks and one commit tick
+        n_blocks = total_steps // (inp.num_steps + 1) + 4
+        self.n_blocks = n_blocks
+        xt_full = torch.full((B, n_blocks * L), inp.mask_id, dtype=torch.int64)
+        xt_full[:, :L] = inp.xt
+        self.state0 = dict(xt_full=xt_full, k=inp.k_step.clone(), c=inp.is_commit.clone())
+        self.xt_full = xt_full.to(device)
+        self.k = inp.k_step.to(device).clone()
+        self.c = inp.is_commit.to(device).clone()
+        self.blk = torch.zeros(B, dtype=torch.int64, device=device)
+        self.cache = torch.zeros(B, dtype=torch.int64, device=device)
+        self.nsp = torch.full((B,), n_blocks * L, dtype=torch.int64, device=device)
+        self.flags = torch.zeros(B, 6, dtype=torch.int64, device=device)
+        self.count = torch.zeros(1, dtype=torch.int64, device=device)
+        self.eng = S.EngineBuffers(xt_full=self.xt_full, blk_start=self.blk, cache_len=self.cache,
+                                   n_speech=self.nsp, flags=self.flags, blk_limit=(n_blocks - 1) * L,
+                                   cache_limit=n_blocks * L)
         o = S.SelectOutputs.empty(B, L, device)
-        self.out = S.SelectOutputs(xt=self.xt, sampled=o.sampled, pmi=o.pmi, n_unmask=o.n_unmask,
+        self.out = S.SelectOutputs(xt=o.xt, sampled=o.sampled, pmi=o.pmi, n_unmask=o.n_unmask,
                                    n_mask_after=o.n_mask_after, hit_eos=o.hit_eos, k_step=self.k,
                                    is_commit=self.c)
         self.kw = dict(cfg_scale=inp.cfg_scale, mask_id=inp.mask_id, stop_id=inp.stop_id,
@@ -208,31 +242,37 @@ class Runner:
         self.lp = inp.log_prior.to(device)
         self.sched = inp.sched_t.to(device)
         self.q = inp.q_t.to(device)
-        self.K = inp.num_steps
+        self.L = L
         self.ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                   for _ in range(self.K)]
+                   for _ in range(self.G)]
         self.gev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                    for _ in range(self.K)] if gemm else None
+                    for _ in range(self.G)] if gemm else None
         for a, b in self.ev + (self.gev or []):  # torch creates the CUDA events lazily
             a.record()
             b.record()
         torch.cuda.synchronize()
-        self.graphs = []
+        self.graphs, self.pgraphs = [], []
+        self.dense_graph = None
 
-    def step(self, k: int, prof: bool = True):
-        if k == 0:
-            self.xt.copy_(self.xt0)
-            self.k.copy_(self.k0)
-            self.c.copy_(self.c0)
+    def restore(self):
+        """Back to the starting state (the same steps then replay identically)."""
+        self.xt_full.copy_(self.state0["xt_full"])
+        self.k.copy_(self.state0["k"])
+        self.c.copy_(self.state0["c"])
+        self.blk.zero_()
+        self.cache.zero_()
+
+    def step(self, k: int, prof: bool = True, dense: bool = False, logits=None):
         if self.gemm:
             if prof:
                 record_event(self.gev[k][0])
             self.head_gemm(self.gemm["hidden"][k % len(self.gemm["hidden"])])
             if prof:
                 record_event(self.gev[k][1])
-        S.select_step(self.bufs[k % len(self.bufs)], self.xt, self.k, self.c, self.lp, self.sched,
-                      self.q, seed=1234, offset=k, out=self.out,
-                      prof_events=self.ev[k] if prof else None, **self.kw)
+        S.select_step(self.bufs[k % len(self.bufs)] if logits is None else logits, None, self.k, self.c,
+                      self.lp, self.sched, self.q, seed=1234, offset=k, out=self.out, dense=dense,
+                      prof_events=self.ev[k] if prof else None, engine=self.eng, L=self.L,
+                      positions_sampled=self.count, **self.kw)
 
     def head_gemm(self, hidden):
         """logits = hidden @ weight.T (cuBLAS bf16, fp32 accumulation) into the
@@ -240,32 +280,19 @@ class Runner:
         torch.mm(hidden, self.gemm["weight"].t(), out=self.gemm["out"])
         return self.bufs[0]
 
-    def rows_per_step(self):
-        """Sampled positions per step index, from one eager block."""
-        pos = []
-        for k in range(self.K):
-            if k == 0:
-                masked = self.inp.B * self.inp.L
-            else:
-                masked = int(((self.xt == self.inp.mask_id) & ~self.c[:, None]).sum())
-            self.step(k, prof=False)
-            pos.append(masked)
-        torch.cuda.synchronize()
-        return pos
-
     def capture(self):
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
-            for k in range(self.K):
+            for k in range(self.G):
                 self.step(k)
+            self.step(0, prof=False, dense=True)
         torch.cuda.current_stream().wait_stream(s)
         torch.cuda.synchronize()
         # timed graphs carry no profiling events (an event between kernels adds
         # to the step); a second set records the sample kernel's duration for
-        # the roofline
-        self.pgraphs = []
-        for k in range(self.K):
+        # the roofline; one dense step (every position sampled)
+        for k in range(self.G):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 self.step(k, prof=False)
@@ -274,6 +301,12 @@ class Runner:
             with torch.cuda.graph(g):
                 self.step(k)
             self.pgraphs.append(g)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.step(0, prof=False, dense=True)
+        self.dense_graph = g
+        torch.cuda.synchronize()
+        self.restore()
         torch.cuda.synchronize()
 
 
@@ -337,11 +370,40 @@ def cpu_head(inp):
         inp.logits = WL.lmhead_logits_of(inp.meta["hidden"], inp.meta["weight"]).view(inp.logits.shape)
 
 
+def host_cpu() -> dict:
+    """The host CPU: model name, physical cores and logical CPUs."""
+    model, phys = None, set()
+    try:
+        cur = {}
+        for line in open("/proc/cpuinfo"):
+            if ":" not in line:
+                if cur:
+                    phys.add((cur.get("physical id", "0"), cur.get("core id", cur.get("processor"))))
+                cur = {}
+                continue
+            k, v = [x.strip() for x in line.split(":", 1)]
+            cur[k] = v
+            if k == "model name" and model is None:
+                model = v
+        if cur:
+            phys.add((cur.get("physical id", "0"), cur.get("core id", cur.get("processor"))))
+    except OSError:
+        pass
+    return {"cpu_model": model, "physical_cores": len(phys) or None, "logical_cpus": os.cpu_count()}
+
+
+def cpu_threads() -> int:
+    """Threads for the CPU arms: one per physical core."""
+    n = host_cpu()["physical_cores"] or os.cpu_count() or 1
+    torch.set_num_threads(n)
+    return n
+
+
 def cpu_sample(cfg: int, seconds: float, B_s: int = 2):
     """The CPU oracle (the reference algorithm, torch CPU, all host cores) on a
     bounded sample of the same workload: B_s requests, all positions masked."""
     from oracle import select_oracle as O
-    torch.set_num_threads(os.cpu_count() or 1)
+    cpu_threads()
     inp = WL.make_config(cfg, seed=999, B=B_s, explicit_noise=False)
     rows = 2 * inp.B * inp.L
     O.select_step(inp, noise="philox", seed=1, offset=0)
@@ -354,7 +416,7 @@ def cpu_sample(cfg: int, seconds: float, B_s: int = 2):
         if el >= seconds:
             break
     return {"value": rows * n / el, "unit": "rows/s", "cores": torch.get_num_threads(),
-            "kind": "port", "sample": f"{config_name(cfg)} shape with B={B_s} requests, all "
+            "kind": "port", **host_cpu(), "sample": f"{config_name(cfg)} shape with B={B_s} requests, all "
             f"{inp.L} positions masked, {n} steps in {el:.1f} s (torch CPU oracle"
             f"{', after the head GEMM' if cfg == 4 else ''})"}, el / n, rows
 
@@ -368,7 +430,7 @@ def run_reference(args, ws, rank):
         return run_reference_turbo(args)
     B_s = 4
     from oracle import select_oracle as O
-    torch.set_num_threads(os.cpu_count() or 1)
+    cpu_threads()
     inp = WL.make_config(args.config, seed=999, B=B_s, explicit_noise=False)
     rows = 2 * inp.B * inp.L
     for i in range(args.warmup):
@@ -380,7 +442,7 @@ def run_reference(args, ws, rank):
         O.select_step(inp, noise="philox", seed=1, offset=i)
     el = time.perf_counter() - t0
     v = rows * args.steps / el
-    cb = {"value": v, "unit": "rows/s", "cores": torch.get_num_threads(), "kind": "port",
+    cb = {"value": v, "unit": "rows/s", "cores": torch.get_num_threads(), "kind": "port", **host_cpu(),
           "sample": f"{config_name(args.config)} shape with B={B_s} requests per step, all positions "
                     f"masked (torch CPU oracle of server/engine.py:533-612"
                     f"{', after the head GEMM' if args.config == 4 else ''})"}
@@ -395,19 +457,24 @@ def run_reference(args, ws, rank):
     print(json.dumps(line), flush=True)
 
 
+def count_now(R) -> int:
+    torch.cuda.synchronize()
+    return int(R.count.item())
+
+
 def run_ours(args, ws, rank, local):
     dist = dist_init(ws, local)
     dev = torch.device("cuda", local)
     cfg = args.config
     inp, bufs, gemm = make_inputs(cfg, rank, dev)
-    R = Runner(inp, bufs, dev, gemm)
-    positions = R.rows_per_step()
+    total = args.warmup + args.steps + Runner.G + args.e2e_steps + 8
+    R = Runner(inp, bufs, dev, total, gemm)
     R.capture()
-    K = R.K
-    # warm-up
+    G = R.G
+    # warm-up (the state evolves: the timed steps see a running batch)
     for i in range(args.warmup):
-        R.graphs[i % K].replay()
-    torch.cuda.synchronize()
+        R.graphs[i % G].replay()
+    c0 = count_now(R)
     if dist:
         dist.barrier()
     clocks = ClockSampler(local)
@@ -420,45 +487,64 @@ def run_ours(args, ws, rank, local):
         dist.barrier()
     e0.record()
     for i in range(args.steps):
-        R.graphs[(args.warmup + i) % K].replay()
+        R.graphs[(args.warmup + i) % G].replay()
     e1.record()
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
     ms = e0.elapsed_time(e1)
     ck = clocks.stop()
-    # sample-kernel time of each step index: one block of the profiling graphs
-    # (run after the timed region; the same inputs and block states)
-    for k in range(K):
-        R.pgraphs[k].replay()
-    torch.cuda.synchronize()
-    kern_ms = [event_ms(*R.ev[k]) for k in range(K)]
-    gemm_ms = [event_ms(*R.gev[k]) for k in range(K)] if gemm else None
-    my_rows = sum(2 * positions[(args.warmup + i) % K] for i in range(args.steps))
-    byt = [algorithmic_bytes(inp, positions[k]) for k in range(K)]
-    achieved = sum(byt) / (sum(kern_ms) * 1e-3) / 1e9
+    my_pos = count_now(R) - c0
+    # sample-kernel time: one cycle of the profiling graphs, continuing the
+    # same running batch after the timed region
+    c1 = count_now(R)
+    for k in range(G):
+        R.pgraphs[(args.warmup + args.steps + k) % G].replay()
+    prof_pos = count_now(R) - c1
+    order = [(args.warmup + args.steps + k) % G for k in range(G)]
+    kern_ms = sum(event_ms(*R.ev[k]) for k in order)
+    gemm_ms = [event_ms(*R.gev[k]) for k in order] if gemm else None
+    byt = sum(algorithmic_bytes(inp, 0) for _ in range(G)) + (algorithmic_bytes(inp, prof_pos) -
+                                                               algorithmic_bytes(inp, 0))
+    achieved = byt / (kern_ms * 1e-3) / 1e9
+    # the dense figure: every position of every request sampled (the
+    # reference's tick reads all L positions, server/engine.py:533-550)
+    nd = max(4, min(32, args.steps // 4))
+    cd = count_now(R)
+    d0 = torch.cuda.Event(enable_timing=True)
+    d1 = torch.cuda.Event(enable_timing=True)
+    d0.record()
+    for _ in range(nd):
+        R.dense_graph.replay()
+    d1.record()
+    dense_pos = count_now(R) - cd
+    dense_ms = d0.elapsed_time(d1)
     if dist:
-        t = torch.tensor([ms, float(my_rows)], device=dev, dtype=torch.float64)
+        t = torch.tensor([ms, float(my_pos), dense_ms, float(dense_pos)], device=dev, dtype=torch.float64)
         mx = t.clone()
         dist.all_reduce(mx, op=dist.ReduceOp.MAX)
         sm_ = t.clone()
         dist.all_reduce(sm_, op=dist.ReduceOp.SUM)
-        ms_max, rows_all = float(mx[0]), float(sm_[1])
+        ms_max, pos_all = float(mx[0]), float(sm_[1])
+        dense_ms_max, dense_pos_all = float(mx[2]), float(sm_[3])
         # final gather of the committed block tokens (the only collective)
         from yapd_b200.shard import gather_committed
-        gather_committed(R.xt, R.xt.shape[0] * ws, dist)
+        gather_committed(R.out.xt, R.out.xt.shape[0] * ws, dist)
         torch.cuda.synchronize()
     else:
-        ms_max, rows_all = ms, float(my_rows)
+        ms_max, pos_all, dense_ms_max, dense_pos_all = ms, float(my_pos), dense_ms, float(dense_pos)
+    rows_all = 2.0 * pos_all
     value = rows_all / (ms_max * 1e-3)
 
     # ---- end to end through the public API with host buffers ----
     e2e = run_e2e(R, inp, dev, args.e2e_steps)
     if dist:
-        t = torch.tensor([e2e["ms"]], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t[0])
-        e2e_rows = rows_all / args.steps * args.e2e_steps
+        t = torch.tensor([e2e["ms"], float(e2e["rows"])], device=dev, dtype=torch.float64)
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm_ = t.clone()
+        dist.all_reduce(sm_, op=dist.ReduceOp.SUM)
+        e2e_ms, e2e_rows = float(mx[0]), float(sm_[1])
     else:
         e2e_ms, e2e_rows = e2e["ms"], e2e["rows"]
 
@@ -477,16 +563,23 @@ def run_ours(args, ws, rank, local):
             "data": "synthetic",
             "config": {
                 "workload": f"{config_name(cfg)}: {inp.B} requests x 2 CFG rows x {inp.L} positions x "
-                            f"V={inp.V} per GPU, {K}-step diffusion blocks, sparse (masked, non-commit) rows",
+                            f"V={inp.V} per GPU, continuous batching through the engine buffers "
+                            f"({inp.num_steps}-step blocks, requests staggered"
+                            f"{': U{1..32} masked and a random step counter at start' if cfg in (2, 3) else ''}), "
+                            f"rows of masked positions of non-commit requests",
                 "global_batch": inp.B * ws, "seq_len": inp.L, "parallelism": f"request-sharded x{ws}",
                 "l2": f"{N_BUFFERS} rotating logits buffers ({N_BUFFERS * inp.logits.numel() * inp.logits.element_size() / 1e6:.0f} MB) > L2",
                 "noise": "in-kernel Philox4x32-10 Gumbel",
                 "rows_per_step_mean": rows_all / args.steps / ws,
+                "dense": {"value": 2.0 * dense_pos_all / (dense_ms_max * 1e-3), "unit": "rows/s",
+                          "ms_per_step": dense_ms_max / nd,
+                          "note": "every position of every request sampled (the reference's tick)"},
             },
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
-                         "kernel": "wsample_kernel", "kernel_ms_per_launch": sum(kern_ms) / K,
-                         "bytes_per_launch": sum(byt) / K},
+                         "traffic_source": "profiles/traffic.json (ncu dram__bytes per launch, committed)",
+                         "kernel": "wsample_kernel" if inp.logits.dtype == torch.bfloat16 else "sample_kernel",
+                         "kernel_ms_per_launch": kern_ms / G, "bytes_per_launch": byt / G},
             "e2e": {"value": e2e_rows / (e2e_ms * 1e-3), "unit": "rows/s",
                     "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"]},
             "gpu_launches": LAUNCHES_PER_STEP * args.steps,
@@ -496,12 +589,12 @@ def run_ours(args, ws, rank, local):
         if gemm:
             h = gemm["hidden"][0]
             flop = 2.0 * h.shape[0] * h.shape[1] * inp.V  # useful flops (V columns)
-            gm = sum(gemm_ms) / K
+            gm = sum(gemm_ms) / G
             line["config"].update({
                 "workload": f"config4 (unfused): cuBLAS bf16 head GEMM [{h.shape[0]} x {h.shape[1]}] x "
                             f"[{inp.V} x {h.shape[1]}]^T (weight zero-padded to {LOGIT_PAD} rows) -> "
                             f"bf16 logits rows of stride {LOGIT_PAD}, then the select step; "
-                            f"{inp.B} requests x 2 CFG rows x {inp.L} positions, {K}-step blocks",
+                            f"{inp.B} requests x 2 CFG rows x {inp.L} positions, continuous batching",
                 "gemm_ms_per_step": gm, "gemm_tflops": flop / (gm * 1e-3) / 1e12,
                 "l2": f"{N_HIDDEN} rotating hidden-state buffers ({N_HIDDEN * h.numel() * 2 / 1e6:.0f} MB) "
                       f"and a {inp.logits.numel() * 2 / 1e6:.0f} MB logits buffer > L2"})
@@ -514,71 +607,45 @@ def run_ours(args, ws, rank, local):
 
 def run_e2e(R, inp, dev, steps):
     """Same metric through select_step with host buffers: every step copies its
-    logits and block state host->device and reads the new state back (the one
-    device->host sync of the engine tick, server/engine.py:635-636)."""
-    K = R.K
+    logits (configuration 4: its hidden states) from pinned host memory to the
+    device, runs the step on the engine's device-resident state, and reads back
+    the flags and the block tokens, the engine tick's one device-to-host sync
+    (server/engine.py:635-636)."""
     if R.gemm:
         pin = [h.cpu().pin_memory() for h in R.gemm["hidden"][:2]]
         dhid = torch.empty_like(R.gemm["hidden"][0])
     else:
         pin = [b.cpu().pin_memory() for b in R.bufs[:2]]
     dlog = None if R.gemm else torch.empty(R.bufs[0].shape, dtype=R.bufs[0].dtype, device=dev)
-    hx = R.xt0.cpu().pin_memory()
-    hk = R.k0.cpu().pin_memory()
-    hc = R.c0.cpu().pin_memory()
-    ox = torch.empty_like(hx).pin_memory()
-    ok_ = torch.empty_like(hk).pin_memory()
-    oc = torch.empty_like(hc).pin_memory()
-    on = torch.empty(inp.B, dtype=torch.int32).pin_memory()
-    oe = torch.empty(inp.B, dtype=torch.bool).pin_memory()
-    dx, dk, dc = R.xt0.clone(), R.k0.clone(), R.c0.clone()
-    o = S.SelectOutputs.empty(inp.B, inp.L, dev)
-    out = S.SelectOutputs(xt=dx, sampled=o.sampled, pmi=o.pmi, n_unmask=o.n_unmask,
-                          n_mask_after=o.n_mask_after, hit_eos=o.hit_eos, k_step=dk, is_commit=dc)
-    xt0 = R.xt0.cpu()
+    of = torch.empty(R.flags.shape, dtype=torch.int64).pin_memory()
+    ox = torch.empty(R.out.xt.shape, dtype=torch.int64).pin_memory()
 
     def tick(i):
-        k = i % K
-        if k == 0:
-            hx.copy_(xt0)
-            hk.zero_()
-            hc.zero_()
-        rows = 2 * int(((hx == inp.mask_id) & ~hc[:, None]).sum())
         if R.gemm:
             dhid.copy_(pin[i % 2], non_blocking=True)
             logits = R.head_gemm(dhid)
         else:
             dlog.copy_(pin[i % 2], non_blocking=True)
             logits = dlog
-        dx.copy_(hx, non_blocking=True)
-        dk.copy_(hk, non_blocking=True)
-        dc.copy_(hc, non_blocking=True)
-        S.select_step(logits, dx, dk, dc, R.lp, R.sched, R.q, seed=99, offset=k, out=out, **R.kw)
-        ox.copy_(dx, non_blocking=True)
-        ok_.copy_(dk, non_blocking=True)
-        oc.copy_(dc, non_blocking=True)
-        on.copy_(o.n_mask_after, non_blocking=True)
-        oe.copy_(o.hit_eos, non_blocking=True)
+        R.step(i % R.G, prof=False, logits=logits)
+        of.copy_(R.flags, non_blocking=True)
+        ox.copy_(R.out.xt, non_blocking=True)
         torch.cuda.current_stream().synchronize()
-        hx.copy_(ox)
-        hk.copy_(ok_)
-        hc.copy_(oc)
-        return rows
 
     for i in range(2):
         tick(i)
-    torch.cuda.synchronize()
+    c0 = count_now(R)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
-    rows = 0
     for i in range(steps):
-        rows += tick(i)
+        tick(i)
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
-    h2d = pin[0].numel() * pin[0].element_size() + hx.numel() * 8 + hk.numel() * 8 + hc.numel()
-    d2h = ox.numel() * 8 + ok_.numel() * 8 + oc.numel() + on.numel() * 4 + oe.numel()
+    rows = 2 * (count_now(R) - c0)
+    h2d = pin[0].numel() * pin[0].element_size()
+    d2h = of.numel() * 8 + ox.numel() * 8
     return {"ms": ms, "rows": rows, "h2d": h2d, "d2h": d2h}
 
 
@@ -733,7 +800,7 @@ def run_turbo(args, ws, rank, local):
 
 def turbo_cpu(seconds: float, R: int = 16):
     """The Turbo chain on the host cores (oracle port) on a bounded sample."""
-    torch.set_num_threads(os.cpu_count() or 1)
+    cpu_threads()
     logits, seen, prm = turbo_inputs(999, R)
     turbo_oracle_step(logits, seen, prm, 0)
     n, t0 = 0, time.perf_counter()
@@ -744,14 +811,14 @@ def turbo_cpu(seconds: float, R: int = 16):
         if el >= seconds:
             break
     return {"value": R * n / el, "unit": "rows/s", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{R} Turbo rows per call, {n} calls in {el:.1f} s (torch CPU oracle of "
+            **host_cpu(), "sample": f"{R} Turbo rows per call, {n} calls in {el:.1f} s (torch CPU oracle of "
                       f"server/engine_ar.py:220-243)"}
 
 
 def run_reference_turbo(args, R: int = 16):
     """The reference arm of configuration 5: the Turbo chain on the host cores
     (oracle port), R rows per step."""
-    torch.set_num_threads(os.cpu_count() or 1)
+    cpu_threads()
     logits, seen, prm = turbo_inputs(999, R)
     for i in range(args.warmup):
         turbo_oracle_step(logits, seen, prm, i)
@@ -760,7 +827,7 @@ def run_reference_turbo(args, R: int = 16):
         turbo_oracle_step(logits, seen, prm, i)
     el = time.perf_counter() - t0
     v = R * args.steps / el
-    cb = {"value": v, "unit": "rows/s", "cores": torch.get_num_threads(), "kind": "port",
+    cb = {"value": v, "unit": "rows/s", "cores": torch.get_num_threads(), "kind": "port", **host_cpu(),
           "sample": f"{R} Turbo rows per step (torch CPU oracle of server/engine_ar.py:220-243)"}
     print(json.dumps({"metric": TURBO_METRIC, "value": v, "unit": "rows/s",
                       "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,

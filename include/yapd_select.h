@@ -10,7 +10,8 @@
  *   calibrated PMI (server/engine.py:553-558, chatterbox_flash/calibration.py:
  *   39-82, cfg_guidance.py:50-57), position noise, the time-shifted quantile
  *   threshold and rank-based unmask (server/engine.py:559-593), and the
- *   per-request state update (server/engine.py:586-612).
+ *   per-request state update (server/engine.py:586-622, with the engine's
+ *   token buffer, cache / block offsets and flags when args->engine is set).
  *
  * A second entry point, yapd_sample_rows, is TurboEngine._sample
  * (server/engine_ar.py:220-243): one token per V-wide row, no CFG, no PMI.
@@ -33,7 +34,7 @@
 extern "C" {
 #endif
 
-#define YAPD_ABI_VERSION 1
+#define YAPD_ABI_VERSION 2
 
 /* Return codes (host-side validation; nothing is launched on error). */
 #define YAPD_OK 0
@@ -98,6 +99,29 @@ typedef struct yapd_noise {
 } yapd_noise;
 
 /*
+ * FlashEngine's whole-generation buffers (server/engine.py:493-497 gathers a
+ * request's block from them, :586-622 writes the step's result back).  With
+ * yapd_select_args.engine set, the state update also
+ *   - scatters xt_final into xt_full at the request's blk_start,
+ *   - advances cache_len and blk_start of the requests that were committing
+ *     (by L, clamped to cache_limit / blk_limit as the engine clamps them),
+ *   - writes the packed flags the engine reads back with its one host sync
+ *     (server/engine.py:614-622, 635).
+ * args->xt may then be NULL: the block is read from xt_full at blk_start.
+ */
+typedef struct yapd_engine_state {
+  int64_t* xt_full;          /* (B, xt_stride) all tokens of each request */
+  int64_t xt_stride;         /* elements between requests (>= blk_limit + L) */
+  int64_t* blk_start;        /* (B,) in / out */
+  int64_t* cache_len;        /* (B,) in / out */
+  const int64_t* n_speech;   /* (B,) copied into the flags */
+  int64_t blk_limit;         /* blk_start clamp: N_max - L */
+  int64_t cache_limit;       /* cache_len clamp: L_cache - L */
+  int64_t* flags;            /* (B, 6): was_commit, n_mask_after, hit_eos,
+                                k_step, blk_start, n_speech (after the step) */
+} yapd_engine_state;
+
+/*
  * yapd_select_args — one block-diffusion step over B requests.
  *
  * logits element (request b, branch r, position l, token v) lives at
@@ -112,7 +136,8 @@ typedef struct yapd_select_args {
   int32_t logits_dtype;         /* enum yapd_dtype */
   const void* logits;
   int64_t stride_req, stride_branch, stride_pos, logits_numel;
-  const int64_t* xt;            /* (B, L) block tokens */
+  const int64_t* xt;            /* (B, L) block tokens (NULL with engine:
+                                   read from engine->xt_full) */
   const int64_t* k_step;        /* (B,) */
   const uint8_t* is_commit;     /* (B,) bool */
   const float* log_prior;       /* (V,) log of the clamped prior */
@@ -143,6 +168,11 @@ typedef struct yapd_select_args {
    * kernel (the step's dominant kernel), for roofline timing; NULL = none */
   void* prof_event_begin;
   void* prof_event_end;
+  /* optional engine buffers (NULL: the caller keeps them) */
+  const yapd_engine_state* engine;
+  /* optional device counter: the step adds the number of positions it
+     samples (2 logit rows each with CFG), for throughput accounting */
+  int64_t* positions_sampled;
 } yapd_select_args;
 
 /* Rows for TurboEngine._sample: logits (R, V) with row stride `stride_row`. */
@@ -177,12 +207,13 @@ int yapd_clear_status(void* workspace, void* stream);
 int yapd_read_status(const void* workspace, void* stream, uint32_t* status_out);
 
 /*
- * One select step.  Replaces server/engine.py:533-612 (the select body and
+ * One select step.  Replaces server/engine.py:533-622 (the select body and
  * state update of FlashEngine._step_gpu, called from FlashEngine.tick at
- * server/engine.py:634); cache_len / blk_start advancement stays with the
- * caller.  Two kernel launches: token selection (which also builds the work
- * list and initialises the outputs of unsampled positions), then the
- * per-request state update.
+ * server/engine.py:634); with args->engine set it also writes xt_full,
+ * cache_len, blk_start and the flags, so the engine's tick is this call plus
+ * its one device-to-host copy.  Two kernel launches: token selection (which
+ * also builds the work list and initialises the outputs of unsampled
+ * positions), then the per-request state update.
  */
 int yapd_select_step(const yapd_select_args* args, void* stream);
 

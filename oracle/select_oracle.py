@@ -236,3 +236,22 @@ def select_step(inp, *, noise: str = "explicit", seed: int = 0, offset: int = 0,
                filtered=is_filtered(V, inp.top_k, inp.top_p, inp.min_p, inp.rep_penalty,
                                     inp.history is not None))
     return res
+
+def engine_update(res, xt_full, blk_start, cache_len, n_speech, is_commit, *, L: int,
+                  blk_limit: int, cache_limit: int):
+    """The engine-side write-back of ``server/engine.py:586-622`` after
+    ``unmask_select``: scatter ``xt_final`` into the token buffer at
+    ``blk_start``, advance the cache length and block start of the rows that
+    were committing (clamped), and pack the flags ``(B, 6)``.  Returns
+    ``(xt_full, blk_start, cache_len, flags)`` (new tensors)."""
+    B = blk_start.shape[0]
+    ar = torch.arange(L)
+    blk_idx = blk_start[:, None] + ar
+    xt_full = xt_full.clone()
+    xt_full[:B] = xt_full[:B].scatter(1, blk_idx, res["xt_final"])
+    adv = is_commit
+    cache_len = torch.where(adv, (cache_len + L).clamp(max=cache_limit), cache_len)
+    blk_start = torch.where(adv, (blk_start + L).clamp(max=blk_limit), blk_start)
+    flags = torch.stack([adv.long(), res["n_mask_after"].long(), res["hit_eos"].long(),
+                         res["k_step_final"].long(), blk_start, n_speech.long()], dim=1)
+    return xt_full, blk_start, cache_len, flags

@@ -30,7 +30,9 @@ def test_binding_matches_header():
     from yapd_b200 import _native as N
     assert set(N.EXPORTED) == set(declared_symbols())
     lib = N.lib()
-    assert lib.yapd_abi_version() == 1
+    assert lib.yapd_abi_version() == N.YAPD_ABI_VERSION
+    hdr = open(os.path.join(ROOT, "include", "yapd_select.h")).read()
+    assert re.search(r"#define YAPD_ABI_VERSION %d\b" % N.YAPD_ABI_VERSION, hdr)
     assert lib.yapd_select_workspace_size(64, 32) >= 64 * 32 * 4
     assert b"NULL" in lib.yapd_status_string(-1)
 
@@ -52,3 +54,34 @@ def test_host_validation_without_gpu():
     a.L = 33
     assert lib.yapd_select_step(C.byref(a), None) == -2          # L > 32
     assert lib.yapd_sample_rows(None, None) == -1
+
+
+def test_ctypes_layout_matches_c():
+    """The ctypes mirror of the argument structs has the C compiler's layout
+    (sizes and the offset of every field), checked with the host gcc."""
+    import ctypes as C
+    import shutil
+    import subprocess
+    import tempfile
+    from yapd_b200 import _native as N
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no host C compiler")
+    structs = {"yapd_sampling": N.Sampling, "yapd_noise": N.Noise, "yapd_engine_state": N.EngineState,
+               "yapd_select_args": N.SelectArgs, "yapd_sample_args": N.SampleArgs}
+    lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "yapd_select.h"', "int main(void) {"]
+    want = []
+    for cname, py in structs.items():
+        lines.append(f'printf("%zu\\n", sizeof({cname}));')
+        want.append(C.sizeof(py))
+        for fname, _ in py._fields_:
+            lines.append(f'printf("%zu\\n", offsetof({cname}, {fname}));')
+            want.append(getattr(py, fname).offset)
+    lines.append("return 0; }")
+    with tempfile.TemporaryDirectory() as d:
+        src = os.path.join(d, "layout.c")
+        exe = os.path.join(d, "layout")
+        open(src, "w").write("\n".join(lines))
+        subprocess.run([cc, "-I", os.path.join(ROOT, "include"), "-o", exe, src], check=True)
+        got = [int(x) for x in subprocess.run([exe], check=True, capture_output=True, text=True).stdout.split()]
+    assert got == want

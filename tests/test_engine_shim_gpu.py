@@ -54,6 +54,51 @@ def test_flash_select_shim():
     assert torch.equal(e.xt.cpu(), orc["xt_final"])
 
 
+@pytest.mark.parametrize("gather", [False, True])
+def test_engine_writeback(gather):
+    # the step writes the engine's token buffer, cache / block offsets and the
+    # packed flags (server/engine.py:586-622); with gather=True the kernels also
+    # read the block from the token buffer themselves (xt=None)
+    from yapd_b200.select import EngineBuffers, SelectOutputs, select_step
+    inp = make_config(2, seed=19, B=12, masked="ragged", explicit_noise=False, commit_frac=0.3)
+    dev = torch.device("cuda")
+    B, L = inp.B, inp.L
+    nblk = 5
+    g = torch.Generator().manual_seed(3)
+    blk = torch.randint(0, nblk, (B,), generator=g)
+    blk[0] = nblk - 1                       # a row at the last block: blk_start clamps
+    blk_start = blk * L
+    xt_full = torch.randint(0, 6561, (B, nblk * L), generator=g)
+    xt_full.scatter_(1, blk_start[:, None] + torch.arange(L), inp.xt)
+    cache_len = blk_start + 7
+    cache_len[1] = 10 * L                   # at the cache limit: clamps
+    n_speech = torch.randint(0, 500, (B,), generator=g)
+    eng = EngineBuffers(xt_full=xt_full.to(dev), blk_start=blk_start.to(dev), cache_len=cache_len.to(dev),
+                        n_speech=n_speech.to(dev), flags=torch.empty(B, 6, dtype=torch.int64, device=dev),
+                        blk_limit=(nblk - 1) * L, cache_limit=10 * L)
+    out = SelectOutputs.empty(B, L, dev)
+    select_step(inp.logits.to(dev), None if gather else inp.xt.to(dev), inp.k_step.to(dev),
+                inp.is_commit.to(dev), inp.log_prior.to(dev), inp.sched_t.to(dev), inp.q_t.to(dev),
+                cfg_scale=inp.cfg_scale, mask_id=inp.mask_id, stop_id=inp.stop_id,
+                temperature=inp.temperature.to(dev), top_k=inp.top_k.to(dev), top_p=inp.top_p.to(dev),
+                min_p=inp.min_p.to(dev), rep_penalty=inp.rep_penalty.to(dev),
+                history=inp.history_bitmap().to(dev), pmi_lambda=inp.pmi_lambda, seed=5, offset=1,
+                out=out, engine=eng, L=L)
+    torch.cuda.synchronize()
+    orc = O.select_step(inp, noise="philox", seed=5, offset=1)
+    gt, _ = O.philox_noise(5, 1, B, L, inp.V)
+    gpu = {k: getattr(out, k).cpu() for k in ("xt", "sampled", "pmi", "n_mask_after", "hit_eos", "k_step",
+                                              "is_commit")}
+    pos = (inp.xt == inp.mask_id) & ~inp.is_commit[:, None]
+    assert compare(inp, gpu, orc, gt, positions=pos) == 0
+    xf, bs, cl, fl = O.engine_update(orc, xt_full, blk_start, cache_len, n_speech, inp.is_commit, L=L,
+                                     blk_limit=(nblk - 1) * L, cache_limit=10 * L)
+    assert torch.equal(eng.xt_full.cpu(), xf)
+    assert torch.equal(eng.blk_start.cpu(), bs)
+    assert torch.equal(eng.cache_len.cpu(), cl)
+    assert torch.equal(eng.flags.cpu(), fl)
+
+
 def test_turbo_sample_shim():
     from yapd_b200.engine_shim import turbo_sample
     from oracle import philox

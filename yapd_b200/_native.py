@@ -20,6 +20,7 @@ YAPD_NOISE_PHILOX = 0
 YAPD_NOISE_EXPLICIT = 1
 YAPD_MAX_V = 8208
 YAPD_MAX_L = 32
+YAPD_ABI_VERSION = 2
 YAPD_STATUS_WAIT_TIMEOUT = 1
 YAPD_STATUS_INTERNAL = 2
 
@@ -50,6 +51,14 @@ class Noise(C.Structure):
     ]
 
 
+class EngineState(C.Structure):
+    _fields_ = [
+        ("xt_full", C.c_void_p), ("xt_stride", C.c_int64), ("blk_start", C.c_void_p),
+        ("cache_len", C.c_void_p), ("n_speech", C.c_void_p), ("blk_limit", C.c_int64),
+        ("cache_limit", C.c_int64), ("flags", C.c_void_p),
+    ]
+
+
 class SelectArgs(C.Structure):
     _fields_ = [
         ("B", C.c_int32), ("nb", C.c_int32), ("L", C.c_int32), ("V", C.c_int32), ("K", C.c_int32),
@@ -67,6 +76,7 @@ class SelectArgs(C.Structure):
         ("k_step_out", C.c_void_p), ("is_commit_out", C.c_void_p),
         ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
         ("prof_event_begin", C.c_void_p), ("prof_event_end", C.c_void_p),
+        ("engine", C.c_void_p), ("positions_sampled", C.c_void_p),
     ]
 
 
@@ -109,7 +119,7 @@ def lib():
     h.yapd_sample_rows.argtypes = [C.POINTER(SampleArgs), C.c_void_p]
     h.yapd_select_step_noalloc.restype = C.c_int
     h.yapd_select_step_noalloc.argtypes = [C.POINTER(SelectArgs), C.c_void_p]
-    if h.yapd_abi_version() != 1:
+    if h.yapd_abi_version() != YAPD_ABI_VERSION:
         raise RuntimeError("yapd_select ABI version mismatch")
     _lib = h
     return h

@@ -96,7 +96,23 @@ struct UnmaskParams {
   uint8_t* hit_eos;
   int64_t* k_step_out;
   uint8_t* is_commit_out;
+  // the engine's whole-generation buffers (server/engine.py:493-497, 586-622),
+  // or xt_full == null
+  int64_t* xt_full;
+  int64_t xt_stride;
+  int64_t* blk_start;
+  int64_t* cache_len;
+  const int64_t* n_speech;
+  int64_t blk_limit, cache_limit;
+  int64_t* flags;
 };
+
+// Block token l of request b: from the caller's (B, L) block, or gathered
+// from the engine's token buffer at the request's block start
+// (server/engine.py:495-496).
+__device__ __forceinline__ int64_t xt_at(const UnmaskParams& U, int b, int l) {
+  return U.xt ? U.xt[b * U.L + l] : U.xt_full[(int64_t)b * U.xt_stride + U.blk_start[b] + l];
+}
 
 // Unsigned division by an invariant divisor d >= 1 for dividends below 2^31:
 // q = umulhi(x, m) >> sh with l = ceil(log2 d), m = ceil(2^(31 + l) / d),
@@ -160,6 +176,7 @@ struct SampleParams {
   DivU div_L;               // division by L
   DivU div_grid;            // division by the launch's grid size
   int32_t* work_w;          // work list (each CTA writes its own entries)
+  unsigned long long* pos_count;  // optional: += positions sampled this step
   UnmaskParams U;
 };
 
@@ -329,7 +346,8 @@ __device__ __forceinline__ void unmask_request(const UnmaskParams& U, int dense,
   // every load that does not depend on another goes out first (lanes past L
   // read the request's first position and ignore it)
   const int pc = in ? p : b * L;
-  const int64_t xr = U.xt[pc];
+  const int64_t xr = xt_at(U, b, in ? lane : 0);
+  const int64_t bs = U.xt_full ? U.blk_start[b] : 0;
   const uint8_t cm = U.is_commit[b];
   const int64_t ks = U.k_step[b];
   const int sraw = U.sampled[pc];   // -1 where not sampled this step
@@ -405,6 +423,8 @@ __device__ __forceinline__ void unmask_request(const UnmaskParams& U, int dense,
   if (in) {
     U.xt_out[p] = xf;
     if (smp >= 0) U.pmi[p] = pm;
+    // server/engine.py:586: the block goes back into the token buffer
+    if (U.xt_full) U.xt_full[(int64_t)b * U.xt_stride + bs + lane] = xf;
   }
   const int n_after = __popc(__ballot_sync(0xffffffffu, in && xf == U.mask_id));
   const bool eos = __any_sync(0xffffffffu, in && xf == U.stop_id);
@@ -417,6 +437,23 @@ __device__ __forceinline__ void unmask_request(const UnmaskParams& U, int dense,
     U.hit_eos[b] = eos ? 1 : 0;
     U.k_step_out[b] = k_fin;
     U.is_commit_out[b] = to_commit ? 1 : 0;
+    if (U.xt_full) {
+      // commit rows move to the next block (server/engine.py:597-603, the
+      // engine's clamps keep inert rows in range) and the packed flags
+      // (:614-622) for the engine's one host sync
+      const int64_t cl = U.cache_len[b];
+      const int64_t cl2 = commit ? min(cl + (int64_t)L, U.cache_limit) : cl;
+      const int64_t bs2 = commit ? min(bs + (int64_t)L, U.blk_limit) : bs;
+      U.cache_len[b] = cl2;
+      U.blk_start[b] = bs2;
+      int64_t* f = U.flags + (int64_t)b * 6;
+      f[0] = commit ? 1 : 0;
+      f[1] = n_after;
+      f[2] = eos ? 1 : 0;
+      f[3] = k_fin;
+      f[4] = bs2;
+      f[5] = U.n_speech[b];
+    }
   }
 }
 
@@ -485,8 +522,9 @@ __device__ int cta_prepare(const SampleParams& P, int* scan, ReqTable* rt = null
 #pragma unroll
     for (int r = 0; r < kR; ++r) {
       const int pc = min(c0 + r * 32 + lane, total - 1);
-      xv[r] = U.xt[pc];
-      cv[r] = U.is_commit[divu(pc, P.div_L)];
+      const int bq = divu(pc, P.div_L);
+      xv[r] = xt_at(U, bq, pc - bq * U.L);
+      cv[r] = U.is_commit[bq];
     }
     // the table loads go out while the scan loads are in flight
     if (with_table) load_req_table(P, *rt);
@@ -512,6 +550,7 @@ __device__ int cta_prepare(const SampleParams& P, int* scan, ReqTable* rt = null
     base += q < w ? c : 0;
     tot += c;
   }
+  if (P.pos_count && blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(P.pos_count, (unsigned long long)tot);
   // this CTA's entries: global indices me + k*grid (the k-th item) and, for
   // the output initialisation, positions me + j*grid; both stride by grid,
   // so each round of 32 meets few of them (warp-uniform loops)
@@ -4367,7 +4406,12 @@ int yapd_select_step(const yapd_select_args* a, void* stream) {
   if (a->V > YAPD_MAX_V) return YAPD_ERR_V_TOO_LARGE;
   if ((int64_t)a->B * a->L > (1 << 30)) return YAPD_ERR_BAD_SHAPE;
   if (a->logits_dtype != YAPD_DTYPE_F32 && a->logits_dtype != YAPD_DTYPE_BF16) return YAPD_ERR_BAD_DTYPE;
-  if (!a->logits || !a->xt || !a->k_step || !a->is_commit || !a->log_prior || !a->sched_t || !a->q_t ||
+  const yapd_engine_state* eng = a->engine;
+  if (eng && (!eng->xt_full || !eng->blk_start || !eng->cache_len || !eng->n_speech || !eng->flags))
+    return YAPD_ERR_NULL_POINTER;
+  if (eng && (eng->blk_limit < 0 || eng->cache_limit < 0 || eng->xt_stride < eng->blk_limit + a->L))
+    return YAPD_ERR_BAD_SHAPE;
+  if (!a->logits || (!a->xt && !eng) || !a->k_step || !a->is_commit || !a->log_prior || !a->sched_t || !a->q_t ||
       !a->xt_out || !a->sampled || !a->pmi || !a->n_unmask || !a->n_mask_after || !a->hit_eos ||
       !a->k_step_out || !a->is_commit_out)
     return YAPD_ERR_NULL_POINTER;
@@ -4404,6 +4448,7 @@ int yapd_select_step(const yapd_select_args* a, void* stream) {
   P.cfg_w = a->cfg_scale;
   P.cfg_1pw = a->cfg_one_plus;
   P.sampled = a->sampled;
+  P.pos_count = reinterpret_cast<unsigned long long*>(a->positions_sampled);
   P.fused = 1;
   P.dense = a->dense ? 1 : 0;
 
@@ -4438,6 +4483,14 @@ int yapd_select_step(const yapd_select_args* a, void* stream) {
   U.hit_eos = a->hit_eos;
   U.k_step_out = a->k_step_out;
   U.is_commit_out = a->is_commit_out;
+  U.xt_full = eng ? eng->xt_full : nullptr;
+  U.xt_stride = eng ? eng->xt_stride : 0;
+  U.blk_start = eng ? eng->blk_start : nullptr;
+  U.cache_len = eng ? eng->cache_len : nullptr;
+  U.n_speech = eng ? eng->n_speech : nullptr;
+  U.blk_limit = eng ? eng->blk_limit : 0;
+  U.cache_limit = eng ? eng->cache_limit : 0;
+  U.flags = eng ? eng->flags : nullptr;
 
   cudaStream_t st = (cudaStream_t)stream;
   // profiling events: inside a stream capture they must be external event

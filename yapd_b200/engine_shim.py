@@ -1,8 +1,8 @@
 """Drop-in wiring of the select-step library into the reference's engines.
 
 ``FlashEngine._step_gpu`` (m8than/yapd ``server/engine.py:491-622``) keeps its
-signature; its select body and state update (``:533-612``) become one
-``select_step`` call.  ``TurboEngine._sample`` (``server/engine_ar.py:220-243``)
+signature; its select body, state update and write-back (``:533-622``) become
+one ``select_step`` call.  ``TurboEngine._sample`` (``server/engine_ar.py:220-243``)
 keeps its signature and becomes one ``sample_rows`` call.
 
 The engines are duck-typed: any object with the reference's attributes works
@@ -16,50 +16,48 @@ import types
 
 import torch
 
-from .select import SelectOutputs, sample_rows, select_step
+from .select import EngineBuffers, SelectOutputs, sample_rows, select_step
 
 
 class FlashSelect:
-    """State the select step keeps per engine: preallocated outputs and the
-    Philox step counter (the reference draws fresh ``torch.rand`` noise every
-    tick, ``server/engine.py:88-91``; here every tick advances the offset)."""
+    """State the select step keeps per engine: preallocated outputs and flags,
+    and the Philox step counter (the reference draws fresh ``torch.rand``
+    noise every tick, ``server/engine.py:88-91``; here every tick advances the
+    offset)."""
 
     def __init__(self, engine, seed: int = 1234):
         self.seed = seed
         self.offset = 0
         self.out = None
+        self.flags = None
         self.engine = engine
 
     def __call__(self, logits: torch.Tensor, B: int, blk_idx: torch.Tensor, xt_blk: torch.Tensor,
                  commit_rows: torch.Tensor):
-        """Select body + state update of ``FlashEngine._step_gpu`` for rows
-        ``[0, B)`` (``server/engine.py:533-622``); returns ``(flags, xt_final)``."""
+        """Select body, state update and engine write-back of
+        ``FlashEngine._step_gpu`` for rows ``[0, B)`` (``server/engine.py:533-622``):
+        one library call (two kernels, no torch op); returns ``(flags, xt_final)``.
+        ``k_step``, ``is_commit``, ``xt``, ``cache_len`` and ``blk_start`` are
+        updated in the engine's own tensors."""
         e = self.engine
         L = e.BS
         if self.out is None or self.out.xt.shape[0] < B:
-            self.out = SelectOutputs.empty(max(B, getattr(e, "max_active", B)), L, logits.device)
+            n = max(B, getattr(e, "max_active", B))
+            self.out = SelectOutputs.empty(n, L, logits.device)
+            self.flags = torch.empty(n, 6, dtype=torch.int64, device=logits.device)
         o = self.out
         out = SelectOutputs(xt=o.xt[:B], sampled=o.sampled[:B], pmi=o.pmi[:B], n_unmask=o.n_unmask[:B],
                             n_mask_after=o.n_mask_after[:B], hit_eos=o.hit_eos[:B],
-                            k_step=o.k_step[:B], is_commit=o.is_commit[:B])
+                            k_step=e.k_step[:B], is_commit=e.is_commit[:B])
+        eng = EngineBuffers(xt_full=e.xt, blk_start=e.blk_start[:B], cache_len=e.cache_len[:B],
+                            n_speech=e.n_speech[:B], flags=self.flags[:B],
+                            blk_limit=int(e.N_max) - L, cache_limit=int(e.L) - L)
         select_step(logits, xt_blk, e.k_step[:B], commit_rows, e.log_prior, e.sched_t, e.q_t,
                     cfg_scale=float(e.cfg) if e.n_branch == 2 else 0.0, mask_id=e.MASK,
                     stop_id=e.STOP, temperature=float(e.temp), pos_noise=e.posT > 0,
-                    use_quantile=e.tau > 0, seed=self.seed, offset=self.offset, out=out)
+                    use_quantile=e.tau > 0, seed=self.seed, offset=self.offset, out=out, engine=eng)
         self.offset += 1
-        xt_final = out.xt
-        e.xt[:B] = e.xt[:B].scatter(1, blk_idx, xt_final)
-        # k_step / is_commit came back updated (server/engine.py:593, 606-612)
-        e.k_step[:B] = out.k_step
-        adv = commit_rows
-        e.cache_len[:B] = torch.where(adv, (e.cache_len[:B] + e.BS).clamp(max=e.L - e.BS),
-                                      e.cache_len[:B])
-        e.blk_start[:B] = torch.where(adv, (e.blk_start[:B] + e.BS).clamp(max=e.N_max - e.BS),
-                                      e.blk_start[:B])
-        e.is_commit[:B] = out.is_commit
-        flags = torch.stack([commit_rows.long(), out.n_mask_after.long(), out.hit_eos.long(),
-                             e.k_step[:B], e.blk_start[:B], e.n_speech[:B]], dim=1)
-        return flags, xt_final
+        return self.flags[:B], out.xt
 
 
 def flash_step_gpu(self, B: int, l_used: int):

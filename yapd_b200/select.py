@@ -70,6 +70,23 @@ class SelectOutputs:
         )
 
 
+@dataclass
+class EngineBuffers:
+    """FlashEngine's whole-generation buffers (``server/engine.py:493-497``,
+    ``:586-622``) for rows ``[0, B)``: the step scatters its block result into
+    ``xt_full`` at ``blk_start``, advances ``cache_len`` / ``blk_start`` of
+    committing rows (clamped to ``cache_limit`` / ``blk_limit``) and writes
+    ``flags`` ``(B, 6)`` int64 = (was_commit, n_mask_after, hit_eos, k_step,
+    blk_start, n_speech)."""
+    xt_full: torch.Tensor       # (B, >= blk_limit + L) int64, unit column stride
+    blk_start: torch.Tensor     # (B,) int64
+    cache_len: torch.Tensor     # (B,) int64
+    n_speech: torch.Tensor      # (B,) int64
+    flags: torch.Tensor         # (B, 6) int64, contiguous
+    blk_limit: int              # N_max - L
+    cache_limit: int            # L_cache - L
+
+
 _WORKSPACES: dict = {}
 
 
@@ -135,17 +152,28 @@ def select_step(logits: torch.Tensor, xt: torch.Tensor, k_step: torch.Tensor,
                 gumbel_pos: torch.Tensor | None = None, seed: int = 0, offset: int = 0,
                 zero_temp_greedy: bool = True, dense: bool = False,
                 out: SelectOutputs | None = None,
-                prof_events: tuple | None = None) -> SelectOutputs:
-    """One block-diffusion select step (``server/engine.py:533-612``).
+                prof_events: tuple | None = None, engine: EngineBuffers | None = None,
+                L: int | None = None, positions_sampled: torch.Tensor | None = None) -> SelectOutputs:
+    """One block-diffusion select step (``server/engine.py:533-622``).
 
     ``nb`` is 2 when ``cfg_scale > 0`` (conditional + unconditional rows) and 1
     otherwise, as ``FlashEngine.n_branch`` (``server/engine.py:322``).  Noise is
     explicit when ``gumbel_tok`` (``(B, L, V)``) and ``gumbel_pos`` (``(B, L)``)
-    are given, else generated in-kernel from ``(seed, offset)``.
+    are given, else generated in-kernel from ``(seed, offset)``.  With
+    ``engine`` the step also writes the engine's token buffer, block / cache
+    offsets and flags; ``xt`` may then be None (the block is gathered from
+    ``engine.xt_full`` in the kernels, ``L`` giving its length).
+    ``positions_sampled``, a one-element int64 device tensor, is incremented
+    by the number of positions the step samples.
     """
     if not logits.is_cuda:
         raise ValueError("select_step runs on CUDA tensors only (no CPU fallback)")
-    B, L = xt.shape
+    if xt is None:
+        if engine is None or L is None:
+            raise ValueError("xt=None needs engine buffers and the block length L")
+        B = engine.blk_start.shape[0]
+    else:
+        B, L = xt.shape
     nb = 2 if cfg_scale > 0 else 1
     if logits.dim() != 3 or logits.shape[0] != B * nb or logits.shape[1] != L:
         raise ValueError(f"logits must be ({B * nb}, {L}, V), got {tuple(logits.shape)}")
@@ -155,7 +183,7 @@ def select_step(logits: torch.Tensor, xt: torch.Tensor, k_step: torch.Tensor,
     K = sched_t.numel()
     dev = logits.device
     keep = []
-    xt_c = xt.to(dev, torch.int64).contiguous()
+    xt_c = None if xt is None else xt.to(dev, torch.int64).contiguous()
     ks_c = k_step.to(dev, torch.int64).contiguous()
     ic_c = is_commit.to(dev).contiguous().to(torch.bool)
     lp_c = log_prior.to(dev, torch.float32).contiguous()
@@ -173,7 +201,7 @@ def select_step(logits: torch.Tensor, xt: torch.Tensor, k_step: torch.Tensor,
     a.stride_branch = logits.stride(0)
     a.stride_pos = logits.stride(1)
     a.logits_numel = _extent(logits)
-    a.xt, a.k_step, a.is_commit = xt_c.data_ptr(), ks_c.data_ptr(), ic_c.data_ptr()
+    a.xt, a.k_step, a.is_commit = _ptr(xt_c), ks_c.data_ptr(), ic_c.data_ptr()
     a.log_prior, a.sched_t, a.q_t = lp_c.data_ptr(), st_c.data_ptr(), qt_c.data_ptr()
     a.cfg_scale = float(cfg_scale)
     a.cfg_one_plus = float(1.0 + float(cfg_scale))
@@ -207,6 +235,27 @@ def select_step(logits: torch.Tensor, xt: torch.Tensor, k_step: torch.Tensor,
     a.is_commit_out = out.is_commit.data_ptr()
     if prof_events is not None:
         a.prof_event_begin, a.prof_event_end = prof_events[0].cuda_event, prof_events[1].cuda_event
+    if engine is not None:
+        es = N.EngineState()
+        xf = engine.xt_full
+        for name, t, shape in (("blk_start", engine.blk_start, (B,)), ("cache_len", engine.cache_len, (B,)),
+                               ("n_speech", engine.n_speech, (B,)), ("flags", engine.flags, (B, 6))):
+            if t.dtype != torch.int64 or tuple(t.shape) != shape or not t.is_contiguous() or t.device != dev:
+                raise ValueError(f"engine.{name} must be a contiguous int64 {shape} tensor on {dev}")
+        if xf.dtype != torch.int64 or xf.dim() != 2 or xf.shape[0] < B or xf.stride(1) != 1 or xf.device != dev:
+            raise ValueError("engine.xt_full must be an int64 (B, N) tensor with unit column stride")
+        if xf.shape[1] < int(engine.blk_limit) + L:
+            raise ValueError("engine.xt_full is shorter than blk_limit + L")
+        es.xt_full, es.xt_stride = xf.data_ptr(), xf.stride(0)
+        es.blk_start, es.cache_len = engine.blk_start.data_ptr(), engine.cache_len.data_ptr()
+        es.n_speech, es.flags = engine.n_speech.data_ptr(), engine.flags.data_ptr()
+        es.blk_limit, es.cache_limit = int(engine.blk_limit), int(engine.cache_limit)
+        keep.append(es)
+        a.engine = C.addressof(es)
+    if positions_sampled is not None:
+        if positions_sampled.dtype != torch.int64 or positions_sampled.numel() < 1 or positions_sampled.device != dev:
+            raise ValueError("positions_sampled must be an int64 device tensor")
+        a.positions_sampled = positions_sampled.data_ptr()
     need = N.lib().yapd_select_workspace_size(B, L)
     ws = workspace(need, dev)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()

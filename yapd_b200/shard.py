@@ -21,7 +21,8 @@ def shard_range(total: int, world: int, rank: int) -> tuple[int, int]:
 
 
 def gather_committed(xt_local: torch.Tensor, total: int, dist) -> torch.Tensor | None:
-    """All-gather every rank's ``(B_local, L)`` committed tokens into ``(total, L)``.
+    """All-gather every rank's ``(B_local, L)`` committed tokens into ``(total, L)``
+    int32 token ids (speech ids and MASK are below 2^31).
 
     Shards may be ragged; they are padded to the largest shard for the
     collective and trimmed afterwards.  Returns the full tensor on every rank.
@@ -30,8 +31,8 @@ def gather_committed(xt_local: torch.Tensor, total: int, dist) -> torch.Tensor |
     L = xt_local.shape[1]
     sizes = [shard_range(total, world, r)[1] - shard_range(total, world, r)[0] for r in range(world)]
     mx = max(sizes)
-    pad = torch.full((mx, L), -1, dtype=xt_local.dtype, device=xt_local.device)
-    pad[: xt_local.shape[0]] = xt_local
+    pad = torch.full((mx, L), -1, dtype=torch.int32, device=xt_local.device)
+    pad[: xt_local.shape[0]] = xt_local.to(torch.int32)
     parts = [torch.empty_like(pad) for _ in range(world)]
     dist.all_gather(parts, pad)
     return torch.cat([p[:n] for p, n in zip(parts, sizes)], dim=0)

@@ -22,7 +22,9 @@
  * memory: scratch comes from the caller's workspace.  A negative return value
  * is a host-side validation error (nothing was launched); YAPD_OK means the
  * kernels were enqueued.  Device-side conditions (a bounded wait that expired)
- * are recorded in the workspace status word, read by yapd_read_status.
+ * are recorded in the workspace status word, read by yapd_read_status; a
+ * select step whose sampling did not finish for some position leaves that
+ * position's sampled id at -2 and its request's state unchanged.
  */
 #ifndef YAPD_SELECT_H_
 #define YAPD_SELECT_H_
@@ -51,6 +53,9 @@ extern "C" {
 /* Device status bits (yapd_read_status). */
 #define YAPD_STATUS_WAIT_TIMEOUT 1u   /* a bounded pipeline wait expired */
 #define YAPD_STATUS_INTERNAL 2u       /* a kernel invariant check failed */
+#define YAPD_STATUS_ROWS_SKIPPED 4u   /* a request's state update was skipped:
+                                         some of its positions were not sampled
+                                         (their sampled id is left at -2) */
 
 /* Largest vocabulary one logit row may have (register-resident rows). */
 #define YAPD_MAX_V 8208
@@ -173,6 +178,10 @@ typedef struct yapd_select_args {
   /* optional device counter: the step adds the number of positions it
      samples (2 logit rows each with CFG), for throughput accounting */
   int64_t* positions_sampled;
+  /* limit of each bounded pipeline wait: 0 = the default 0.5 s; < 0 = every
+     pipeline wait gives up at once (for testing the failure path); the final
+     drain of in-flight copies always waits up to the default */
+  int64_t wait_limit_ns;
 } yapd_select_args;
 
 /* Rows for TurboEngine._sample: logits (R, V) with row stride `stride_row`. */
@@ -186,6 +195,7 @@ typedef struct yapd_sample_args {
   int32_t* sampled;             /* (R,) */
   void* workspace;
   size_t workspace_bytes;
+  int64_t wait_limit_ns;        /* as in yapd_select_args */
 } yapd_sample_args;
 
 /* ABI version of the loaded library (YAPD_ABI_VERSION). */
@@ -237,7 +247,10 @@ int yapd_sample_rows(const yapd_sample_args* args, void* stream);
  * The first call on a device looks up that array's device address, so make
  * it before any stream capture.  All calls share the array: calls whose
  * kernels overlap on the GPU race.  The status word is cleared per call and
- * is not readable through yapd_read_status.
+ * is not readable through yapd_read_status; a call whose sampling did not
+ * finish leaves the affected positions' sampled ids at -2 and their requests'
+ * state unchanged, which the caller sees in its own outputs.  Arguments are
+ * checked before anything is enqueued.
  */
 int yapd_select_step_noalloc(const yapd_select_args* args, void* stream);
 

@@ -56,6 +56,37 @@ def test_host_validation_without_gpu():
     assert lib.yapd_sample_rows(None, None) == -1
 
 
+def test_history_stride_checked():
+    """A history row shorter than the vocabulary is rejected (no out-of-row reads)."""
+    import ctypes as C
+    from yapd_b200 import _native as N
+    lib = N.lib()
+    a = N.SampleArgs()
+    a.R, a.V, a.logits_dtype = 4, 8194, N.YAPD_DTYPE_F32
+    a.logits, a.sampled = 4096, 4096            # never dereferenced: rejected on the host
+    a.stride_row, a.logits_numel = 8194, 4 * 8194
+    a.workspace, a.workspace_bytes = 4096, 256
+    a.sampling.history_kind = N.YAPD_HISTORY_BITMAP
+    a.sampling.history = 4096
+    a.sampling.history_stride = (8194 + 31) // 32 - 1
+    assert lib.yapd_sample_rows(C.byref(a), None) == -2
+    a.sampling.history_kind = N.YAPD_HISTORY_BYTES
+    a.sampling.history_stride = 8193
+    assert lib.yapd_sample_rows(C.byref(a), None) == -2
+
+
+def test_noalloc_checks_before_enqueue():
+    """yapd_select_step_noalloc rejects bad arguments before touching the stream
+    (an invalid stream handle is never used)."""
+    import ctypes as C
+    from yapd_b200 import _native as N
+    lib = N.lib()
+    a = N.SelectArgs()
+    a.B, a.nb, a.L, a.V, a.K = 2, 2, 16, 8194, 4
+    a.logits_dtype = 5
+    assert lib.yapd_select_step_noalloc(C.byref(a), C.c_void_p(0xdead)) == -3
+
+
 def test_ctypes_layout_matches_c():
     """The ctypes mirror of the argument structs has the C compiler's layout
     (sizes and the offset of every field), checked with the host gcc."""

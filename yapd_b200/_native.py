@@ -23,6 +23,7 @@ YAPD_MAX_L = 32
 YAPD_ABI_VERSION = 2
 YAPD_STATUS_WAIT_TIMEOUT = 1
 YAPD_STATUS_INTERNAL = 2
+YAPD_STATUS_ROWS_SKIPPED = 4
 
 EXPORTED = [
     "yapd_abi_version", "yapd_status_string", "yapd_select_workspace_size",
@@ -76,7 +77,7 @@ class SelectArgs(C.Structure):
         ("k_step_out", C.c_void_p), ("is_commit_out", C.c_void_p),
         ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
         ("prof_event_begin", C.c_void_p), ("prof_event_end", C.c_void_p),
-        ("engine", C.c_void_p), ("positions_sampled", C.c_void_p),
+        ("engine", C.c_void_p), ("positions_sampled", C.c_void_p), ("wait_limit_ns", C.c_int64),
     ]
 
 
@@ -86,6 +87,7 @@ class SampleArgs(C.Structure):
         ("stride_row", C.c_int64), ("logits_numel", C.c_int64),
         ("sampling", Sampling), ("noise", Noise),
         ("sampled", C.c_void_p), ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
+        ("wait_limit_ns", C.c_int64),
     ]
 
 

@@ -128,14 +128,16 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// Wait for phase `parity` of `bar`, giving up after `limit_ns` nanoseconds.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+// Wait for phase `parity` of `bar`, giving up after `limit_ns` nanoseconds;
+// a negative limit gives up without waiting (the failure path, for tests).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int64_t limit_ns) {
+  if (limit_ns < 0) return false;
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (;;) {
     // the thread sleeps in the wait until the phase completes (or 20 us pass)
     if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
-    if (globaltimer_ns() - t0 > limit_ns) return false;
+    if (globaltimer_ns() - t0 > (uint64_t)limit_ns) return false;
   }
 }
 

@@ -24,6 +24,9 @@
 #include <stdint.h>
 #include <math.h>
 
+#include <atomic>
+#include <mutex>
+
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -69,7 +72,7 @@ __device__ __forceinline__ int gtid() { return (int)(threadIdx.x % C::NT); }
 template <class C>
 __device__ __forceinline__ int gidx() { return threadIdx.x / C::NT; }
 
-constexpr uint64_t kWaitLimitNs = 500ull * 1000ull * 1000ull;  // 0.5 s per pipeline wait
+constexpr int64_t kWaitLimitNs = 500ll * 1000ll * 1000ll;  // 0.5 s: default pipeline wait, and every drain
 
 // Parameters of the block-state update (server/engine.py:559-612).
 struct UnmaskParams {
@@ -105,6 +108,7 @@ struct UnmaskParams {
   const int64_t* n_speech;
   int64_t blk_limit, cache_limit;
   int64_t* flags;
+  uint32_t* status;
 };
 
 // Block token l of request b: from the caller's (B, L) block, or gathered
@@ -177,6 +181,7 @@ struct SampleParams {
   DivU div_grid;            // division by the launch's grid size
   int32_t* work_w;          // work list (each CTA writes its own entries)
   unsigned long long* pos_count;  // optional: += positions sampled this step
+  int64_t wait_ns;          // limit of each pipeline wait (drains: kWaitLimitNs)
   UnmaskParams U;
 };
 
@@ -365,7 +370,12 @@ __device__ __forceinline__ void unmask_request(const UnmaskParams& U, int dense,
     gn = (U.noise_kind == YAPD_NOISE_EXPLICIT) ? U.gumbel_pos[p]
                                                 : philox_position_gumbel(U.seed, U.offset, (uint32_t)p);
   float pm = 0.f;
-  const int smp = (in && (dense || (!commit && x == U.mask_id))) ? sraw : -1;
+  const bool want = in && (dense || (!commit && x == U.mask_id));
+  // a masked position of a denoising request that this step had to sample but
+  // did not (its id left at -2 after an expired wait): the request keeps its
+  // state (commit rows do not use their samples)
+  const bool skip = __any_sync(0xffffffffu, want && !commit && sraw < 0);
+  const int smp = (want && !skip && sraw >= 0) ? sraw : -1;
   if (smp >= 0) {
     const float lpl = __fmul_rn(U.pmi_lambda, __ldg(U.log_prior + smp));
     pm = __fsub_rn(logf(fmaxf(pr.x, 1e-8f)), lpl);
@@ -419,20 +429,22 @@ __device__ __forceinline__ void unmask_request(const UnmaskParams& U, int dense,
   }
   const bool do_un = is_mask && rank < n_un;
   int64_t xf = x;
-  if (denoise && do_un) xf = (int64_t)U.sampled[p];
+  if (denoise && do_un && !skip) xf = (int64_t)U.sampled[p];
   if (in) {
     U.xt_out[p] = xf;
     if (smp >= 0) U.pmi[p] = pm;
+    else if (want) U.pmi[p] = __int_as_float(0x7fc00000);
     // server/engine.py:586: the block goes back into the token buffer
     if (U.xt_full) U.xt_full[(int64_t)b * U.xt_stride + bs + lane] = xf;
   }
   const int n_after = __popc(__ballot_sync(0xffffffffu, in && xf == U.mask_id));
   const bool eos = __any_sync(0xffffffffu, in && xf == U.stop_id);
   if (lane == 0) {
-    const int64_t k_new = denoise ? ks + 1 : ks;
+    const int64_t k_new = (denoise && !skip) ? ks + 1 : ks;
     const int64_t k_fin = commit ? 0 : k_new;
-    const bool to_commit = denoise && !eos && (n_after == 0 || k_fin >= (int64_t)K);
-    U.n_unmask[b] = denoise ? n_un : 0;
+    const bool to_commit = denoise && !skip && !eos && (n_after == 0 || k_fin >= (int64_t)K);
+    if (skip) atomicOr(U.status, (unsigned)YAPD_STATUS_ROWS_SKIPPED);
+    U.n_unmask[b] = (denoise && !skip) ? n_un : 0;
     U.n_mask_after[b] = n_after;
     U.hit_eos[b] = eos ? 1 : 0;
     U.k_step_out[b] = k_fin;
@@ -566,6 +578,7 @@ __device__ int cta_prepare(const SampleParams& P, int* scan, ReqTable* rt = null
         const int ln = (int)__fns(masks[r], 0u, nxt - base + 1);
         if (lane == ln) {
           P.work_w[nxt] = p0 + lane;
+          P.sampled[p0 + lane] = -2;  // until this CTA samples it
           const int qi = divu(nxt - me, P.div_grid);
           if (qi < cap) items_pos[qi] = p0 + lane;
         }
@@ -2985,7 +2998,7 @@ __device__ __forceinline__ void group_phase(const SampleParams& P, KSmem<C>& ks,
     for (int it = g; it < n_my; it += C::NG) {
       const int stage = it % C::NSTAGE;
       const uint32_t parity = (uint32_t)(it / C::NSTAGE) & 1u;
-      const bool ok = mbar_wait_bounded(&ks.full[stage], parity, kWaitLimitNs);
+      const bool ok = mbar_wait_bounded(&ks.full[stage], parity, P.wait_ns);
       if (!ok) atomicOr(P.status, (unsigned)YAPD_STATUS_WAIT_TIMEOUT);
       if (csync_or<C>(!ok)) break;
       if (tid == 0) atomicAdd(&ks.landed[stage], 1);
@@ -3003,7 +3016,7 @@ __device__ __forceinline__ void group_phase(const SampleParams& P, KSmem<C>& ks,
       const int ref_it = it + C::NSTAGE;
       ItemParams refill{};
       if (ref_it < n_my) refill = load_params(P, item_pos<C>(P, first + ref_it * stride));
-      if (!mbar_wait_bounded(&ks.ready[stage], parity, kWaitLimitNs)) {
+      if (!mbar_wait_bounded(&ks.ready[stage], parity, P.wait_ns)) {
         if ((threadIdx.x & 31) == 0) atomicOr(P.status, (unsigned)YAPD_STATUS_WAIT_TIMEOUT);
         break;
       }
@@ -3708,7 +3721,7 @@ __device__ __forceinline__ bool w_position(const SampleParams& P, WSmem& ws, con
     if (!ok_wait) continue;
     const int s = (int)(gcons % WCfg::NSLOT);
     const uint32_t par = (gcons / WCfg::NSLOT) & 1u;
-    const bool ok = mbar_wait_bounded(&ws.bar[warp][s], par, kWaitLimitNs);
+    const bool ok = mbar_wait_bounded(&ws.bar[warp][s], par, P.wait_ns);
     if (!__all_sync(0xffffffffu, ok)) {
       if (lane == 0) atomicOr(P.status, (unsigned)YAPD_STATUS_WAIT_TIMEOUT);
       ok_wait = false;
@@ -3907,7 +3920,9 @@ __device__ __forceinline__ bool w_position(const SampleParams& P, WSmem& ws, con
   // merge: lanes (shuffles), then the team's warps (shared memory)
   float m3[3] = {mcl, CFG ? mul : kNegInf, zabs};
   const float r3[3] = {rc, ru, rz};
-  float s3[3] = {sc, su, s};
+  // a warp whose wait expired poisons the team's sum: the team defers the
+  // position to the grouped pipeline (its own waits decide there)
+  float s3[3] = {sc, su, ok_wait ? s : __int_as_float(0x7fc00000)};
   const float mscale[3] = {kLog2e, kLog2e, 1.0f};
 #pragma unroll
   for (int j = 0; j < 3; ++j) {
@@ -4228,7 +4243,7 @@ constexpr size_t wsmem_bytes() {
 struct DevInfo {
   int sms = 0;
   int occ[2][2] = {{0, 0}, {0, 0}};  // [bf16][cfg]
-  bool init = false;
+  std::atomic<bool> init{false};
 };
 
 template <bool CFG>
@@ -4243,7 +4258,11 @@ static int prepare_wkernel() {
   return occ >= 1 ? YAPD_OK : YAPD_ERR_LAUNCH;
 }
 
+// Per-device set-up (kernel attributes, SM count), done once per device under
+// a lock; a device reset (cudaDeviceReset) is not detected, so a process that
+// resets a device must not call the library on it again.
 static DevInfo g_dev[64];
+static std::mutex g_init_mu;
 
 template <class C, bool CFG>
 static int prepare_kernel(int* occ) {
@@ -4260,7 +4279,12 @@ static int device_info(DevInfo** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return YAPD_ERR_NO_DEVICE;
   DevInfo& d = g_dev[dev];
-  if (!d.init) {
+  if (!d.init.load(std::memory_order_acquire)) {
+    std::lock_guard<std::mutex> lock(g_init_mu);
+    if (d.init.load(std::memory_order_relaxed)) {
+      *out = &d;
+      return YAPD_OK;
+    }
     if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       return YAPD_ERR_NO_DEVICE;
     int rc = prepare_kernel<CfgBF16, true>(&d.occ[1][1]);
@@ -4275,13 +4299,13 @@ static int device_info(DevInfo** out) {
                                               (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess)
       rc = YAPD_ERR_LAUNCH;
     if (rc != YAPD_OK) return rc;
-    d.init = true;
+    d.init.store(true, std::memory_order_release);
   }
   *out = &d;
   return YAPD_OK;
 }
 
-static int fill_sampling(SampleParams& P, const yapd_sampling& s, const yapd_noise& n) {
+static int fill_sampling(SampleParams& P, const yapd_sampling& s, const yapd_noise& n, int V) {
   P.temperature = s.temperature;
   P.top_k = s.top_k;
   P.top_p = s.top_p;
@@ -4296,8 +4320,10 @@ static int fill_sampling(SampleParams& P, const yapd_sampling& s, const yapd_noi
   if (s.history_kind != YAPD_HISTORY_NONE && s.history_kind != YAPD_HISTORY_BITMAP &&
       s.history_kind != YAPD_HISTORY_BYTES)
     return YAPD_ERR_BAD_ARG;
-  if (s.history_kind != YAPD_HISTORY_NONE && (!s.history || s.history_stride <= 0))
-    return YAPD_ERR_NULL_POINTER;
+  if (s.history_kind != YAPD_HISTORY_NONE && !s.history) return YAPD_ERR_NULL_POINTER;
+  // a row must hold every token's bit (word v >> 5) or byte (v)
+  if (s.history_kind == YAPD_HISTORY_BITMAP && s.history_stride < (int64_t)((V + 31) / 32)) return YAPD_ERR_BAD_SHAPE;
+  if (s.history_kind == YAPD_HISTORY_BYTES && s.history_stride < (int64_t)V) return YAPD_ERR_BAD_SHAPE;
   P.history_kind = s.history_kind;
   P.history = s.history;
   P.history_stride = s.history_stride;
@@ -4347,6 +4373,42 @@ static int launch_sample(const SampleParams& P, int dtype, int max_items, cudaSt
 
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
+static size_t select_workspace_bytes(int32_t B, int32_t L) {
+  if (B <= 0 || L <= 0) return 256;
+  const size_t n = (size_t)B * (size_t)L;
+  return 256 + align256(n * sizeof(int32_t)) + align256(n * sizeof(float2));
+}
+
+// Every host-side check of a select step, before anything is enqueued
+// (`need_workspace`: the caller's workspace must be present and large enough).
+static int validate_select(const yapd_select_args* a, bool need_workspace) {
+  if (!a) return YAPD_ERR_NULL_POINTER;
+  if (a->B <= 0 || a->L <= 0 || a->L > YAPD_MAX_L || a->V <= 0 || a->K <= 0 || (a->nb != 1 && a->nb != 2))
+    return YAPD_ERR_BAD_SHAPE;
+  if (a->V > YAPD_MAX_V) return YAPD_ERR_V_TOO_LARGE;
+  if ((int64_t)a->B * a->L > (1 << 30)) return YAPD_ERR_BAD_SHAPE;
+  if (a->logits_dtype != YAPD_DTYPE_F32 && a->logits_dtype != YAPD_DTYPE_BF16) return YAPD_ERR_BAD_DTYPE;
+  const yapd_engine_state* eng = a->engine;
+  if (eng && (!eng->xt_full || !eng->blk_start || !eng->cache_len || !eng->n_speech || !eng->flags))
+    return YAPD_ERR_NULL_POINTER;
+  if (eng && (eng->blk_limit < 0 || eng->cache_limit < 0 || eng->xt_stride < eng->blk_limit + a->L))
+    return YAPD_ERR_BAD_SHAPE;
+  if (!a->logits || (!a->xt && !eng) || !a->k_step || !a->is_commit || !a->log_prior || !a->sched_t || !a->q_t ||
+      !a->xt_out || !a->sampled || !a->pmi || !a->n_unmask || !a->n_mask_after || !a->hit_eos ||
+      !a->k_step_out || !a->is_commit_out)
+    return YAPD_ERR_NULL_POINTER;
+  if ((reinterpret_cast<uintptr_t>(a->logits) & 15u) != 0) return YAPD_ERR_MISALIGNED;
+  if (a->stride_req < 0 || a->stride_branch < 0 || a->stride_pos < 0) return YAPD_ERR_BAD_SHAPE;
+  const int64_t last = (int64_t)(a->B - 1) * a->stride_req + (int64_t)(a->nb - 1) * a->stride_branch +
+                       (int64_t)(a->L - 1) * a->stride_pos + a->V;
+  if (a->logits_numel < last) return YAPD_ERR_BAD_SHAPE;
+  if (need_workspace && (!a->workspace || a->workspace_bytes < select_workspace_bytes(a->B, a->L)))
+    return YAPD_ERR_WORKSPACE;
+  if (a->noise.kind == YAPD_NOISE_EXPLICIT && a->pos_noise && !a->noise.gumbel_pos) return YAPD_ERR_NULL_POINTER;
+  SampleParams scratch{};
+  return fill_sampling(scratch, a->sampling, a->noise, a->V);
+}
+
 
 }  // namespace yapd
 
@@ -4372,11 +4434,7 @@ const char* yapd_status_string(int code) {
   }
 }
 
-size_t yapd_select_workspace_size(int32_t B, int32_t L) {
-  if (B <= 0 || L <= 0) return 256;
-  const size_t n = (size_t)B * (size_t)L;
-  return 256 + align256(n * sizeof(int32_t)) + align256(n * sizeof(float2));
-}
+size_t yapd_select_workspace_size(int32_t B, int32_t L) { return select_workspace_bytes(B, L); }
 
 size_t yapd_sample_workspace_size(int32_t R) {
   (void)R;
@@ -4399,30 +4457,9 @@ int yapd_read_status(const void* workspace, void* stream, uint32_t* status_out) 
 }
 
 int yapd_select_step(const yapd_select_args* a, void* stream) {
-  if (!a) return YAPD_ERR_NULL_POINTER;
-  if (a->B <= 0 || a->L <= 0 || a->L > YAPD_MAX_L || a->V <= 0 || a->K <= 0 ||
-      (a->nb != 1 && a->nb != 2))
-    return YAPD_ERR_BAD_SHAPE;
-  if (a->V > YAPD_MAX_V) return YAPD_ERR_V_TOO_LARGE;
-  if ((int64_t)a->B * a->L > (1 << 30)) return YAPD_ERR_BAD_SHAPE;
-  if (a->logits_dtype != YAPD_DTYPE_F32 && a->logits_dtype != YAPD_DTYPE_BF16) return YAPD_ERR_BAD_DTYPE;
+  int rc = validate_select(a, true);
+  if (rc != YAPD_OK) return rc;
   const yapd_engine_state* eng = a->engine;
-  if (eng && (!eng->xt_full || !eng->blk_start || !eng->cache_len || !eng->n_speech || !eng->flags))
-    return YAPD_ERR_NULL_POINTER;
-  if (eng && (eng->blk_limit < 0 || eng->cache_limit < 0 || eng->xt_stride < eng->blk_limit + a->L))
-    return YAPD_ERR_BAD_SHAPE;
-  if (!a->logits || (!a->xt && !eng) || !a->k_step || !a->is_commit || !a->log_prior || !a->sched_t || !a->q_t ||
-      !a->xt_out || !a->sampled || !a->pmi || !a->n_unmask || !a->n_mask_after || !a->hit_eos ||
-      !a->k_step_out || !a->is_commit_out)
-    return YAPD_ERR_NULL_POINTER;
-  if ((reinterpret_cast<uintptr_t>(a->logits) & 15u) != 0) return YAPD_ERR_MISALIGNED;
-  if (a->stride_req < 0 || a->stride_branch < 0 || a->stride_pos < 0) return YAPD_ERR_BAD_SHAPE;
-  const int64_t last = (int64_t)(a->B - 1) * a->stride_req + (int64_t)(a->nb - 1) * a->stride_branch +
-                       (int64_t)(a->L - 1) * a->stride_pos + a->V;
-  if (a->logits_numel < last) return YAPD_ERR_BAD_SHAPE;
-  if (!a->workspace || a->workspace_bytes < yapd_select_workspace_size(a->B, a->L)) return YAPD_ERR_WORKSPACE;
-  if (a->noise.kind == YAPD_NOISE_EXPLICIT && a->pos_noise && !a->noise.gumbel_pos)
-    return YAPD_ERR_NULL_POINTER;
 
   SampleParams P{};
   const int es = a->logits_dtype == YAPD_DTYPE_BF16 ? 2 : 4;
@@ -4436,7 +4473,7 @@ int yapd_select_step(const yapd_select_args* a, void* stream) {
   P.L = a->L;
   P.div_L = divu_make(a->L);
   P.V = a->V;
-  int rc = fill_sampling(P, a->sampling, a->noise);
+  rc = fill_sampling(P, a->sampling, a->noise, a->V);
   if (rc != YAPD_OK) return rc;
   char* ws = static_cast<char*>(a->workspace);
   const size_t n_pos = (size_t)a->B * a->L;
@@ -4449,6 +4486,7 @@ int yapd_select_step(const yapd_select_args* a, void* stream) {
   P.cfg_1pw = a->cfg_one_plus;
   P.sampled = a->sampled;
   P.pos_count = reinterpret_cast<unsigned long long*>(a->positions_sampled);
+  P.wait_ns = a->wait_limit_ns == 0 ? kWaitLimitNs : a->wait_limit_ns;
   P.fused = 1;
   P.dense = a->dense ? 1 : 0;
 
@@ -4491,6 +4529,7 @@ int yapd_select_step(const yapd_select_args* a, void* stream) {
   U.blk_limit = eng ? eng->blk_limit : 0;
   U.cache_limit = eng ? eng->cache_limit : 0;
   U.flags = eng ? eng->flags : nullptr;
+  U.status = P.status;
 
   cudaStream_t st = (cudaStream_t)stream;
   // profiling events: inside a stream capture they must be external event
@@ -4531,7 +4570,7 @@ int yapd_sample_rows(const yapd_sample_args* a, void* stream) {
   P.L = 1;
   P.div_L = divu_make(1);
   P.V = a->V;
-  int rc = fill_sampling(P, a->sampling, a->noise);
+  int rc = fill_sampling(P, a->sampling, a->noise, a->V);
   if (rc != YAPD_OK) return rc;
   P.status = static_cast<uint32_t*>(a->workspace);
   P.work_w = nullptr;
@@ -4540,6 +4579,7 @@ int yapd_sample_rows(const yapd_sample_args* a, void* stream) {
   P.n_identity = a->R;
   P.sampled = a->sampled;
   P.pcu = nullptr;
+  P.wait_ns = a->wait_limit_ns == 0 ? kWaitLimitNs : a->wait_limit_ns;
   return launch_sample(P, a->logits_dtype, a->R, (cudaStream_t)stream);
 }
 
@@ -4575,10 +4615,12 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 // name is only a stand-in: the kernels need the address that
 // cudaGetSymbolAddress returns with the device current.
 static void* g_noalloc_ptr[64];
+static std::mutex g_noalloc_mu;
 
 static int noalloc_scratch(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return YAPD_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
   if (!g_noalloc_ptr[dev]) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return YAPD_ERR_LAUNCH;
@@ -4591,11 +4633,14 @@ static int noalloc_scratch(void** out) {
 }  // namespace yapd
 
 extern "C" int yapd_select_step_noalloc(const yapd_select_args* args, void* stream) {
+  // every argument check first: a rejected call enqueues nothing
   if (!args) return YAPD_ERR_NULL_POINTER;
-  if (args->B <= 0 || args->L <= 0) return YAPD_ERR_BAD_SHAPE;
-  if ((int64_t)args->B * (int64_t)args->L > (int64_t)YAPD_NOALLOC_MAX_POSITIONS) return YAPD_ERR_WORKSPACE;
+  if (args->B > 0 && args->L > 0 && (int64_t)args->B * (int64_t)args->L > (int64_t)YAPD_NOALLOC_MAX_POSITIONS)
+    return YAPD_ERR_WORKSPACE;
+  int rc = validate_select(args, false);
+  if (rc != YAPD_OK) return rc;
   void* scratch = nullptr;
-  const int rc = noalloc_scratch(&scratch);
+  rc = noalloc_scratch(&scratch);
   if (rc != YAPD_OK) return rc;
   if (yapd_select_workspace_size(args->B, args->L) > kNoAllocBytes) return YAPD_ERR_WORKSPACE;
   if (cudaMemsetAsync(scratch, 0, sizeof(uint32_t), (cudaStream_t)stream) != cudaSuccess) return YAPD_ERR_LAUNCH;

@@ -91,7 +91,15 @@ _WORKSPACES: dict = {}
 
 
 def workspace(nbytes: int, device) -> torch.Tensor:
-    """A zero-initialised, cached byte buffer of at least ``nbytes`` on ``device``."""
+    """A zero-initialised, cached byte buffer of at least ``nbytes`` on ``device``
+    (status word, work list, PMI inputs).
+
+    One buffer serves every call on the device, so the calls of one device must
+    be ordered on one stream (the engine's, ``server/engine.py:268-274``):
+    calls on two streams that overlap would share the scratch, and a buffer
+    replaced by a larger one is freed in the order of the stream that made the
+    replacement.  Callers with several streams pass their own workspace through
+    the C ABI (``yapd_select_args.workspace``)."""
     dev = torch.device(device)
     key = (dev.type, dev.index if dev.index is not None else torch.cuda.current_device())
     ws = _WORKSPACES.get(key)
@@ -153,7 +161,8 @@ def select_step(logits: torch.Tensor, xt: torch.Tensor, k_step: torch.Tensor,
                 zero_temp_greedy: bool = True, dense: bool = False,
                 out: SelectOutputs | None = None,
                 prof_events: tuple | None = None, engine: EngineBuffers | None = None,
-                L: int | None = None, positions_sampled: torch.Tensor | None = None) -> SelectOutputs:
+                L: int | None = None, positions_sampled: torch.Tensor | None = None,
+                wait_limit_ns: int = 0) -> SelectOutputs:
     """One block-diffusion select step (``server/engine.py:533-622``).
 
     ``nb`` is 2 when ``cfg_scale > 0`` (conditional + unconditional rows) and 1
@@ -164,7 +173,9 @@ def select_step(logits: torch.Tensor, xt: torch.Tensor, k_step: torch.Tensor,
     offsets and flags; ``xt`` may then be None (the block is gathered from
     ``engine.xt_full`` in the kernels, ``L`` giving its length).
     ``positions_sampled``, a one-element int64 device tensor, is incremented
-    by the number of positions the step samples.
+    by the number of positions the step samples.  ``wait_limit_ns`` bounds
+    each pipeline wait (0: 0.5 s; negative: every pipeline wait gives up at
+    once, for testing the failure path).
     """
     if not logits.is_cuda:
         raise ValueError("select_step runs on CUDA tensors only (no CPU fallback)")
@@ -252,6 +263,7 @@ def select_step(logits: torch.Tensor, xt: torch.Tensor, k_step: torch.Tensor,
         es.blk_limit, es.cache_limit = int(engine.blk_limit), int(engine.cache_limit)
         keep.append(es)
         a.engine = C.addressof(es)
+    a.wait_limit_ns = int(wait_limit_ns)
     if positions_sampled is not None:
         if positions_sampled.dtype != torch.int64 or positions_sampled.numel() < 1 or positions_sampled.device != dev:
             raise ValueError("positions_sampled must be an int64 device tensor")
@@ -267,7 +279,7 @@ def select_step(logits: torch.Tensor, xt: torch.Tensor, k_step: torch.Tensor,
 def sample_rows(logits: torch.Tensor, *, temperature=0.8, top_k=0, top_p=1.0, min_p=0.0,
                 rep_penalty=1.0, seen=None, gumbel: torch.Tensor | None = None, seed: int = 0,
                 offset: int = 0, zero_temp_greedy: bool = False,
-                out: torch.Tensor | None = None) -> torch.Tensor:
+                out: torch.Tensor | None = None, wait_limit_ns: int = 0) -> torch.Tensor:
     """One token per row of ``logits`` ``(R, V)`` (``server/engine_ar.py:220-243``).
 
     ``seen`` is the ``(R, V)`` bool history (``server/engine_ar.py:187``) or an
@@ -303,6 +315,7 @@ def sample_rows(logits: torch.Tensor, *, temperature=0.8, top_k=0, top_p=1.0, mi
     n.seed, n.offset = int(seed) & (2**64 - 1), int(offset) & (2**64 - 1)
     a.noise = n
     a.sampled = out.data_ptr()
+    a.wait_limit_ns = int(wait_limit_ns)
     ws = workspace(N.lib().yapd_sample_workspace_size(R), dev)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     stream = torch.cuda.current_stream(dev).cuda_stream
@@ -311,7 +324,7 @@ def sample_rows(logits: torch.Tensor, *, temperature=0.8, top_k=0, top_p=1.0, mi
 
 
 def read_status(device=None) -> int:
-    """Device status word of the cached workspace (synchronises the stream)."""
+    """Device status word of the device's workspace (synchronises the current stream)."""
     dev = torch.device(device or "cuda")
     ws = workspace(256, dev)
     v = C.c_uint32(0)
@@ -319,3 +332,11 @@ def read_status(device=None) -> int:
                                      C.c_void_p(torch.cuda.current_stream(dev).cuda_stream),
                                      C.byref(v)))
     return v.value
+
+
+def clear_status(device=None) -> None:
+    """Zero the status word of the device's workspace (enqueued on the current stream)."""
+    dev = torch.device(device or "cuda")
+    ws = workspace(256, dev)
+    N.check(N.lib().yapd_clear_status(C.c_void_p(ws.data_ptr()),
+                                      C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)))

@@ -182,6 +182,11 @@ typedef struct yapd_select_args {
      pipeline wait gives up at once (for testing the failure path); the final
      drain of in-flight copies always waits up to the default */
   int64_t wait_limit_ns;
+  /* quantile interpolation of the unmask threshold: 0 = the engine's
+     v_lo + (p - lo) * (v_hi - v_lo) (server/engine.py:567-572); 1 =
+     torch.quantile's (torch.lerp, fused multiply-add form), as the offline
+     block loop computes it (chatterbox_flash/model.py:284) */
+  int32_t quantile_lerp;
 } yapd_select_args;
 
 /* Rows for TurboEngine._sample: logits (R, V) with row stride `stride_row`. */

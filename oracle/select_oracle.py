@@ -255,3 +255,71 @@ def engine_update(res, xt_full, blk_start, cache_len, n_speech, is_commit, *, L:
     flags = torch.stack([adv.long(), res["n_mask_after"].long(), res["hit_eos"].long(),
                          res["k_step_final"].long(), blk_start, n_speech.long()], dim=1)
     return xt_full, blk_start, cache_len, flags
+
+
+def offline_gumbel(u: torch.Tensor) -> torch.Tensor:
+    """The offline generator's Gumbel transform ``-log(-log(u + 1e-10) + 1e-10)``
+    (``chatterbox_flash/model.py:76-80``)."""
+    return -torch.log(-torch.log(u + 1e-10) + 1e-10)
+
+
+def offline_block_step(logits_cond, logits_uncond, xt, done, *, k: int, K: int, sched_k: int,
+                       time_shift_tau: float, prior, cfg_scale: float, temperature: float,
+                       position_temperature: float, G, Gpos, mask_id: int, stop_id: int):
+    """Every row of one step of ``ChatterboxFlashT3.generate``'s block loop
+    (``chatterbox_flash/model.py:856-906``): ``_pmi_count_early_step_unmask``
+    (``model.py:185-311``) per row not yet done, with ``temperature_sampling=
+    "gumbel"`` and explicit noise (``G`` ``(B, bl, V)``, ``Gpos`` ``(B, bl)``),
+    the prior override path, then the row's done flag.  Returns ``(xt, done)``."""
+    B, bl = xt.shape
+    xt = xt.clone()
+    done = done.clone()
+    for b in range(B):
+        if bool(done[b]):
+            continue
+        c = logits_cond[b].float()
+        if cfg_scale != 0.0 and logits_uncond is not None:
+            u = logits_uncond[b].float()
+            guided = F.log_softmax(c, dim=-1)
+            guided = guided + cfg_scale * (guided - F.log_softmax(u, dim=-1))
+            pc, pu = F.softmax(c, dim=-1), F.softmax(u, dim=-1)
+        else:
+            guided, pc, pu = c, F.softmax(c, dim=-1), None
+        if temperature > 0:
+            sampled = (guided / temperature + G[b]).argmax(-1)
+        else:
+            sampled = guided.argmax(-1)
+        is_mask = xt[b] == mask_id
+        s1 = sampled.unsqueeze(1)
+        lp = prior[sampled].clamp_min(1e-8).log()
+        pmi = pc.gather(1, s1).squeeze(1).clamp_min(1e-8).log() - 1.0 * lp
+        if pu is not None:
+            pmi_u = pu.gather(1, s1).squeeze(1).clamp_min(1e-8).log() - 1.0 * lp
+            pmi = (1.0 + cfg_scale) * pmi - cfg_scale * pmi_u
+        if position_temperature > 0:
+            pmi = torch.where(is_mask, pmi + (torch.zeros_like(pmi) / position_temperature + Gpos[b]), pmi)
+        if k == K - 1:
+            do_unmask = is_mask
+        else:
+            idx = torch.arange(bl)[is_mask]
+            m = int(idx.numel())
+            do_unmask = torch.zeros_like(is_mask)
+            if m > 0:
+                pm = pmi[idx]
+                n_sched = max(0, min(int(sched_k), m))
+                if time_shift_tau > 0:
+                    q = max(0.0, 1.0 - time_shift_tau * (k + 1) / K)
+                    tau_k = torch.quantile(pm.float(), q)
+                    n_quant = int((pm >= tau_k).sum())
+                else:
+                    n_quant = 0
+                n_un = min(max(n_sched, n_quant), m)
+                if n_un >= m:
+                    do_unmask[idx] = True
+                elif n_un > 0:
+                    order = torch.argsort(pm, descending=True, stable=True)[:n_un]
+                    do_unmask[idx[order]] = True
+        xt[b] = torch.where(do_unmask, sampled, xt[b])
+        if int((xt[b] == mask_id).sum()) == 0 or bool((xt[b] == stop_id).any()):
+            done[b] = True
+    return xt, done

@@ -78,6 +78,7 @@ class SelectArgs(C.Structure):
         ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
         ("prof_event_begin", C.c_void_p), ("prof_event_end", C.c_void_p),
         ("engine", C.c_void_p), ("positions_sampled", C.c_void_p), ("wait_limit_ns", C.c_int64),
+        ("quantile_lerp", C.c_int32),
     ]
 
 

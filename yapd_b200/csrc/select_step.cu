@@ -93,6 +93,7 @@ struct UnmaskParams {
   int B, L, K;
   int64_t mask_id, stop_id;
   int pos_noise, use_quantile;
+  int quantile_lerp;  // 1: torch.quantile's interpolation (torch.lerp)
   int64_t* xt_out;
   int32_t* n_unmask;
   int32_t* n_mask_after;
@@ -410,7 +411,16 @@ __device__ __forceinline__ void unmask_request(const UnmaskParams& U, int dense,
   hi = hi < 0 ? 0 : (hi > 31 ? 31 : hi);
   const float v_lo = __shfl_sync(0xffffffffu, asc, lo);
   const float v_hi = __shfl_sync(0xffffffffu, asc, hi);
-  const float tau = __fadd_rn(v_lo, __fmul_rn(__fsub_rn(pq, (float)lo), __fsub_rn(v_hi, v_lo)));
+  const float wq = __fsub_rn(pq, (float)lo), dq = __fsub_rn(v_hi, v_lo);
+  float tau;
+  if (!U.quantile_lerp) {
+    tau = __fadd_rn(v_lo, __fmul_rn(wq, dq));
+  } else {
+    // torch.quantile (chatterbox_flash/model.py:284) interpolates with
+    // torch.lerp: a + w*(b - a) for w < 1/2, else b - (b - a)*(1 - w), each a
+    // fused multiply-add
+    tau = fabsf(wq) < 0.5f ? __fmaf_rn(wq, dq, v_lo) : __fmaf_rn(-dq, __fsub_rn(1.0f, wq), v_hi);
+  }
   int n_quant = __popc(__ballot_sync(0xffffffffu, is_mask && pm >= tau));
   if (!U.use_quantile) n_quant = 0;
   const int64_t sch = U.sched_t[kc];
@@ -4515,6 +4525,7 @@ int yapd_select_step(const yapd_select_args* a, void* stream) {
   U.stop_id = a->stop_id;
   U.pos_noise = a->pos_noise;
   U.use_quantile = a->use_quantile;
+  U.quantile_lerp = a->quantile_lerp ? 1 : 0;
   U.xt_out = a->xt_out;
   U.n_unmask = a->n_unmask;
   U.n_mask_after = a->n_mask_after;

@@ -162,7 +162,7 @@ def select_step(logits: torch.Tensor, xt: torch.Tensor, k_step: torch.Tensor,
                 out: SelectOutputs | None = None,
                 prof_events: tuple | None = None, engine: EngineBuffers | None = None,
                 L: int | None = None, positions_sampled: torch.Tensor | None = None,
-                wait_limit_ns: int = 0) -> SelectOutputs:
+                wait_limit_ns: int = 0, quantile_lerp: bool = False) -> SelectOutputs:
     """One block-diffusion select step (``server/engine.py:533-622``).
 
     ``nb`` is 2 when ``cfg_scale > 0`` (conditional + unconditional rows) and 1
@@ -175,7 +175,12 @@ def select_step(logits: torch.Tensor, xt: torch.Tensor, k_step: torch.Tensor,
     ``positions_sampled``, a one-element int64 device tensor, is incremented
     by the number of positions the step samples.  ``wait_limit_ns`` bounds
     each pipeline wait (0: 0.5 s; negative: every pipeline wait gives up at
-    once, for testing the failure path).
+    once, for testing the failure path).  ``quantile_lerp`` selects
+    torch.quantile's interpolation for the unmask threshold (the offline block
+    loop's, ``chatterbox_flash/model.py:284``) instead of the engine's.
+    ``logits`` may also be a ``(B, nb, L, V)`` view with any strides and a
+    unit last stride (e.g. the offline loop's ``[cond rows; uncond rows]``
+    layout seen as ``(2, B, L, V).transpose(0, 1)``).
     """
     if not logits.is_cuda:
         raise ValueError("select_step runs on CUDA tensors only (no CPU fallback)")
@@ -186,11 +191,19 @@ def select_step(logits: torch.Tensor, xt: torch.Tensor, k_step: torch.Tensor,
     else:
         B, L = xt.shape
     nb = 2 if cfg_scale > 0 else 1
-    if logits.dim() != 3 or logits.shape[0] != B * nb or logits.shape[1] != L:
-        raise ValueError(f"logits must be ({B * nb}, {L}, V), got {tuple(logits.shape)}")
-    if logits.stride(2) != 1:
-        logits = logits.contiguous()
-    V = logits.shape[2]
+    if logits.dim() == 4:
+        if tuple(logits.shape[:3]) != (B, nb, L):
+            raise ValueError(f"logits must be ({B}, {nb}, {L}, V), got {tuple(logits.shape)}")
+        if logits.stride(3) != 1:
+            logits = logits.contiguous()
+        strides = (logits.stride(0), logits.stride(1), logits.stride(2))
+    else:
+        if logits.dim() != 3 or logits.shape[0] != B * nb or logits.shape[1] != L:
+            raise ValueError(f"logits must be ({B * nb}, {L}, V), got {tuple(logits.shape)}")
+        if logits.stride(2) != 1:
+            logits = logits.contiguous()
+        strides = (logits.stride(0) * nb, logits.stride(0), logits.stride(1))
+    V = logits.shape[-1]
     K = sched_t.numel()
     dev = logits.device
     keep = []
@@ -208,9 +221,7 @@ def select_step(logits: torch.Tensor, xt: torch.Tensor, k_step: torch.Tensor,
     a.mask_id, a.stop_id = int(mask_id), int(stop_id)
     a.logits_dtype = _dtype_code(logits)
     a.logits = logits.data_ptr()
-    a.stride_req = logits.stride(0) * nb
-    a.stride_branch = logits.stride(0)
-    a.stride_pos = logits.stride(1)
+    a.stride_req, a.stride_branch, a.stride_pos = strides
     a.logits_numel = _extent(logits)
     a.xt, a.k_step, a.is_commit = _ptr(xt_c), ks_c.data_ptr(), ic_c.data_ptr()
     a.log_prior, a.sched_t, a.q_t = lp_c.data_ptr(), st_c.data_ptr(), qt_c.data_ptr()
@@ -264,6 +275,7 @@ def select_step(logits: torch.Tensor, xt: torch.Tensor, k_step: torch.Tensor,
         keep.append(es)
         a.engine = C.addressof(es)
     a.wait_limit_ns = int(wait_limit_ns)
+    a.quantile_lerp = 1 if quantile_lerp else 0
     if positions_sampled is not None:
         if positions_sampled.dtype != torch.int64 or positions_sampled.numel() < 1 or positions_sampled.device != dev:
             raise ValueError("positions_sampled must be an int64 device tensor")

@@ -263,7 +263,9 @@ class Runner:
         self.cache.zero_()
 
     def step(self, k: int, prof: bool = True, dense: bool = False, logits=None):
-        if self.gemm:
+        """Step k of the cycle; `logits` (already on the device) replaces the
+        step's own logits buffer (and, in configuration 4, its head GEMM)."""
+        if self.gemm and logits is None:
             if prof:
                 record_event(self.gev[k][0])
             self.head_gemm(self.gemm["hidden"][k % len(self.gemm["hidden"])])

@@ -34,10 +34,15 @@ def _extent(t: torch.Tensor) -> int:
 
 
 def _param(x, B: int, dtype, device, name: str):
-    """(pointer, scalar) for a per-request parameter given as scalar or (B,) tensor."""
+    """(pointer, scalar) for a per-request parameter given as scalar or (B,) tensor.
+
+    A 0-dim tensor on the CPU is read as a scalar; one on the device is
+    broadcast to ``(B,)`` on the device (reading it would synchronise)."""
     if isinstance(x, torch.Tensor):
         if x.numel() == 1 and x.dim() == 0:
-            return None, x.item()
+            if not x.is_cuda:
+                return None, x.item()
+            x = x.expand(B)
         if x.shape != (B,):
             raise ValueError(f"{name} must be a scalar or a ({B},) tensor, got {tuple(x.shape)}")
         x = x.to(device=device, dtype=dtype).contiguous()

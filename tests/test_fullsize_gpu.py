@@ -37,10 +37,12 @@ def _outputs(out):
 
 def _step_and_compare(inp, dev, seed, offset, dense=False):
     from yapd_b200 import select as S
+    S.clear_status()
     out = S.select_step(inp.logits.to(dev), inp.xt.to(dev), inp.k_step.to(dev), inp.is_commit.to(dev),
                         inp.log_prior.to(dev), inp.sched_t.to(dev), inp.q_t.to(dev), seed=seed,
                         offset=offset, dense=dense, **_kw(inp, dev))
     torch.cuda.synchronize()
+    assert S.read_status() == 0   # no expired wait, no kernel invariant broken
     gpu = _outputs(out)
     _with_philox(inp, seed, offset)
     orc = O.select_step(inp, noise="explicit")

@@ -209,8 +209,15 @@ struct Hand {
   // written by the group
   float m[3], s[3];  // group maxima (c, u, z2') and sums relative to them
   int n;             // band members found (ids of the first 32 in cv)
-  int handed;        // 1: the tail warp resolves the band and writes the outputs
+  int handed;        // 1: the tail warp resolves the min-p band and writes the outputs;
+                     // 2: it finishes a histogram select (the fields below)
   int cv[32];
+  // histogram select handed to the tail: band P / band K / kept-token ids,
+  // their counts, the counts and masses above and between the bands, and the
+  // group's best kept token when the kept set is larger than aid
+  int hs_nP, hs_nK, hs_nA, hs_sep, hs_kept;
+  float hs_na, hs_ma, hs_mP, hs_nb, hs_mb;
+  int pid[32], kid[32], aid[64];
 };
 
 template <class C>
@@ -1603,7 +1610,6 @@ struct Smem {
   };
   int hsi[8];                 // histogram select: the scan's crossings ...
   float hsf[8];               // ... and its mass bounds
-  uint32_t hbits[(YAPD_MAX_V + 31) / 32];  // the position's history bitmap (histogram select)
   int klist[C::NT];           // histogram select: ids of the tokens above band P (kept)
 };
 
@@ -2439,7 +2445,7 @@ __device__ __forceinline__ void hist_scan(Smem<C>& sm, bool topk_on, int k, bool
 
 template <class C, bool CFG>
 __device__ __noinline__ bool select_hist(const SampleParams& P, const ItemParams Q, const RowRef<C> R, const Span S,
-                                         Smem<C>& sm) {
+                                         Smem<C>& sm, Hand& hd) {
   csync<C>();  // out-of-line reductions use scratch slots 2/3
   int slot = 2;
   const int tid = gtid<C>();
@@ -2453,13 +2459,6 @@ __device__ __noinline__ bool select_hist(const SampleParams& P, const ItemParams
   for (int i = tid; i < kHistBins; i += C::NT) {
     sm.hc[i] = 0;
     sm.hq[i] = 0u;
-  }
-  // the request's history bitmap, read once into shared memory (the kept
-  // tokens' penalty tests then cost no global round trip)
-  const bool stage_hist = P.history_kind == YAPD_HISTORY_BITMAP && P.history != nullptr && Q.rep != 1.0f;
-  if (stage_hist) {
-    const uint32_t* h = reinterpret_cast<const uint32_t*>(P.history) + (int64_t)(Q.pos / P.L) * P.history_stride;
-    for (int i = tid; i < (V + 31) / 32; i += C::NT) sm.hbits[i] = __ldg(h + i);
   }
   // ---- pass 1: group maxima ----
   float mc, mu, zm;
@@ -2489,7 +2488,6 @@ __device__ __noinline__ bool select_hist(const SampleParams& P, const ItemParams
     return false;
   ScoreCtx K;
   stats_rest<CFG>(P, Q, sA, X, K);
-  if (stage_hist) K.hbits = sm.hbits;
   // ---- the scan ----
   if (tid < 32) hist_scan<C>(sm, topk_on, Q.top_k, topp_on, Q.top_p, X.S);
   csync<C>();
@@ -2511,7 +2509,7 @@ __device__ __noinline__ bool select_hist(const SampleParams& P, const ItemParams
   // ---- pass 3: the bands, the kept set's candidates ----
   // (tokens between the bands are not visited: their count and mass come from
   // the histogram, less the band members that sit in those bins)
-  float n_above = 0.f, m_above = 0.f, m_bandP = 0.f, n_corr = 0.f, m_corr = 0.f;
+  float n_above = 0.f, m_above = 0.f, m_bandP = 0.f, n_corr = 0.f, m_corr = 0.f, m_bandK = 0.f;
   auto visit = [&](int v) {
     const float c = load_elem_smem<C>(R.sc, R.gc, v);
     const float u = CFG ? load_elem_smem<C>(R.su, R.gu, v) : 0.f;
@@ -2543,6 +2541,7 @@ __device__ __noinline__ bool select_hist(const SampleParams& P, const ItemParams
         sm.cande[at] = e;
       }
     } else {
+      m_bandK += e;
       const int at = atomicAdd(&sm.misc[1], 1);
       const int idx = C::BAND - 1 - at;
       if (idx >= 0) {
@@ -2607,8 +2606,9 @@ __device__ __noinline__ bool select_hist(const SampleParams& P, const ItemParams
     const float u = CFG ? load_elem_smem<C>(R.su, R.gu, v) : 0.f;
     if (wanted(hdepth<CFG>(X, K2mz, c, u))) visit(v);
   }
-  float acc[8] = {n_above, m_above, m_bandP, n_corr, m_corr, 0.f, 0.f, 0.f};
+  float acc[8] = {n_above, m_above, m_bandP, n_corr, m_corr, m_bandK, 0.f, 0.f};
   block_sum8<C>(acc, sm, slot);
+  m_bandK = acc[5];
   n_above = acc[0];
   m_above = acc[1];
   m_bandP = acc[2];
@@ -2616,6 +2616,87 @@ __device__ __noinline__ bool select_hist(const SampleParams& P, const ItemParams
   const float m_between = __fsub_rn(m_bins_between, acc[4]);
   const int nP = sm.misc[0], nK = sm.misc[1], nA = sm.misc[2];
   if (nP + nK > C::BAND || nP == 0 || (sep && nK == 0)) return false;
+  // ---- hand the rest to the group's tail warp ----
+  // (top-p rows whose lists fit the hand-off record, when the float bounds of
+  // S_k already guarantee what the exact resolution checks: band P's first
+  // member kept, every token below band P dropped, the k-th token in band K)
+  {
+    bool hand = topp_on && nP <= 32 && nK <= 32 && (!topk_on || sep);
+    float s_lo = X.S, s_hi = X.S;
+    if (hand && sep) {
+      const int kl = Q.top_k - (int)(n_above + (float)nP + n_between);
+      s_lo = __fadd_rn(__fadd_rn(m_above, m_bandP), fmaxf(m_between, 0.f));
+      s_hi = __fadd_rn(s_lo, m_bandK);
+      hand = kl >= 1 && kl <= nK;
+    }
+    hand = hand && m_above < __fmul_rn(__fmul_rn(Q.top_p, s_lo), 0.99999f) &&
+           __fadd_rn(m_above, m_bandP) >= __fmul_rn(__fmul_rn(Q.top_p, s_hi), 1.00001f);
+    if (hand) {
+      // the kept set: its ids for the tail, or (too many) its best scored here
+      int best_kept = -1;
+      if (nA > 64) {
+        Pick kb{kNegInf, kNegInf, 0x7fffffff};
+        for (int q = tid; q < nA && q < C::NT; q += C::NT) {
+          const int v = sm.klist[q];
+          const float vals = exact_val<C>(P, X, R, v);
+          const float es = exact_score<C>(P, K, v, vals);
+          const Pick cand{es, vals, v};
+          if (es == es && es > kNegInf && pick_better(cand, kb, K.turbo)) kb = cand;
+        }
+        if (nA > C::NT) {
+          // more kept tokens than the list holds: every thread scores its own
+          for (int j = S.j0 + tid; j < S.j1; j += C::NT) {
+            const int v0 = j * C::W - S.head;
+#pragma unroll 1
+            for (int i = 0; i < C::W; ++i) {
+              const int v = v0 + i;
+              const float c = load_elem_smem<C>(R.sc, R.gc, v);
+              const float u = CFG ? load_elem_smem<C>(R.su, R.gu, v) : 0.f;
+              if (!(hdepth<CFG>(X, K2mz, c, u) >= dH)) continue;
+              const float vals = exact_val_cu(P, X, c, u);
+              const float es = exact_score<C>(P, K, v, vals);
+              const Pick cand{es, vals, v};
+              if (es == es && es > kNegInf && pick_better(cand, kb, K.turbo)) kb = cand;
+            }
+          }
+          for (int e = tid; e < S.nscal; e += C::NT) {
+            const int v = scalar_v(S, e);
+            const float c = load_elem_smem<C>(R.sc, R.gc, v);
+            const float u = CFG ? load_elem_smem<C>(R.su, R.gu, v) : 0.f;
+            if (!(hdepth<CFG>(X, K2mz, c, u) >= dH)) continue;
+            const float vals = exact_val_cu(P, X, c, u);
+            const float es = exact_score<C>(P, K, v, vals);
+            const Pick cand{es, vals, v};
+            if (es == es && es > kNegInf && pick_better(cand, kb, K.turbo)) kb = cand;
+          }
+        }
+        best_kept = block_pick<C>(kb, K.turbo, sm, slot);
+      }
+      if (tid < nP) hd.pid[tid] = cand_id(sm.cand[tid]);
+      if (tid < nK) hd.kid[tid] = cand_id(sm.cand[C::BAND - 1 - tid]);
+      if (nA <= 64 && tid < nA) hd.aid[tid] = sm.klist[tid];
+      if (tid == 0) {
+        hd.m[0] = X.mc;
+        hd.m[1] = CFG ? X.mu : kNegInf;
+        hd.m[2] = zm;
+        hd.s[0] = X.Sc;
+        hd.s[1] = CFG ? X.Su : 0.f;
+        hd.s[2] = X.S;
+        hd.hs_nP = nP;
+        hd.hs_nK = nK;
+        hd.hs_nA = nA;
+        hd.hs_sep = sep ? 1 : 0;
+        hd.hs_kept = best_kept;
+        hd.hs_na = n_above;
+        hd.hs_ma = m_above;
+        hd.hs_mP = m_bandP;
+        hd.hs_nb = n_between;
+        hd.hs_mb = m_between;
+        hd.handed = 2;
+      }
+      return true;
+    }
+  }
   // exact scores of the kept tokens above the bands (they do not depend on
   // the band resolution below)
   Pick bp{kNegInf, kNegInf, 0x7fffffff};
@@ -2740,7 +2821,7 @@ __device__ __forceinline__ void compute_item(const SampleParams& P, KSmem<C>& ks
   }
   // top-k / top-p without min-p: the histogram select (three passes)
   if ((topk_on || topp_on) && !minp_on && !(topp_on && !(Q.top_p > 0.0f)))
-    if (select_hist<C, CFG>(P, Q, R, S, sm)) return;
+    if (select_hist<C, CFG>(P, Q, R, S, sm, h)) return;
 
   // ---- pass 1: this thread's maxima ----
   float mc_t, mu_t, nu_t;
@@ -2970,6 +3051,158 @@ __device__ __forceinline__ void tail_finish(const SampleParams& P, KSmem<C>& ks,
   band_finish_warp<C, CFG>(P, Q, X, K, n, v0, c0, u0);
 }
 
+// Tail warp: the end of a histogram select the group handed over (band K's
+// top-k cut and S_k, band P sorted by (exact value, id) with its top-p
+// flags, the kept tokens' and kept members' exact scores, the pick and the
+// outputs), from the stage's rows, which stay staged until the tail refills
+// the stage.  The group handed it over only when its float bounds of S_k
+// guarantee the checks below.
+template <class C, bool CFG>
+__device__ __noinline__ void tail_hist(const SampleParams& P, KSmem<C>& ks, int stage) {
+  const int lane = threadIdx.x & 31;
+  const Hand& h = ks.hand[stage];
+  const ItemParams Q = h.Q;
+  const RowRef<C> R = row_ref<C, CFG>(P, ks, stage, Q.pos);
+  PosCtx X;
+  float sA;
+  item_ctx<CFG>(P, Q, X, sA);
+  float m[3], s[3];
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    m[j] = h.m[j];
+    s[j] = h.s[j];
+  }
+  ScoreCtx K;
+  stats_core<CFG>(m, s, X);
+  stats_rest<CFG>(P, Q, sA, X, K);
+  const float K2mz = __fsub_rn(X.K2, X.zmax);
+  const int nP = h.hs_nP, nK = h.hs_nK, nA = h.hs_nA;
+  const float m_above = h.hs_ma;
+  auto logits = [&](int v, float& c, float& u) {
+    c = load_elem_smem<C>(R.sc, R.gc, v);
+    u = CFG ? load_elem_smem<C>(R.su, R.gu, v) : 0.f;
+  };
+  float Sk = X.S;
+  if (h.hs_sep) {
+    // S_k: everything above band K plus its first k - n_above members
+    const int kl = Q.top_k - (int)(h.hs_na + (float)nP + h.hs_nb);
+    unsigned long long key = 0ull;
+    float e = 0.f;
+    if (lane < nK) {
+      const int v = h.kid[lane];
+      float c, u;
+      logits(v, c, u);
+      key = cand_key(exact_val_cu(P, X, c, u), v);
+      e = ex2_approx(hdepth<CFG>(X, K2mz, c, u));
+    }
+    int rank = 0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) rank += (__shfl_sync(0xffffffffu, key, j) > key) ? 1 : 0;
+    const float part = warp_sum(lane < nK && rank < kl ? e : 0.f);
+    Sk = __fadd_rn(__fadd_rn(__fadd_rn(m_above, h.hs_mP), fmaxf(h.hs_mb, 0.f)), part);
+  }
+  // band P: exact values, masses and scores, sorted by (exact value, id)
+  const bool live0 = lane < nP;
+  unsigned long long key = 0ull;
+  float e = 0.f, score = kNegInf;
+  if (live0) {
+    const int v = h.pid[lane];
+    float c, u;
+    logits(v, c, u);
+    const float vals = exact_val_cu(P, X, c, u);
+    key = cand_key(vals, v);
+    e = ex2_approx(hdepth<CFG>(X, K2mz, c, u));
+    score = exact_score<C>(P, K, v, vals);
+  }
+  int kmax = 2;
+  while (kmax < nP) kmax <<= 1;
+  for (int kk = 2; kk <= kmax; kk <<= 1) {
+    for (int j = kk >> 1; j > 0; j >>= 1) {
+      const unsigned long long y = __shfl_xor_sync(0xffffffffu, key, j);
+      const float ey = __shfl_xor_sync(0xffffffffu, e, j);
+      const float sy = __shfl_xor_sync(0xffffffffu, score, j);
+      const bool up = ((lane & kk) == 0) || kk == kmax;
+      const bool lower = ((lane & j) == 0);
+      if ((up == lower) ? (y > key) : (y < key)) {
+        key = y;
+        e = ey;
+        score = sy;
+      }
+    }
+  }
+  const bool live = lane < nP;
+  K.r = __fdiv_rn(1.0f, Sk);
+  const float p = __fmul_rn(e, K.r);
+  double incl = live ? (double)p : 0.0;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  incl += (double)m_above * (double)K.r;
+  const bool keep = live && (__fsub_rn((float)incl, p) < Q.top_p);
+  // what the group's bounds guaranteed (recorded if the exact values disagree)
+  const double tot = __shfl_sync(0xffffffffu, incl, nP - 1);
+  if (lane == 0 && (!keep || !((float)tot >= Q.top_p))) atomicOr(P.status, (unsigned)YAPD_STATUS_INTERNAL);
+  // the best kept score: band P's kept members and the kept tokens above them
+  Pick bp{kNegInf, kNegInf, 0x7fffffff};
+  if (keep && score == score && score > kNegInf) bp = Pick{score, cand_val(key), cand_id(key)};
+  auto consider = [&](int v) {
+    float c, u;
+    logits(v, c, u);
+    const float vals = exact_val_cu(P, X, c, u);
+    const float es = exact_score<C>(P, K, v, vals);
+    const Pick cand{es, vals, v};
+    if (es == es && es > kNegInf && pick_better(cand, bp, K.turbo)) bp = cand;
+  };
+  if (nA <= 64) {
+    for (int i = lane; i < nA; i += 32) consider(h.aid[i]);
+  } else if (lane == 0 && h.hs_kept >= 0) {
+    consider(h.hs_kept);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    Pick y;
+    y.score = __shfl_xor_sync(0xffffffffu, bp.score, o);
+    y.vals = __shfl_xor_sync(0xffffffffu, bp.vals, o);
+    y.v = __shfl_xor_sync(0xffffffffu, bp.v, o);
+    if (pick_better(y, bp, K.turbo)) bp = y;
+  }
+  int chosen = bp.v;
+  if (!(bp.score > kNegInf)) {
+    // nothing kept scores above -inf: the first sorted candidate (torch's
+    // argmax over an all -inf row)
+    unsigned long long best = live ? key : 0ull;
+    if (nA <= 64) {
+      for (int i = lane; i < nA; i += 32) {
+        float c, u;
+        logits(h.aid[i], c, u);
+        const unsigned long long k2 = cand_key(exact_val_cu(P, X, c, u), h.aid[i]);
+        best = k2 > best ? k2 : best;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long y = __shfl_xor_sync(0xffffffffu, best, o);
+      best = y > best ? y : best;
+    }
+    chosen = cand_id(best);
+  }
+  if (lane == 0) {
+    if (chosen < 0 || chosen >= P.V) {
+      atomicOr(P.status, (unsigned)YAPD_STATUS_INTERNAL);
+      chosen = 0;
+    }
+    P.sampled[Q.pos] = chosen;
+    if (P.pcu) {
+      float c, u;
+      logits(chosen, c, u);
+      P.pcu[Q.pos] = pmi_cu<CFG>(X, c, u);
+    }
+  }
+  __syncwarp();
+}
+
 // The grouped pipeline over this CTA's items 0..n_my-1 (global item index
 // first + k * stride): NG groups of NT threads, each working one position at
 // a time from a shared NSTAGE-deep ring of staged rows, and one tail warp per
@@ -3030,7 +3263,8 @@ __device__ __forceinline__ void group_phase(const SampleParams& P, KSmem<C>& ks,
         if ((threadIdx.x & 31) == 0) atomicOr(P.status, (unsigned)YAPD_STATUS_WAIT_TIMEOUT);
         break;
       }
-      if (ks.hand[stage].handed) tail_finish<C, CFG>(P, ks, stage);
+      if (ks.hand[stage].handed == 1) tail_finish<C, CFG>(P, ks, stage);
+      else if (ks.hand[stage].handed == 2) tail_hist<C, CFG>(P, ks, stage);
       if ((threadIdx.x & 31) == 0 && ref_it < n_my) {
         fence_proxy_async_smem();
         issue_item<C>(P, ks, stage, refill);

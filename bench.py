@@ -233,9 +233,14 @@ class Runner:
         self.out = S.SelectOutputs(xt=o.xt, sampled=o.sampled, pmi=o.pmi, n_unmask=o.n_unmask,
                                    n_mask_after=o.n_mask_after, hit_eos=o.hit_eos, k_step=self.k,
                                    is_commit=self.c)
+        # min-p off for every request (configurations 2 and 3): the scalar tells
+        # the library so, and the select step runs its grouped kernel alone
+        min_p = 0.0 if float(inp.min_p.max()) <= 0.0 else inp.min_p.to(device)
+        bf = inp.logits.dtype == torch.bfloat16
+        self.kernel = "wsample_kernel" if bf and not isinstance(min_p, float) else "sample_kernel"
         self.kw = dict(cfg_scale=inp.cfg_scale, mask_id=inp.mask_id, stop_id=inp.stop_id,
                        temperature=inp.temperature.to(device), top_k=inp.top_k.to(device),
-                       top_p=inp.top_p.to(device), min_p=inp.min_p.to(device),
+                       top_p=inp.top_p.to(device), min_p=min_p,
                        rep_penalty=inp.rep_penalty.to(device),
                        history=inp.history_bitmap().to(device), pmi_lambda=inp.pmi_lambda,
                        pos_noise=True, use_quantile=True)
@@ -580,7 +585,7 @@ def run_ours(args, ws, rank, local):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
                          "traffic_source": "profiles/traffic.json (ncu dram__bytes per launch, committed)",
-                         "kernel": "wsample_kernel" if inp.logits.dtype == torch.bfloat16 else "sample_kernel",
+                         "kernel": R.kernel,
                          "kernel_ms_per_launch": kern_ms / G, "bytes_per_launch": byt / G},
             "e2e": {"value": e2e_rows / (e2e_ms * 1e-3), "unit": "rows/s",
                     "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"]},

@@ -46,12 +46,20 @@ def gap_ulps(a: float, b: float) -> float:
 
 
 def run_gpu(inp, *, noise="explicit", seed=0, offset=0, dense=True, zero_temp_greedy=True,
-            history_as="bitmap"):
+            history_as="bitmap", scalar_minp=False):
+    """One select step on the GPU.  ``scalar_minp``: pass min-p as the scalar 0
+    (every request has it off), which launches the grouped kernel alone for
+    bf16 select steps instead of the warp kernel."""
     from yapd_b200 import select as S
     dev = torch.device("cuda")
     hist = None
     if inp.history is not None:
         hist = inp.history_bitmap() if history_as == "bitmap" else inp.history
+    if scalar_minp:
+        assert float(inp.min_p.max()) <= 0.0
+        min_p = 0.0
+    else:
+        min_p = inp.min_p.to(dev)
     kw = {}
     if noise == "explicit":
         kw = dict(gumbel_tok=inp.gumbel_tok.to(dev), gumbel_pos=inp.gumbel_pos.to(dev))
@@ -59,7 +67,7 @@ def run_gpu(inp, *, noise="explicit", seed=0, offset=0, dense=True, zero_temp_gr
         inp.logits.to(dev), inp.xt.to(dev), inp.k_step.to(dev), inp.is_commit.to(dev),
         inp.log_prior.to(dev), inp.sched_t.to(dev), inp.q_t.to(dev), cfg_scale=inp.cfg_scale,
         mask_id=inp.mask_id, stop_id=inp.stop_id, temperature=inp.temperature.to(dev),
-        top_k=inp.top_k.to(dev), top_p=inp.top_p.to(dev), min_p=inp.min_p.to(dev),
+        top_k=inp.top_k.to(dev), top_p=inp.top_p.to(dev), min_p=min_p,
         rep_penalty=inp.rep_penalty.to(dev), history=None if hist is None else hist.to(dev),
         pmi_lambda=inp.pmi_lambda, pos_noise=inp.pos_noise, use_quantile=inp.use_quantile,
         seed=seed, offset=offset, zero_temp_greedy=zero_temp_greedy, dense=dense, **kw)

@@ -19,12 +19,12 @@ from yapd_b200.workloads import make_config
 pytestmark = pytest.mark.gpu
 
 
-def _run(inp, dev, **kw):
+def _run(inp, dev, min_p=None, **kw):
     out = S.select_step(
         inp.logits.to(dev), inp.xt.to(dev), inp.k_step.to(dev), inp.is_commit.to(dev), inp.log_prior.to(dev),
         inp.sched_t.to(dev), inp.q_t.to(dev), cfg_scale=inp.cfg_scale, mask_id=inp.mask_id,
         stop_id=inp.stop_id, temperature=inp.temperature.to(dev), top_k=inp.top_k.to(dev),
-        top_p=inp.top_p.to(dev), min_p=inp.min_p.to(dev), rep_penalty=inp.rep_penalty.to(dev),
+        top_p=inp.top_p.to(dev), min_p=inp.min_p.to(dev) if min_p is None else min_p, rep_penalty=inp.rep_penalty.to(dev),
         history=inp.history_bitmap().to(dev), pmi_lambda=inp.pmi_lambda, gumbel_tok=inp.gumbel_tok.to(dev),
         gumbel_pos=inp.gumbel_pos.to(dev), **kw)
     torch.cuda.synchronize()
@@ -33,13 +33,16 @@ def _run(inp, dev, **kw):
 
 
 # configuration 1: the bf16 warp kernel; 3: its grouped pipeline (histogram
-# select); 2: the fp32 sample kernel
-@pytest.mark.parametrize("config", [1, 3, 2])
-def test_expired_wait_is_reported_and_contained(config):
+# select); 3 with the scalar min-p 0: the bf16 grouped kernel launched alone;
+# 2: the fp32 sample kernel
+@pytest.mark.parametrize("config,scalar_minp", [(1, False), (3, False), (3, True), (2, False)])
+def test_expired_wait_is_reported_and_contained(config, scalar_minp):
     dev = torch.device("cuda")
     inp = make_config(config, seed=11, B=16, masked="ragged", commit_frac=0.2)
+    if scalar_minp:
+        assert float(inp.min_p.max()) <= 0.0
     S.clear_status()
-    got = _run(inp, dev, wait_limit_ns=-1)
+    got = _run(inp, dev, min_p=0.0 if scalar_minp else None, wait_limit_ns=-1)
     st = S.read_status()
     assert st & N.YAPD_STATUS_WAIT_TIMEOUT
     orc = O.select_step(inp, noise="explicit")

@@ -23,9 +23,12 @@ def _with_philox(inp, seed, offset):
 
 
 def _kw(inp, dev):
+    # as bench.py: min-p off everywhere is passed as the scalar (the grouped
+    # kernel then runs alone); the reduced tests keep the per-request tensors
+    min_p = 0.0 if float(inp.min_p.max()) <= 0.0 else inp.min_p.to(dev)
     return dict(cfg_scale=inp.cfg_scale, mask_id=inp.mask_id, stop_id=inp.stop_id,
                 temperature=inp.temperature.to(dev), top_k=inp.top_k.to(dev), top_p=inp.top_p.to(dev),
-                min_p=inp.min_p.to(dev), rep_penalty=inp.rep_penalty.to(dev),
+                min_p=min_p, rep_penalty=inp.rep_penalty.to(dev),
                 history=inp.history_bitmap().to(dev), pmi_lambda=inp.pmi_lambda,
                 pos_noise=inp.pos_noise, use_quantile=inp.use_quantile)
 

@@ -21,8 +21,9 @@ def _noise(inp, noise, seed, offset):
     return gt
 
 
-def check(inp, noise="explicit", seed=0, offset=0, dense=True, history_as="bitmap"):
-    gpu = run_gpu(inp, noise=noise, seed=seed, offset=offset, dense=dense, history_as=history_as)
+def check(inp, noise="explicit", seed=0, offset=0, dense=True, history_as="bitmap", scalar_minp=False):
+    gpu = run_gpu(inp, noise=noise, seed=seed, offset=offset, dense=dense, history_as=history_as,
+                  scalar_minp=scalar_minp)
     orc = O.select_step(inp, noise=noise, seed=seed, offset=offset)
     if dense:
         pos = torch.ones(inp.B, inp.L, dtype=torch.bool)
@@ -70,6 +71,16 @@ def test_philox_noise(config):
     inp = make_config(config, seed=13, B=6 if config else None, masked="ragged",
                       explicit_noise=False)
     check(inp, noise="philox", seed=1234 + config, offset=7 * config + 1)
+
+
+# min-p off everywhere, passed as the scalar: bf16 select steps run on the
+# grouped kernel alone (the warp kernel only serves min-p positions)
+@pytest.mark.parametrize("noise,dense,masked", [("explicit", True, "all"), ("explicit", False, "ragged"),
+                                                ("philox", False, "ragged")])
+def test_grouped_route_scalar_min_p(noise, dense, masked):
+    inp = make_config(3, seed=17, B=24, masked=masked, commit_frac=0.2,
+                      explicit_noise=noise == "explicit")
+    check(inp, noise=noise, seed=99, offset=3, dense=dense, scalar_minp=True)
 
 
 def test_history_as_bytes():

@@ -4599,7 +4599,11 @@ static int launch_sample(const SampleParams& P, int dtype, int max_items, cudaSt
   const bool bf = dtype == YAPD_DTYPE_BF16;
   const bool cfg = P.nb == 2;
   const int occ = d->occ[bf ? 1 : 0][cfg ? 1 : 0];
-  if (bf && P.fused) {
+  // the warp kernel's teams serve min-p positions; without min-p anywhere
+  // (a scalar min_p <= 0) every position goes to the grouped pipeline, which
+  // then runs on its own, without the warp path's code and deferral
+  const bool minp_any = P.min_p != nullptr || P.min_p_s > 0.0f;
+  if (bf && P.fused && minp_any) {
     // select step: warp-per-position kernel, one CTA per SM
     SampleParams Pw = P;
     Pw.div_grid = divu_make(d->sms);

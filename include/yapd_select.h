@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define YAPD_ABI_VERSION 2
+#define YAPD_ABI_VERSION 3
 
 /* Return codes (host-side validation; nothing is launched on error). */
 #define YAPD_OK 0
@@ -56,6 +56,9 @@ extern "C" {
 #define YAPD_STATUS_ROWS_SKIPPED 4u   /* a request's state update was skipped:
                                          some of its positions were not sampled
                                          (their sampled id is left at -2) */
+#define YAPD_STATUS_CANDIDATE_OVERFLOW 8u  /* fused head: a position had more
+                                         near-maximal tokens than its kept-token
+                                         slots (its pick may then be off) */
 
 /* Largest vocabulary one logit row may have (register-resident rows). */
 #define YAPD_MAX_V 8208
@@ -258,6 +261,49 @@ int yapd_sample_rows(const yapd_sample_args* args, void* stream);
  * checked before anything is enqueued.
  */
 int yapd_select_step_noalloc(const yapd_select_args* args, void* stream);
+
+/*
+ * yapd_lmhead_args — the speech head and the select step in one call.
+ *
+ * The reference computes logits = speech_head(hidden) with a library GEMM
+ * (server/engine.py:517-520; chatterbox_flash/engines/flashinfer.py:1452-1461)
+ * and then runs the select step on them.  Here the head runs on the tensor
+ * cores and the select step's statistics and Gumbel-max scoring run on its
+ * accumulators: the logits are never written to device memory.
+ *
+ * hidden element (request b, branch r, position l, feature d), bf16, lives at
+ *   hidden + b*h_stride_req + r*h_stride_branch + l*h_stride_pos + d
+ * (branch 0 = conditional, 1 = unconditional); weight is the (V, D) bf16 head
+ * with row stride w_stride.  Strides are elements, multiples of 8; both bases
+ * 16-byte aligned; D a multiple of 64.
+ *
+ * select: the select step's arguments as for yapd_select_step, with these
+ * restrictions: nb = 2, L = 16 or 32, no top-k / top-p / min-p (NULL arrays,
+ * scalars off), repetition penalty >= 1 (a request with a smaller penalty is
+ * left unsampled, its state unchanged), history NONE or BITMAP.  Its logits
+ * fields are ignored.  select.workspace holds yapd_lmhead_workspace_size bytes
+ * (status word first, as for yapd_select_step).  prof_event_begin /
+ * prof_event_end bracket the fused GEMM kernel.
+ */
+typedef struct yapd_lmhead_args {
+  const void* hidden;
+  int64_t h_stride_req, h_stride_branch, h_stride_pos, hidden_numel;
+  const void* weight;
+  int64_t w_stride, weight_numel;
+  int32_t D;
+  float* logits_out;            /* optional fp32 (B, 2, L, V): the logits the
+                                   epilogue consumed (for testing); NULL = none */
+  yapd_select_args select;
+} yapd_lmhead_args;
+
+/* Workspace bytes a yapd_lmhead_select_step call over B x L positions needs. */
+size_t yapd_lmhead_workspace_size(int32_t B, int32_t L);
+
+/* Fused speech head + select step.  A memset of the workspace's publication
+ * words, then three kernel launches: the tensor-core head GEMM with the select
+ * epilogue, the per-position resolve of the kept tokens, and the per-request
+ * state update of yapd_select_step. */
+int yapd_lmhead_select_step(const yapd_lmhead_args* args, void* stream);
 
 #ifdef __cplusplus
 }

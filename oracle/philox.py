@@ -77,3 +77,29 @@ def position_uniforms(seed: int, offset: int, B: int, L: int) -> torch.Tensor:
     out = philox4x32_10(ctr, (seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF))
     words = out[np.arange(n), p & np.uint32(3)]
     return _uniform_from_words(words).reshape(B, L)
+
+
+def token_uniforms_at(seed: int, offset: int, flat_pos: np.ndarray, V: int) -> torch.Tensor:
+    """``(n, V)`` token uniforms of the given flat positions ``b*L + l`` (the
+    same counters as ``token_uniforms``, for a subset of a large batch)."""
+    nq = (V + 3) // 4
+    pos = np.asarray(flat_pos, dtype=np.uint32)
+    ctr = np.empty((pos.size, nq, 4), dtype=np.uint32)
+    ctr[:, :, 0] = np.arange(nq, dtype=np.uint32)[None, :]
+    ctr[:, :, 1] = pos[:, None]
+    ctr[:, :, 2] = np.uint32(offset & 0xFFFFFFFF)
+    ctr[:, :, 3] = np.uint32((offset >> 32) & 0x7FFFFFFF)
+    out = philox4x32_10(ctr.reshape(-1, 4), (seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF))
+    return _uniform_from_words(out.reshape(pos.size, nq * 4)[:, :V])
+
+
+def position_uniforms_at(seed: int, offset: int, flat_pos: np.ndarray) -> torch.Tensor:
+    """``(n,)`` position uniforms of the given flat positions."""
+    p = np.asarray(flat_pos, dtype=np.uint32)
+    ctr = np.empty((p.size, 4), dtype=np.uint32)
+    ctr[:, 0] = p >> np.uint32(2)
+    ctr[:, 1] = np.uint32(0xFFFFFFFF)
+    ctr[:, 2] = np.uint32(offset & 0xFFFFFFFF)
+    ctr[:, 3] = np.uint32(((offset >> 32) & 0x7FFFFFFF) | 0x80000000)
+    out = philox4x32_10(ctr, (seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF))
+    return _uniform_from_words(out[np.arange(p.size), p & np.uint32(3)])

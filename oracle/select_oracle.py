@@ -59,6 +59,16 @@ def philox_noise(seed: int, offset: int, B: int, L: int, V: int):
     return gt, gp
 
 
+def philox_noise_rows(seed: int, offset: int, rows, L: int, V: int):
+    """Token noise ``(n, L, V)`` and position noise ``(n, L)`` of requests
+    ``rows`` (original indices) of a batch with block length ``L``."""
+    import numpy as np
+    flat = (np.asarray(rows, dtype=np.int64)[:, None] * L + np.arange(L)[None, :]).reshape(-1)
+    gt = gumbel_from_uniform(philox.token_uniforms_at(seed, offset, flat, V)).view(len(rows), L, V)
+    gp = gumbel_from_uniform(philox.position_uniforms_at(seed, offset, flat)).view(len(rows), L)
+    return gt, gp
+
+
 def cfg_combine(logits: torch.Tensor, nb: int, L: int, w: float):
     """``server/engine.py:533-544``: returns ``guided, probs_c, probs_u``
     each ``(B, L, V)`` (``probs_u`` is None without CFG)."""

@@ -99,7 +99,8 @@ def test_ctypes_layout_matches_c():
     if cc is None:
         pytest.skip("no host C compiler")
     structs = {"yapd_sampling": N.Sampling, "yapd_noise": N.Noise, "yapd_engine_state": N.EngineState,
-               "yapd_select_args": N.SelectArgs, "yapd_sample_args": N.SampleArgs}
+               "yapd_select_args": N.SelectArgs, "yapd_sample_args": N.SampleArgs,
+               "yapd_lmhead_args": N.LmheadArgs}
     lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "yapd_select.h"', "int main(void) {"]
     want = []
     for cname, py in structs.items():
@@ -116,3 +117,42 @@ def test_ctypes_layout_matches_c():
         subprocess.run([cc, "-I", os.path.join(ROOT, "include"), "-o", exe, src], check=True)
         got = [int(x) for x in subprocess.run([exe], check=True, capture_output=True, text=True).stdout.split()]
     assert got == want
+
+
+def test_lmhead_validation_without_gpu():
+    """The fused head's host checks: shapes, alignment and the sampling chain
+    it serves are rejected before any CUDA call."""
+    import ctypes as C
+    from yapd_b200 import _native as N
+    lib = N.lib()
+    h = N.LmheadArgs()
+    assert lib.yapd_lmhead_select_step(None, None) == -1
+    assert lib.yapd_lmhead_select_step(C.byref(h), None) == -2      # B = 0
+    a = h.select
+    a.B, a.nb, a.L, a.V, a.K = 4, 2, 32, 8194, 8
+    h.D = 1000
+    assert lib.yapd_lmhead_select_step(C.byref(h), None) == -2      # D not a multiple of 64
+    h.D = 1024
+    assert lib.yapd_lmhead_select_step(C.byref(h), None) == -1      # NULL hidden / weight
+    h.hidden, h.weight = 4096 + 8, 4096
+    assert lib.yapd_lmhead_select_step(C.byref(h), None) == -4      # hidden not 16-byte aligned
+    h.hidden = 4096
+    h.h_stride_req, h.h_stride_branch, h.h_stride_pos = 2 * 32 * 1024, 32 * 1024, 1024
+    h.hidden_numel, h.w_stride, h.weight_numel = 4 * 2 * 32 * 1024, 1024, 8194 * 1024
+    for f in ("xt", "k_step", "is_commit", "log_prior", "sched_t", "q_t", "xt_out", "sampled", "pmi",
+              "n_unmask", "n_mask_after", "hit_eos", "k_step_out", "is_commit_out", "workspace"):
+        setattr(a, f, 4096)
+    a.workspace_bytes = lib.yapd_lmhead_workspace_size(4, 32)
+    a.sampling.top_p_s = 0.9
+    assert lib.yapd_lmhead_select_step(C.byref(h), None) == -8      # top-p is not on this path
+    a.sampling.top_p_s = 1.0
+    a.sampling.min_p_s = 0.05
+    assert lib.yapd_lmhead_select_step(C.byref(h), None) == -8      # nor min-p
+    a.sampling.min_p_s = 0.0
+    a.nb = 1
+    assert lib.yapd_lmhead_select_step(C.byref(h), None) == -2      # CFG rows only
+    a.nb, a.L = 2, 24
+    assert lib.yapd_lmhead_select_step(C.byref(h), None) == -2      # L of 16 or 32
+    a.L = 32
+    a.workspace_bytes = 256
+    assert lib.yapd_lmhead_select_step(C.byref(h), None) == -6      # workspace too small

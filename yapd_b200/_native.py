@@ -20,15 +20,17 @@ YAPD_NOISE_PHILOX = 0
 YAPD_NOISE_EXPLICIT = 1
 YAPD_MAX_V = 8208
 YAPD_MAX_L = 32
-YAPD_ABI_VERSION = 2
+YAPD_ABI_VERSION = 3
 YAPD_STATUS_WAIT_TIMEOUT = 1
 YAPD_STATUS_INTERNAL = 2
 YAPD_STATUS_ROWS_SKIPPED = 4
+YAPD_STATUS_CANDIDATE_OVERFLOW = 8
 
 EXPORTED = [
     "yapd_abi_version", "yapd_status_string", "yapd_select_workspace_size",
     "yapd_sample_workspace_size", "yapd_clear_status", "yapd_read_status",
     "yapd_select_step", "yapd_sample_rows", "yapd_select_step_noalloc",
+    "yapd_lmhead_workspace_size", "yapd_lmhead_select_step",
 ]
 YAPD_NOALLOC_MAX_POSITIONS = 16384
 
@@ -92,6 +94,17 @@ class SampleArgs(C.Structure):
     ]
 
 
+class LmheadArgs(C.Structure):
+    _fields_ = [
+        ("hidden", C.c_void_p),
+        ("h_stride_req", C.c_int64), ("h_stride_branch", C.c_int64), ("h_stride_pos", C.c_int64),
+        ("hidden_numel", C.c_int64),
+        ("weight", C.c_void_p), ("w_stride", C.c_int64), ("weight_numel", C.c_int64),
+        ("D", C.c_int32), ("logits_out", C.c_void_p),
+        ("select", SelectArgs),
+    ]
+
+
 _lib = None
 
 
@@ -122,6 +135,10 @@ def lib():
     h.yapd_sample_rows.argtypes = [C.POINTER(SampleArgs), C.c_void_p]
     h.yapd_select_step_noalloc.restype = C.c_int
     h.yapd_select_step_noalloc.argtypes = [C.POINTER(SelectArgs), C.c_void_p]
+    h.yapd_lmhead_workspace_size.restype = C.c_size_t
+    h.yapd_lmhead_workspace_size.argtypes = [C.c_int32, C.c_int32]
+    h.yapd_lmhead_select_step.restype = C.c_int
+    h.yapd_lmhead_select_step.argtypes = [C.POINTER(LmheadArgs), C.c_void_p]
     if h.yapd_abi_version() != YAPD_ABI_VERSION:
         raise RuntimeError("yapd_select ABI version mismatch")
     _lib = h

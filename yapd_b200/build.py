@@ -19,7 +19,7 @@ CSRC = os.path.join(PKG, "csrc")
 LIBDIR = os.path.join(PKG, "_lib")
 LIB = os.path.join(LIBDIR, "libyapd_select.so")
 SOURCES = ["select_step.cu"]
-HEADERS = ["philox.cuh", "select_common.cuh"]
+HEADERS = ["philox.cuh", "select_common.cuh", "lmhead_select.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -4898,3 +4898,6 @@ extern "C" int yapd_select_step_noalloc(const yapd_select_args* args, void* stre
   a.workspace_bytes = kNoAllocBytes;
   return yapd_select_step(&a, stream);
 }
+
+// the fused speech head + select step (tcgen05 GEMM with the select epilogue)
+#include "lmhead_select.cuh"

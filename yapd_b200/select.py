@@ -22,6 +22,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _native as N
+from .workloads import history_to_bitmap
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
@@ -156,62 +157,14 @@ def _dtype_code(t: torch.Tensor) -> int:
     raise TypeError(f"logits must be float32 or bfloat16, got {t.dtype}")
 
 
-def select_step(logits: torch.Tensor, xt: torch.Tensor, k_step: torch.Tensor,
-                is_commit: torch.Tensor, log_prior: torch.Tensor, sched_t: torch.Tensor,
-                q_t: torch.Tensor, *, cfg_scale: float, mask_id: int, stop_id: int,
-                temperature=0.6, top_k=0, top_p=1.0, min_p=0.0, rep_penalty=1.0,
-                history=None, pmi_lambda: float = 1.0, pos_noise: bool = True,
-                use_quantile: bool = True, gumbel_tok: torch.Tensor | None = None,
-                gumbel_pos: torch.Tensor | None = None, seed: int = 0, offset: int = 0,
-                zero_temp_greedy: bool = True, dense: bool = False,
-                out: SelectOutputs | None = None,
-                prof_events: tuple | None = None, engine: EngineBuffers | None = None,
-                L: int | None = None, positions_sampled: torch.Tensor | None = None,
-                wait_limit_ns: int = 0, quantile_lerp: bool = False) -> SelectOutputs:
-    """One block-diffusion select step (``server/engine.py:533-622``).
-
-    ``nb`` is 2 when ``cfg_scale > 0`` (conditional + unconditional rows) and 1
-    otherwise, as ``FlashEngine.n_branch`` (``server/engine.py:322``).  Noise is
-    explicit when ``gumbel_tok`` (``(B, L, V)``) and ``gumbel_pos`` (``(B, L)``)
-    are given, else generated in-kernel from ``(seed, offset)``.  With
-    ``engine`` the step also writes the engine's token buffer, block / cache
-    offsets and flags; ``xt`` may then be None (the block is gathered from
-    ``engine.xt_full`` in the kernels, ``L`` giving its length).
-    ``positions_sampled``, a one-element int64 device tensor, is incremented
-    by the number of positions the step samples.  ``wait_limit_ns`` bounds
-    each pipeline wait (0: 0.5 s; negative: every pipeline wait gives up at
-    once, for testing the failure path).  ``quantile_lerp`` selects
-    torch.quantile's interpolation for the unmask threshold (the offline block
-    loop's, ``chatterbox_flash/model.py:284``) instead of the engine's.
-    ``logits`` may also be a ``(B, nb, L, V)`` view with any strides and a
-    unit last stride (e.g. the offline loop's ``[cond rows; uncond rows]``
-    layout seen as ``(2, B, L, V).transpose(0, 1)``).
-    """
-    if not logits.is_cuda:
-        raise ValueError("select_step runs on CUDA tensors only (no CPU fallback)")
-    if xt is None:
-        if engine is None or L is None:
-            raise ValueError("xt=None needs engine buffers and the block length L")
-        B = engine.blk_start.shape[0]
-    else:
-        B, L = xt.shape
-    nb = 2 if cfg_scale > 0 else 1
-    if logits.dim() == 4:
-        if tuple(logits.shape[:3]) != (B, nb, L):
-            raise ValueError(f"logits must be ({B}, {nb}, {L}, V), got {tuple(logits.shape)}")
-        if logits.stride(3) != 1:
-            logits = logits.contiguous()
-        strides = (logits.stride(0), logits.stride(1), logits.stride(2))
-    else:
-        if logits.dim() != 3 or logits.shape[0] != B * nb or logits.shape[1] != L:
-            raise ValueError(f"logits must be ({B * nb}, {L}, V), got {tuple(logits.shape)}")
-        if logits.stride(2) != 1:
-            logits = logits.contiguous()
-        strides = (logits.stride(0) * nb, logits.stride(0), logits.stride(1))
-    V = logits.shape[-1]
+def _common_args(a, B, nb, L, V, dev, keep, xt, k_step, is_commit, log_prior, sched_t, q_t, *,
+                 cfg_scale, mask_id, stop_id, temperature, top_k, top_p, min_p, rep_penalty, history,
+                 pmi_lambda, pos_noise, use_quantile, gumbel_tok, gumbel_pos, seed, offset,
+                 zero_temp_greedy, dense, out, prof_events, engine, positions_sampled, wait_limit_ns,
+                 quantile_lerp) -> SelectOutputs:
+    """Every field of ``a`` (a ``yapd_select_args``) except the logits and the
+    workspace; the tensors the call needs alive go to ``keep``."""
     K = sched_t.numel()
-    dev = logits.device
-    keep = []
     xt_c = None if xt is None else xt.to(dev, torch.int64).contiguous()
     ks_c = k_step.to(dev, torch.int64).contiguous()
     ic_c = is_commit.to(dev).contiguous().to(torch.bool)
@@ -221,13 +174,8 @@ def select_step(logits: torch.Tensor, xt: torch.Tensor, k_step: torch.Tensor,
     keep += [xt_c, ks_c, ic_c, lp_c, st_c, qt_c]
     if out is None:
         out = SelectOutputs.empty(B, L, dev)
-    a = N.SelectArgs()
     a.B, a.nb, a.L, a.V, a.K = B, nb, L, V, K
     a.mask_id, a.stop_id = int(mask_id), int(stop_id)
-    a.logits_dtype = _dtype_code(logits)
-    a.logits = logits.data_ptr()
-    a.stride_req, a.stride_branch, a.stride_pos = strides
-    a.logits_numel = _extent(logits)
     a.xt, a.k_step, a.is_commit = _ptr(xt_c), ks_c.data_ptr(), ic_c.data_ptr()
     a.log_prior, a.sched_t, a.q_t = lp_c.data_ptr(), st_c.data_ptr(), qt_c.data_ptr()
     a.cfg_scale = float(cfg_scale)
@@ -285,11 +233,169 @@ def select_step(logits: torch.Tensor, xt: torch.Tensor, k_step: torch.Tensor,
         if positions_sampled.dtype != torch.int64 or positions_sampled.numel() < 1 or positions_sampled.device != dev:
             raise ValueError("positions_sampled must be an int64 device tensor")
         a.positions_sampled = positions_sampled.data_ptr()
+    return out
+
+
+def select_step(logits: torch.Tensor, xt: torch.Tensor, k_step: torch.Tensor,
+                is_commit: torch.Tensor, log_prior: torch.Tensor, sched_t: torch.Tensor,
+                q_t: torch.Tensor, *, cfg_scale: float, mask_id: int, stop_id: int,
+                temperature=0.6, top_k=0, top_p=1.0, min_p=0.0, rep_penalty=1.0,
+                history=None, pmi_lambda: float = 1.0, pos_noise: bool = True,
+                use_quantile: bool = True, gumbel_tok: torch.Tensor | None = None,
+                gumbel_pos: torch.Tensor | None = None, seed: int = 0, offset: int = 0,
+                zero_temp_greedy: bool = True, dense: bool = False,
+                out: SelectOutputs | None = None,
+                prof_events: tuple | None = None, engine: EngineBuffers | None = None,
+                L: int | None = None, positions_sampled: torch.Tensor | None = None,
+                wait_limit_ns: int = 0, quantile_lerp: bool = False) -> SelectOutputs:
+    """One block-diffusion select step (``server/engine.py:533-622``).
+
+    ``nb`` is 2 when ``cfg_scale > 0`` (conditional + unconditional rows) and 1
+    otherwise, as ``FlashEngine.n_branch`` (``server/engine.py:322``).  Noise is
+    explicit when ``gumbel_tok`` (``(B, L, V)``) and ``gumbel_pos`` (``(B, L)``)
+    are given, else generated in-kernel from ``(seed, offset)``.  With
+    ``engine`` the step also writes the engine's token buffer, block / cache
+    offsets and flags; ``xt`` may then be None (the block is gathered from
+    ``engine.xt_full`` in the kernels, ``L`` giving its length).
+    ``positions_sampled``, a one-element int64 device tensor, is incremented
+    by the number of positions the step samples.  ``wait_limit_ns`` bounds
+    each pipeline wait (0: 0.5 s; negative: every pipeline wait gives up at
+    once, for testing the failure path).  ``quantile_lerp`` selects
+    torch.quantile's interpolation for the unmask threshold (the offline block
+    loop's, ``chatterbox_flash/model.py:284``) instead of the engine's.
+    ``logits`` may also be a ``(B, nb, L, V)`` view with any strides and a
+    unit last stride (e.g. the offline loop's ``[cond rows; uncond rows]``
+    layout seen as ``(2, B, L, V).transpose(0, 1)``).
+    """
+    if not logits.is_cuda:
+        raise ValueError("select_step runs on CUDA tensors only (no CPU fallback)")
+    if xt is None:
+        if engine is None or L is None:
+            raise ValueError("xt=None needs engine buffers and the block length L")
+        B = engine.blk_start.shape[0]
+    else:
+        B, L = xt.shape
+    nb = 2 if cfg_scale > 0 else 1
+    if logits.dim() == 4:
+        if tuple(logits.shape[:3]) != (B, nb, L):
+            raise ValueError(f"logits must be ({B}, {nb}, {L}, V), got {tuple(logits.shape)}")
+        if logits.stride(3) != 1:
+            logits = logits.contiguous()
+        strides = (logits.stride(0), logits.stride(1), logits.stride(2))
+    else:
+        if logits.dim() != 3 or logits.shape[0] != B * nb or logits.shape[1] != L:
+            raise ValueError(f"logits must be ({B * nb}, {L}, V), got {tuple(logits.shape)}")
+        if logits.stride(2) != 1:
+            logits = logits.contiguous()
+        strides = (logits.stride(0) * nb, logits.stride(0), logits.stride(1))
+    V = logits.shape[-1]
+    dev = logits.device
+    a = N.SelectArgs()
+    a.logits_dtype = _dtype_code(logits)
+    a.logits = logits.data_ptr()
+    a.stride_req, a.stride_branch, a.stride_pos = strides
+    a.logits_numel = _extent(logits)
+    keep = []
+    out = _common_args(a, B, nb, L, V, dev, keep, xt, k_step, is_commit, log_prior, sched_t, q_t,
+                       cfg_scale=cfg_scale, mask_id=mask_id, stop_id=stop_id, temperature=temperature,
+                       top_k=top_k, top_p=top_p, min_p=min_p, rep_penalty=rep_penalty, history=history,
+                       pmi_lambda=pmi_lambda, pos_noise=pos_noise, use_quantile=use_quantile,
+                       gumbel_tok=gumbel_tok, gumbel_pos=gumbel_pos, seed=seed, offset=offset,
+                       zero_temp_greedy=zero_temp_greedy, dense=dense, out=out, prof_events=prof_events,
+                       engine=engine, positions_sampled=positions_sampled, wait_limit_ns=wait_limit_ns,
+                       quantile_lerp=quantile_lerp)
     need = N.lib().yapd_select_workspace_size(B, L)
     ws = workspace(need, dev)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     stream = torch.cuda.current_stream(dev).cuda_stream
     N.check(N.lib().yapd_select_step(C.byref(a), C.c_void_p(stream)))
+    return out
+
+
+_LM_WORKSPACES: dict = {}
+
+
+def lm_workspace(nbytes: int, device) -> torch.Tensor:
+    """The fused head's cached workspace on ``device`` (status word first),
+    separate from ``workspace`` because the two layouts differ; the
+    one-stream rule of ``workspace`` holds for it too."""
+    dev = torch.device(device)
+    key = (dev.type, dev.index if dev.index is not None else torch.cuda.current_device())
+    ws = _LM_WORKSPACES.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 4096), dtype=torch.uint8, device=dev)
+        _LM_WORKSPACES[key] = ws
+    return ws
+
+
+def lmhead_select_step(hidden: torch.Tensor, weight: torch.Tensor, xt: torch.Tensor | None,
+                       k_step: torch.Tensor, is_commit: torch.Tensor, log_prior: torch.Tensor,
+                       sched_t: torch.Tensor, q_t: torch.Tensor, *, cfg_scale: float, mask_id: int,
+                       stop_id: int, temperature=0.6, rep_penalty=1.0, history=None,
+                       pmi_lambda: float = 1.0, pos_noise: bool = True, use_quantile: bool = True,
+                       gumbel_tok: torch.Tensor | None = None, gumbel_pos: torch.Tensor | None = None,
+                       seed: int = 0, offset: int = 0, zero_temp_greedy: bool = True, dense: bool = False,
+                       out: SelectOutputs | None = None, prof_events: tuple | None = None,
+                       engine: EngineBuffers | None = None, L: int | None = None,
+                       positions_sampled: torch.Tensor | None = None, wait_limit_ns: int = 0,
+                       quantile_lerp: bool = False, logits_out: torch.Tensor | None = None) -> SelectOutputs:
+    """The speech head and the select step in one call: ``logits =
+    hidden @ weight.T`` (``server/engine.py:517-520``) on the tensor cores,
+    with the select step (``server/engine.py:533-622``) run on the GEMM's
+    accumulators, so the logits never reach device memory.
+
+    ``hidden``: bf16 ``(B, 2, L, D)`` (cond rows, then uncond rows per
+    request) with a unit last stride and strides that are multiples of 8;
+    ``weight``: bf16 ``(V, D)``.  The sampling chain is temperature, repetition
+    penalty (``>= 1``; history as a bool ``(B, V)`` tensor, converted to a
+    bitmap here, or an int32 bitmap) and Gumbel-max: no top-k, top-p or min-p.
+    ``logits_out``, an fp32 ``(B, 2, L, V)`` tensor, receives the logits the
+    epilogue consumed (for testing).  Everything else is as in ``select_step``.
+    """
+    if not hidden.is_cuda:
+        raise ValueError("lmhead_select_step runs on CUDA tensors only (no CPU fallback)")
+    if hidden.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise TypeError("hidden and weight must be bfloat16")
+    if hidden.dim() != 4 or hidden.shape[1] != 2:
+        raise ValueError(f"hidden must be (B, 2, L, D), got {tuple(hidden.shape)}")
+    B, _, Lh, D = hidden.shape
+    if xt is not None and tuple(xt.shape) != (B, Lh):
+        raise ValueError(f"xt must be ({B}, {Lh})")
+    L = Lh
+    if hidden.stride(3) != 1 or any(st % 8 for st in hidden.stride()[:3]):
+        hidden = hidden.contiguous()
+    if weight.dim() != 2 or weight.shape[1] != D:
+        raise ValueError(f"weight must be (V, {D})")
+    if weight.stride(1) != 1 or weight.stride(0) % 8:
+        weight = weight.contiguous()
+    V = weight.shape[0]
+    dev = hidden.device
+    if history is not None and history.dtype in (torch.bool, torch.uint8):
+        history = history_to_bitmap(history.to(dev).bool())
+    h = N.LmheadArgs()
+    h.hidden = hidden.data_ptr()
+    h.h_stride_req, h.h_stride_branch, h.h_stride_pos = hidden.stride(0), hidden.stride(1), hidden.stride(2)
+    h.hidden_numel = _extent(hidden)
+    h.weight, h.w_stride, h.weight_numel = weight.data_ptr(), weight.stride(0), _extent(weight)
+    h.D = D
+    if logits_out is not None:
+        if logits_out.dtype != torch.float32 or tuple(logits_out.shape) != (B, 2, L, V) or \
+                not logits_out.is_contiguous():
+            raise ValueError(f"logits_out must be a contiguous float32 ({B}, 2, {L}, {V}) tensor")
+        h.logits_out = logits_out.data_ptr()
+    keep = [hidden, weight, history]
+    out = _common_args(h.select, B, 2, L, V, dev, keep, xt, k_step, is_commit, log_prior, sched_t, q_t,
+                       cfg_scale=cfg_scale, mask_id=mask_id, stop_id=stop_id, temperature=temperature,
+                       top_k=0, top_p=1.0, min_p=0.0, rep_penalty=rep_penalty, history=history,
+                       pmi_lambda=pmi_lambda, pos_noise=pos_noise, use_quantile=use_quantile,
+                       gumbel_tok=gumbel_tok, gumbel_pos=gumbel_pos, seed=seed, offset=offset,
+                       zero_temp_greedy=zero_temp_greedy, dense=dense, out=out, prof_events=prof_events,
+                       engine=engine, positions_sampled=positions_sampled, wait_limit_ns=wait_limit_ns,
+                       quantile_lerp=quantile_lerp)
+    ws = lm_workspace(N.lib().yapd_lmhead_workspace_size(B, L), dev)
+    h.select.workspace, h.select.workspace_bytes = ws.data_ptr(), ws.numel()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    N.check(N.lib().yapd_lmhead_select_step(C.byref(h), C.c_void_p(stream)))
     return out
 
 
@@ -340,10 +446,11 @@ def sample_rows(logits: torch.Tensor, *, temperature=0.8, top_k=0, top_p=1.0, mi
     return out
 
 
-def read_status(device=None) -> int:
-    """Device status word of the device's workspace (synchronises the current stream)."""
+def read_status(device=None, lmhead: bool = False) -> int:
+    """Device status word of the device's workspace, or with ``lmhead`` of the
+    fused head's (synchronises the current stream)."""
     dev = torch.device(device or "cuda")
-    ws = workspace(256, dev)
+    ws = lm_workspace(256, dev) if lmhead else workspace(256, dev)
     v = C.c_uint32(0)
     N.check(N.lib().yapd_read_status(C.c_void_p(ws.data_ptr()),
                                      C.c_void_p(torch.cuda.current_stream(dev).cuda_stream),
@@ -351,9 +458,10 @@ def read_status(device=None) -> int:
     return v.value
 
 
-def clear_status(device=None) -> None:
-    """Zero the status word of the device's workspace (enqueued on the current stream)."""
+def clear_status(device=None, lmhead: bool = False) -> None:
+    """Zero the status word of the device's workspace, or with ``lmhead`` of the
+    fused head's (enqueued on the current stream)."""
     dev = torch.device(device or "cuda")
-    ws = workspace(256, dev)
+    ws = lm_workspace(256, dev) if lmhead else workspace(256, dev)
     N.check(N.lib().yapd_clear_status(C.c_void_p(ws.data_ptr()),
                                       C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)))

@@ -181,6 +181,78 @@ __device__ __forceinline__ float gumbel_approx(uint32_t w) {
   return __fmul_rn(-lg2_approx(E), kLn2);
 }
 
+// Philox4x32-10 (philox.cuh) for the token noise of one position: the
+// counter is (q, pos, off_lo, off_hi & 0x7fffffff) with only q varying, so
+// the products of the first two rounds that involve the other words are
+// computed once per position.
+struct PhiloxPos {
+  uint32_t k0, k1;          // key
+  uint32_t c3;              // counter word 3
+  uint32_t r1w0, r1w1;      // round-1 output words 0 and 1 (independent of q)
+  uint32_t r2hi0, r2lo0;    // round 2: M0 * (round-1 word 0)
+};
+constexpr uint32_t kPhM0 = 0xD2511F53u, kPhM1 = 0xCD9E8D57u, kPhW0 = 0x9E3779B9u, kPhW1 = 0xBB67AE85u;
+
+__device__ __forceinline__ PhiloxPos philox_pos(uint64_t seed, uint64_t offset, uint32_t pos) {
+  PhiloxPos S;
+  S.k0 = (uint32_t)seed;
+  S.k1 = (uint32_t)(seed >> 32);
+  S.c3 = (uint32_t)(offset >> 32) & 0x7fffffffu;
+  const uint32_t c2 = (uint32_t)offset;
+  S.r1w0 = __umulhi(kPhM1, c2) ^ pos ^ S.k0;
+  S.r1w1 = kPhM1 * c2;
+  S.r2hi0 = __umulhi(kPhM0, S.r1w0);
+  S.r2lo0 = kPhM0 * S.r1w0;
+  return S;
+}
+
+// The 16 words of counter blocks q0 .. q0+3 (tokens 4*q0 .. 4*q0+15).
+__device__ __forceinline__ void philox_x4(const PhiloxPos& S, uint32_t q0, uint32_t (&w)[16]) {
+  uint32_t c0[4], c1[4], c2[4], c3[4];
+  uint32_t k0 = S.k0, k1 = S.k1;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {  // round 1
+    const uint32_t q = q0 + (uint32_t)i;
+    c0[i] = S.r1w0;
+    c1[i] = S.r1w1;
+    c2[i] = __umulhi(kPhM0, q) ^ S.c3 ^ k1;
+    c3[i] = kPhM0 * q;
+  }
+  k0 += kPhW0;
+  k1 += kPhW1;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {  // round 2: word 0 is the same for every block
+    const uint32_t hi1 = __umulhi(kPhM1, c2[i]), lo1 = kPhM1 * c2[i];
+    const uint32_t n0 = hi1 ^ c1[i] ^ k0, n2 = S.r2hi0 ^ c3[i] ^ k1;
+    c0[i] = n0;
+    c1[i] = lo1;
+    c2[i] = n2;
+    c3[i] = S.r2lo0;
+  }
+#pragma unroll
+  for (int r = 2; r < 10; ++r) {
+    k0 += kPhW0;
+    k1 += kPhW1;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t hi0 = __umulhi(kPhM0, c0[i]), lo0 = kPhM0 * c0[i];
+      const uint32_t hi1 = __umulhi(kPhM1, c2[i]), lo1 = kPhM1 * c2[i];
+      const uint32_t n0 = hi1 ^ c1[i] ^ k0, n2 = hi0 ^ c3[i] ^ k1;
+      c0[i] = n0;
+      c1[i] = lo1;
+      c2[i] = n2;
+      c3[i] = lo0;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    w[4 * i + 0] = c0[i];
+    w[4 * i + 1] = c1[i];
+    w[4 * i + 2] = c2[i];
+    w[4 * i + 3] = c3[i];
+  }
+}
+
 __device__ __forceinline__ void lm_abort(LmSmem& sm, uint32_t* status) {
   *reinterpret_cast<volatile int*>(&sm.abort_flag) = 1;
   if (status) atomicOr(status, YAPD_STATUS_WAIT_TIMEOUT);
@@ -306,6 +378,7 @@ struct EpiRow {
   const uint32_t* hrow;      // the request's history bitmap row (pen_on)
   float m, S;                // this row's max and sum of exp(x - m) over the columns seen
   float Bh, Mb;              // running max of unpenalised approximate scores, its magnitude
+  PhiloxPos ph;              // the position's token-noise generator state
   int kv[KEEP];              // kept tokens (-1: free slot) with their logits,
   float kc[KEEP], ku[KEEP];  // approximate scores and magnitudes
   float ks[KEEP], km[KEEP];
@@ -353,10 +426,12 @@ __device__ __forceinline__ void keep_raise(EpiRow& R, float s, float mag) {
   }
 }
 
-// One 32-column chunk of this thread's accumulator row.
+// One 32-column chunk of this thread's accumulator row; FULL: all 32 columns
+// are tokens (every chunk but the vocabulary's last).
+template <bool FULL>
 __device__ __forceinline__ void epi_chunk(const SampleParams& P, const LmParams& Q, LmSmem& sm, EpiRow& R,
                                           const float (&x)[32], int v0, int part, int pl, int br, bool dump) {
-  const int nval = min(32, Q.V - v0);
+  const int nval = FULL ? 32 : min(32, Q.V - v0);
   if (dump) {
     float* drow = Q.dump + (((int64_t)R.b * 2 + br) * Q.L + R.l) * Q.V + v0;
 #pragma unroll
@@ -375,77 +450,108 @@ __device__ __forceinline__ void epi_chunk(const SampleParams& P, const LmParams&
     uv[j] = br ? x[16 + j] : got;
   }
   if (R.act) {
-  // statistics of the own row
-  {
-    float cm0 = kNegInf, cm1 = kNegInf;
+    // statistics of the own row (four independent chains)
+    float c4[4] = {kNegInf, kNegInf, kNegInf, kNegInf};
 #pragma unroll
-    for (int j = 0; j < 32; j += 2) {
-      if (j < nval) cm0 = fmaxf(cm0, x[j]);
-      if (j + 1 < nval) cm1 = fmaxf(cm1, x[j + 1]);
-    }
-    const float cm = fmaxf(cm0, cm1);
+    for (int j = 0; j < 32; ++j)
+      if (j < nval) c4[j & 3] = fmaxf(c4[j & 3], x[j]);
+    const float cm = fmaxf(fmaxf(c4[0], c4[1]), fmaxf(c4[2], c4[3]));
     if (cm > R.m) {
       R.S = __fmul_rn(R.S, ex2_approx(__fmul_rn(__fsub_rn(R.m, cm), kLog2e)));
       R.m = cm;
     }
     const float ml = -__fmul_rn(R.m, kLog2e);
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    float a4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int j = 0; j < 32; j += 4) {
-      if (j < nval) a0 = __fadd_rn(a0, ex2_approx(__fmaf_rn(x[j], kLog2e, ml)));
-      if (j + 1 < nval) a1 = __fadd_rn(a1, ex2_approx(__fmaf_rn(x[j + 1], kLog2e, ml)));
-      if (j + 2 < nval) a2 = __fadd_rn(a2, ex2_approx(__fmaf_rn(x[j + 2], kLog2e, ml)));
-      if (j + 3 < nval) a3 = __fadd_rn(a3, ex2_approx(__fmaf_rn(x[j + 3], kLog2e, ml)));
-    }
-    R.S = __fadd_rn(R.S, __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)));
-  }
-  // approximate scores of this thread's 16 tokens
-  const int vb = v0 + br * 16;
-  const int nv = min(16, Q.V - vb);
-  if (nv > 0) {
-  uint32_t hb = 0u;
-  if (R.pen_on) hb = (__ldg(R.hrow + (vb >> 5)) >> (vb & 31)) & 0xffffu;
-  float G[16];
-  if (R.noisy) {
-    if (P.noise_kind == YAPD_NOISE_EXPLICIT) {
-      const float* gr = P.gumbel_tok + (int64_t)R.b * P.gt_stride_req + (int64_t)R.l * P.gt_stride_pos + vb;
+    for (int j = 0; j < 32; ++j)
+      if (j < nval) a4[j & 3] = __fadd_rn(a4[j & 3], ex2_approx(__fmaf_rn(x[j], kLog2e, ml)));
+    R.S = __fadd_rn(R.S, __fadd_rn(__fadd_rn(a4[0], a4[1]), __fadd_rn(a4[2], a4[3])));
+    // approximate scores of this thread's 16 tokens
+    const int vb = v0 + br * 16;
+    const int nv = FULL ? 16 : min(16, Q.V - vb);
+    if (nv > 0) {
+      uint32_t hb = 0u;
+      if (R.pen_on) hb = (__ldg(R.hrow + (vb >> 5)) >> (vb & 31)) & 0xffffu;
+      // approximate scores need no particular rounding (the margins cover it)
+      float y[16];
+      float ym[2] = {kNegInf, kNegInf}, ca[2] = {0.f, 0.f}, ua[2] = {0.f, 0.f};
 #pragma unroll
-      for (int j = 0; j < 16; ++j) G[j] = j < nv ? __ldg(gr + j) : 0.f;
-    } else {
+      for (int j = 0; j < 16; ++j) {
+        y[j] = __fmaf_rn(R.A, cv[j], -__fmul_rn(R.Bc, uv[j]));
+        if (j < nv) {
+          ym[j & 1] = fmaxf(ym[j & 1], y[j]);
+          ca[j & 1] = fmaxf(ca[j & 1], fabsf(cv[j]));
+          ua[j & 1] = fmaxf(ua[j & 1], fabsf(uv[j]));
+        }
+      }
+      const float ymax = fmaxf(ym[0], ym[1]);
+      // Bound of keep_margin over this chunk's tokens: mag <= |A||c| +
+      // |Bc||u| <= mgmax, |y| <= mgmax, |G| < 17 for 24-bit uniforms; plus the
+      // error of the approximate Gumbel and of the FMA form of y.
+      const float mgmax = __fmaf_rn(fabsf(R.A), fmaxf(ca[0], ca[1]), __fmul_rn(fabsf(R.Bc), fmaxf(ua[0], ua[1]))) *
+                          1.0001f;
+      const float mb = 2.2e-3f + 2e-5f * (2.0f * mgmax + R.Mb + 17.0f + fabsf(R.Bh));
+      uint32_t w[16];
+      uint32_t surv = 0u;  // tokens that may pass the keep test
+      const bool philox = R.noisy && P.noise_kind != YAPD_NOISE_EXPLICIT;
+      if (philox) {
+        philox_x4(R.ph, (uint32_t)(vb >> 2), w);
+        // Gumbel noise obeys G = -ln(-ln u) <= -ln(1 - u) (as -ln u >= 1 - u).
+        // A token passes the keep test only if y + G >= Bh - keep_margin,
+        // which needs G >= T = Bh - ymax - mb, i.e. 1 - u <= e^-T: every token
+        // with a smaller uniform is ruled out by one integer compare.
+        int kthr = 0;
+        const float T = R.Bh - ymax - mb;
+        if (R.Bh > kNegInf && T > 0.0f) {
+          const float q = ex2_approx(-T * kLog2e) * 1.0001f;  // e^-T, rounded up past ex2.approx's error
+          const float f = (1.0f - q) * 16777216.0f;
+          kthr = f > 1.0f ? (int)f - 1 : 0;
+        }
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const Philox4 r = philox4x32_10((uint32_t)(vb >> 2) + (uint32_t)q, (uint32_t)R.p, (uint32_t)P.offset,
-                                        (uint32_t)(P.offset >> 32) & 0x7fffffffu, (uint32_t)P.seed,
-                                        (uint32_t)(P.seed >> 32));
-        G[4 * q + 0] = gumbel_approx(r.x);
-        G[4 * q + 1] = gumbel_approx(r.y);
-        G[4 * q + 2] = gumbel_approx(r.z);
-        G[4 * q + 3] = gumbel_approx(r.w);
+        for (int j = 0; j < 16; ++j)
+          if (j < nv && (int)(w[j] >> 8) >= kthr) surv |= 1u << j;
+      } else if (R.noisy) {
+        surv = nv >= 16 ? 0xffffu : ((1u << nv) - 1u);  // explicit noise (parity tests): every token
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (j < nv && y[j] >= R.Bh - mb) surv |= 1u << j;
+      }
+      while (surv) {
+        const int j = __ffs(surv) - 1;
+        surv &= surv - 1u;
+        float yj = 0.f, cj = 0.f, uj = 0.f;
+        uint32_t wj = 0u;
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+          if (k == j) {
+            yj = y[k];
+            cj = cv[k];
+            uj = uv[k];
+            wj = w[k];
+          }
+        const float mgj = __fmaf_rn(fabsf(R.A), fabsf(cj), __fmul_rn(fabsf(R.Bc), fabsf(uj))) * 1.0001f;
+        float G = 0.f;
+        if (philox)
+          G = gumbel_approx(wj);
+        else if (R.noisy)
+          G = __ldg(P.gumbel_tok + (int64_t)R.b * P.gt_stride_req + (int64_t)R.l * P.gt_stride_pos + vb + j);
+        const float sc = R.noisy ? __fadd_rn(yj, G) : yj;
+        if (sc >= R.Bh - keep_margin(R, mgj, sc)) {
+          if (!((hb >> j) & 1u)) keep_raise(R, sc, mgj);  // penalised tokens never raise it
+          if (!keep_insert(R, vb + j, cj, uj, sc, mgj)) {
+            // registers full (a cluster of penalised tokens above the running
+            // maximum): the token goes to the position's list in memory
+            const int slot = atomicAdd(&sm.spl[pl], 1);
+            if (slot < SPILL)
+              Q.cands[((size_t)R.p * PARTS_MAX + part) * CAP + slot] =
+                  make_int4(vb + j, __float_as_int(cj), __float_as_int(uj), 0);
+            else
+              R.ovf = true;
+          }
+        }
       }
     }
-  }
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    if (j >= nv) break;
-    const float ac = __fmul_rn(R.A, cv[j]), bu = __fmul_rn(R.Bc, uv[j]);
-    const float y = __fsub_rn(ac, bu);
-    const float s = R.noisy ? __fadd_rn(y, G[j]) : y;
-    const float mag = __fadd_rn(fabsf(ac), fabsf(bu));
-    if (s >= R.Bh - keep_margin(R, mag, s)) {
-      if (!((hb >> j) & 1u)) keep_raise(R, s, mag);  // penalised tokens never raise it
-      if (!keep_insert(R, vb + j, cv[j], uv[j], s, mag)) {
-        // registers full (a cluster of penalised tokens above the running
-        // maximum): the token goes to the position's list in memory
-        const int slot = atomicAdd(&sm.spl[pl], 1);
-        if (slot < SPILL)
-          Q.cands[((size_t)R.p * PARTS_MAX + part) * CAP + slot] =
-              make_int4(vb + j, __float_as_int(cv[j]), __float_as_int(uv[j]), 0);
-        else
-          R.ovf = true;
-      }
-    }
-  }
-  }
   }
   // the partner thread scans other tokens of the same position: its running
   // maximum bounds this stream's tokens as well
@@ -487,6 +593,7 @@ __device__ __forceinline__ void lm_epilogue(const SampleParams& P, const LmParam
       R.pen_on = P.history_kind == YAPD_HISTORY_BITMAP && P.history != nullptr && rep != 1.0f;
       R.noisy = T > 0.0f || !P.zero_temp_greedy;
       if (R.pen_on) R.hrow = reinterpret_cast<const uint32_t*>(P.history) + (int64_t)R.b * P.history_stride;
+      R.ph = philox_pos(P.seed, P.offset, (uint32_t)R.p);
     }
     R.m = kNegInf;
     R.S = 0.f;
@@ -524,7 +631,11 @@ __device__ __forceinline__ void lm_epilogue(const SampleParams& P, const LmParam
           __syncwarp();
           if (lane == 0) mbar_arrive(&sm.tempty[a]);
         }
-        epi_chunk(P, Q, sm, R, x, t * BN + c0 + ch * 32, part, pl, br, dump);
+        const int v0 = t * BN + c0 + ch * 32;
+        if (v0 + 32 <= Q.V)
+          epi_chunk<true>(P, Q, sm, R, x, v0, part, pl, br, dump);
+        else
+          epi_chunk<false>(P, Q, sm, R, x, v0, part, pl, br, dump);
       }
       if (nch == 0) {
         tc_fence_before();

@@ -78,6 +78,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=16)
+    ap.add_argument("--unfused", action="store_true",
+                    help="configuration 4: time the cuBLAS head GEMM + select step as the main line")
     return ap.parse_args()
 
 
@@ -159,6 +161,17 @@ def config_name(cfg: int) -> str:
 
 
 N_HIDDEN = 3  # rotating hidden-state buffers of config 4 (3 x 64 MB > L2)
+
+
+def cfg4_chain(inp):
+    """Configuration 4's sampling chain, the fused variant's epilogue (BASELINE:
+    PMI / CFG / penalty / sample / unmask): temperature, repetition penalty and
+    Gumbel-max, no top-k / top-p / min-p.  Every leg of configuration 4 (fused,
+    unfused, CPU) samples with it."""
+    inp.top_k = torch.zeros(inp.B, dtype=torch.int32)
+    inp.top_p = torch.ones(inp.B)
+    inp.min_p = torch.zeros(inp.B)
+    return inp
 LOGIT_PAD = 8200  # config 4 logits row length: V = 8194 rounded up to 8 (16 bytes)
 
 
@@ -168,7 +181,7 @@ def make_inputs(cfg: int, rank: int, device):
     Configuration 4 returns one logits buffer and a ``gemm`` dict holding the
     device operands of the head GEMM that fills it every step."""
     if cfg == 4:
-        inp = WL.make_config(4, seed=100 + rank, explicit_noise=False, lmhead_logits=False)
+        inp = cfg4_chain(WL.make_config(4, seed=100 + rank, explicit_noise=False, lmhead_logits=False))
         g = torch.Generator(device=device).manual_seed(7 + 131 * rank)
         hid = [inp.meta["hidden"].to(device)]
         for _ in range(N_HIDDEN - 1):
@@ -180,7 +193,7 @@ def make_inputs(cfg: int, rank: int, device):
         wp = torch.zeros(LOGIT_PAD, w.shape[1], dtype=w.dtype, device=device)
         wp[: w.shape[0]] = w
         out = torch.empty(hid[0].shape[0], LOGIT_PAD, dtype=torch.bfloat16, device=device)
-        gemm = {"hidden": hid, "weight": wp, "out": out}
+        gemm = {"hidden": hid, "weight": wp, "weight_v": w, "out": out}
         logits = out.view(inp.logits.shape[0], inp.logits.shape[1], LOGIT_PAD)[:, :, : inp.V]
         return inp, [logits], gemm
     inp = WL.make_config(cfg, seed=100 + rank, explicit_noise=False,
@@ -208,8 +221,8 @@ class Runner:
 
     G = 8
 
-    def __init__(self, inp, bufs, device, total_steps: int, gemm=None):
-        self.inp, self.bufs, self.dev, self.gemm = inp, bufs, device, gemm
+    def __init__(self, inp, bufs, device, total_steps: int, gemm=None, fused: bool = False):
+        self.inp, self.bufs, self.dev, self.gemm, self.fused = inp, bufs, device, gemm, fused
         B, L = inp.B, inp.L
         # enough blocks that no request reaches the end of its buffer: a block
         # takes at most K denoising ticks and one commit tick
@@ -238,6 +251,8 @@ class Runner:
         min_p = 0.0 if float(inp.min_p.max()) <= 0.0 else inp.min_p.to(device)
         bf = inp.logits.dtype == torch.bfloat16
         self.kernel = "wsample_kernel" if bf and not isinstance(min_p, float) else "sample_kernel"
+        if fused:
+            self.kernel = "lm_select_kernel"
         self.kw = dict(cfg_scale=inp.cfg_scale, mask_id=inp.mask_id, stop_id=inp.stop_id,
                        temperature=inp.temperature.to(device), top_k=inp.top_k.to(device),
                        top_p=inp.top_p.to(device), min_p=min_p,
@@ -251,7 +266,7 @@ class Runner:
         self.ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                    for _ in range(self.G)]
         self.gev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                    for _ in range(self.G)] if gemm else None
+                    for _ in range(self.G)] if gemm and not fused else None
         for a, b in self.ev + (self.gev or []):  # torch creates the CUDA events lazily
             a.record()
             b.record()
@@ -267,9 +282,19 @@ class Runner:
         self.blk.zero_()
         self.cache.zero_()
 
-    def step(self, k: int, prof: bool = True, dense: bool = False, logits=None):
+    def step(self, k: int, prof: bool = True, dense: bool = False, logits=None, hidden=None):
         """Step k of the cycle; `logits` (already on the device) replaces the
-        step's own logits buffer (and, in configuration 4, its head GEMM)."""
+        step's own logits buffer (and, in configuration 4, its head GEMM);
+        fused: `hidden` replaces the step's hidden-state buffer."""
+        if self.fused:
+            h = self.gemm["hidden"][k % len(self.gemm["hidden"])] if hidden is None else hidden
+            B, L = self.inp.B, self.L
+            kw = {k_: v for k_, v in self.kw.items() if k_ not in ("top_k", "top_p", "min_p")}
+            S.lmhead_select_step(h.view(B, 2, L, -1), self.gemm["weight_v"], None, self.k, self.c, self.lp,
+                                 self.sched, self.q, seed=1234, offset=k, out=self.out, dense=dense,
+                                 prof_events=self.ev[k] if prof else None, engine=self.eng, L=L,
+                                 positions_sampled=self.count, **kw)
+            return
         if self.gemm and logits is None:
             if prof:
                 record_event(self.gev[k][0])
@@ -357,6 +382,34 @@ def roofline_peak():
         return 6650.0, "fallback"
 
 
+def tensor_peak():
+    """Dense bf16 TFLOP/s: the measured burst figure (a kernel timed alone)."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured (burst)"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def timed_steps(R, warmup: int, steps: int, dist):
+    """Replay `warmup` then `steps` graphs of R's cycle; (device ms of the
+    timed steps, positions they sampled) on this rank."""
+    for i in range(warmup):
+        R.graphs[i % R.G].replay()
+    c0 = count_now(R)
+    if dist:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        R.graphs[(warmup + i) % R.G].replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1), count_now(R) - c0
+
+
 def committed_traffic(cfg: int):
     """DRAM bytes per sample-kernel launch from the committed ncu summary."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
@@ -412,6 +465,8 @@ def cpu_sample(cfg: int, seconds: float, B_s: int = 2):
     from oracle import select_oracle as O
     cpu_threads()
     inp = WL.make_config(cfg, seed=999, B=B_s, explicit_noise=False)
+    if cfg == 4:
+        cfg4_chain(inp)
     rows = 2 * inp.B * inp.L
     O.select_step(inp, noise="philox", seed=1, offset=0)
     n, t0 = 0, time.perf_counter()
@@ -439,6 +494,8 @@ def run_reference(args, ws, rank):
     from oracle import select_oracle as O
     cpu_threads()
     inp = WL.make_config(args.config, seed=999, B=B_s, explicit_noise=False)
+    if args.config == 4:
+        cfg4_chain(inp)
     rows = 2 * inp.B * inp.L
     for i in range(args.warmup):
         cpu_head(inp)
@@ -475,7 +532,8 @@ def run_ours(args, ws, rank, local):
     cfg = args.config
     inp, bufs, gemm = make_inputs(cfg, rank, dev)
     total = args.warmup + args.steps + Runner.G + args.e2e_steps + 8
-    R = Runner(inp, bufs, dev, total, gemm)
+    fused = cfg == 4 and not args.unfused
+    R = Runner(inp, bufs, dev, total, gemm, fused=fused)
     R.capture()
     G = R.G
     # warm-up (the state evolves: the timed steps see a running batch)
@@ -510,7 +568,7 @@ def run_ours(args, ws, rank, local):
     prof_pos = count_now(R) - c1
     order = [(args.warmup + args.steps + k) % G for k in range(G)]
     kern_ms = sum(event_ms(*R.ev[k]) for k in order)
-    gemm_ms = [event_ms(*R.gev[k]) for k in order] if gemm else None
+    gemm_ms = [event_ms(*R.gev[k]) for k in order] if R.gev else None
     byt = sum(algorithmic_bytes(inp, 0) for _ in range(G)) + (algorithmic_bytes(inp, prof_pos) -
                                                                algorithmic_bytes(inp, 0))
     achieved = byt / (kern_ms * 1e-3) / 1e9
@@ -542,6 +600,26 @@ def run_ours(args, ws, rank, local):
         ms_max, pos_all, dense_ms_max, dense_pos_all = ms, float(my_pos), dense_ms, float(dense_pos)
     rows_all = 2.0 * pos_all
     value = rows_all / (ms_max * 1e-3)
+
+    # ---- configuration 4: the unfused comparison (cuBLAS head GEMM, then
+    # the select step) over the same running batch ----
+    unf = None
+    if fused:
+        R2 = Runner(inp, bufs, dev, total, gemm, fused=False)
+        R2.capture()
+        u_ms, u_pos = timed_steps(R2, args.warmup, args.steps, dist)
+        if dist:
+            t = torch.tensor([u_ms, float(u_pos)], device=dev, dtype=torch.float64)
+            mx = t.clone()
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+            sm_ = t.clone()
+            dist.all_reduce(sm_, op=dist.ReduceOp.SUM)
+            u_ms, u_pos = float(mx[0]), float(sm_[1])
+        unf = {"value": 2.0 * u_pos / (u_ms * 1e-3), "unit": "rows/s", "ms_per_step": u_ms / args.steps,
+               "what": "cuBLAS bf16 head GEMM into 16-byte-aligned bf16 logits rows, then yapd_select_step "
+                       "(same inputs, parameters and noise)"}
+        del R2
+        R.restore()
 
     # ---- end to end through the public API with host buffers ----
     e2e = run_e2e(R, inp, dev, args.e2e_steps)
@@ -593,7 +671,26 @@ def run_ours(args, ws, rank, local):
             "clocks": ck,
             "cpu_baseline": cpu,
         }
-        if gemm:
+        if fused:
+            h = gemm["hidden"][0]
+            flop = 2.0 * h.shape[0] * h.shape[1] * inp.V  # useful flops: every row, V columns
+            kl = kern_ms / G
+            tp, tp_kind = tensor_peak()
+            ach = flop / (kl * 1e-3) / 1e12
+            line["roofline"] = {"bound": "tensor", "achieved": ach, "peak": tp, "unit": "TFLOP/s",
+                                "frac": ach / tp, "traffic": committed_traffic(cfg), "peak_kind": tp_kind,
+                                "traffic_source": "profiles/traffic.json (ncu dram__bytes per launch, committed)",
+                                "kernel": R.kernel, "kernel_ms_per_launch": kl, "flop_per_launch": flop}
+            line["config"].update({
+                "workload": f"config4 (fused): tcgen05 bf16 head GEMM [{h.shape[0]} x {h.shape[1]}] x "
+                            f"[{inp.V} x {h.shape[1]}]^T with the select epilogue on the accumulators "
+                            f"(no logits in HBM), then the resolve and state-update kernels; {inp.B} requests "
+                            f"x 2 CFG rows x {inp.L} positions, continuous batching; temperature, repetition "
+                            f"penalty and Gumbel-max",
+                "l2": f"{N_HIDDEN} rotating hidden-state buffers ({N_HIDDEN * h.numel() * 2 / 1e6:.0f} MB) > L2",
+                "unfused": unf})
+            line["gpu_launches"] = 3 * args.steps
+        elif gemm:
             h = gemm["hidden"][0]
             flop = 2.0 * h.shape[0] * h.shape[1] * inp.V  # useful flops (V columns)
             gm = sum(gemm_ms) / G
@@ -628,6 +725,13 @@ def run_e2e(R, inp, dev, steps):
     ox = torch.empty(R.out.xt.shape, dtype=torch.int64).pin_memory()
 
     def tick(i):
+        if R.fused:
+            dhid.copy_(pin[i % 2], non_blocking=True)
+            R.step(i % R.G, prof=False, hidden=dhid)
+            of.copy_(R.flags, non_blocking=True)
+            ox.copy_(R.out.xt, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            return
         if R.gemm:
             dhid.copy_(pin[i % 2], non_blocking=True)
             logits = R.head_gemm(dhid)

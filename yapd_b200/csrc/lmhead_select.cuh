@@ -50,7 +50,7 @@ constexpr int B_BYTES = BN * BK * 2;     // 32 KB
 constexpr int EPI_WARPS = 8;             // two per tensor-memory lane group
 constexpr int NTHREADS = 64 + EPI_WARPS * 32;
 constexpr int POS = 64;                  // positions per CTA tile
-constexpr int KEEP = 4;                  // kept tokens a thread holds in registers
+constexpr int KEEP = 2;                  // kept tokens a thread holds in registers
 constexpr int SPILL = 32;                // slots per (position, part) for tokens spilled from full registers
 constexpr int FLUSH = 4 * KEEP;          // slots for the registers' survivors: 4 threads per (position, part)
 constexpr int CAP = SPILL + FLUSH;
@@ -212,20 +212,20 @@ __device__ __forceinline__ void philox_x4(const PhiloxPos& S, uint32_t q0, uint3
   uint32_t k0 = S.k0, k1 = S.k1;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {  // round 1
-    const uint32_t q = q0 + (uint32_t)i;
+    const uint64_t p0 = (uint64_t)kPhM0 * (q0 + (uint32_t)i);  // one wide multiply: both halves
     c0[i] = S.r1w0;
     c1[i] = S.r1w1;
-    c2[i] = __umulhi(kPhM0, q) ^ S.c3 ^ k1;
-    c3[i] = kPhM0 * q;
+    c2[i] = (uint32_t)(p0 >> 32) ^ S.c3 ^ k1;
+    c3[i] = (uint32_t)p0;
   }
   k0 += kPhW0;
   k1 += kPhW1;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {  // round 2: word 0 is the same for every block
-    const uint32_t hi1 = __umulhi(kPhM1, c2[i]), lo1 = kPhM1 * c2[i];
-    const uint32_t n0 = hi1 ^ c1[i] ^ k0, n2 = S.r2hi0 ^ c3[i] ^ k1;
+    const uint64_t p1 = (uint64_t)kPhM1 * c2[i];
+    const uint32_t n0 = (uint32_t)(p1 >> 32) ^ c1[i] ^ k0, n2 = S.r2hi0 ^ c3[i] ^ k1;
     c0[i] = n0;
-    c1[i] = lo1;
+    c1[i] = (uint32_t)p1;
     c2[i] = n2;
     c3[i] = S.r2lo0;
   }
@@ -235,13 +235,12 @@ __device__ __forceinline__ void philox_x4(const PhiloxPos& S, uint32_t q0, uint3
     k1 += kPhW1;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const uint32_t hi0 = __umulhi(kPhM0, c0[i]), lo0 = kPhM0 * c0[i];
-      const uint32_t hi1 = __umulhi(kPhM1, c2[i]), lo1 = kPhM1 * c2[i];
-      const uint32_t n0 = hi1 ^ c1[i] ^ k0, n2 = hi0 ^ c3[i] ^ k1;
+      const uint64_t p0 = (uint64_t)kPhM0 * c0[i], p1 = (uint64_t)kPhM1 * c2[i];
+      const uint32_t n0 = (uint32_t)(p1 >> 32) ^ c1[i] ^ k0, n2 = (uint32_t)(p0 >> 32) ^ c3[i] ^ k1;
       c0[i] = n0;
-      c1[i] = lo1;
+      c1[i] = (uint32_t)p1;
       c2[i] = n2;
-      c3[i] = lo0;
+      c3[i] = (uint32_t)p0;
     }
   }
 #pragma unroll
@@ -500,16 +499,22 @@ __device__ __forceinline__ void epi_chunk(const SampleParams& P, const LmParams&
         // A token passes the keep test only if y + G >= Bh - keep_margin,
         // which needs G >= T = Bh - ymax - mb, i.e. 1 - u <= e^-T: every token
         // with a smaller uniform is ruled out by one integer compare.
-        int kthr = 0;
+        uint32_t kthr = 0u;  // in units of the word: uniform u >= k * 2^-24 iff word >= k << 8
         const float T = R.Bh - ymax - mb;
         if (R.Bh > kNegInf && T > 0.0f) {
           const float q = ex2_approx(-T * kLog2e) * 1.0001f;  // e^-T, rounded up past ex2.approx's error
           const float f = (1.0f - q) * 16777216.0f;
-          kthr = f > 1.0f ? (int)f - 1 : 0;
+          kthr = f > 1.0f ? ((uint32_t)f - 1u) << 8 : 0u;
         }
+        uint32_t wmax = 0u;
 #pragma unroll
         for (int j = 0; j < 16; ++j)
-          if (j < nv && (int)(w[j] >> 8) >= kthr) surv |= 1u << j;
+          if (j < nv) wmax = max(wmax, w[j]);
+        if (wmax >= kthr) {  // rarely: build the mask
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (j < nv && w[j] >= kthr) surv |= 1u << j;
+        }
       } else if (R.noisy) {
         surv = nv >= 16 ? 0xffffu : ((1u << nv) - 1u);  // explicit noise (parity tests): every token
       } else {

@@ -47,12 +47,13 @@ constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
 constexpr int A_SUB = 32 * BK * 2;       // one 32-row group of the hidden tile: 4 KB
 constexpr int A_BYTES = BM * BK * 2;     // 16 KB
 constexpr int B_BYTES = BN * BK * 2;     // 32 KB
-constexpr int EPI_WARPS = 8;             // two per tensor-memory lane group
+constexpr int NG = 3;                    // epilogue warps per tensor-memory lane group
+constexpr int EPI_WARPS = 4 * NG;
 constexpr int NTHREADS = 64 + EPI_WARPS * 32;
 constexpr int POS = 64;                  // positions per CTA tile
 constexpr int KEEP = 2;                  // kept tokens a thread holds in registers
 constexpr int SPILL = 32;                // slots per (position, part) for tokens spilled from full registers
-constexpr int FLUSH = 4 * KEEP;          // slots for the registers' survivors: 4 threads per (position, part)
+constexpr int FLUSH = 2 * NG * KEEP;     // slots for the registers' survivors: 2 NG threads per (position, part)
 constexpr int CAP = SPILL + FLUSH;
 constexpr int PARTS_MAX = 8;
 constexpr uint32_t TMEM_COLS = 2 * BN;
@@ -60,7 +61,7 @@ constexpr uint32_t TMEM_COLS = 2 * BN;
 struct LmParams {
   int B, L, V, D, n_kb, NT, parts, n_mb, n_units, rpc, lh;
   uint32_t idesc_full, idesc_last;
-  float2* stats;        // [((p * PARTS_MAX + part) * 2 + half) * 2 + branch]: (max, sum exp(x - max))
+  float2* stats;        // [((p * PARTS_MAX + part) * NG + g) * 2 + branch]: (max, sum exp(x - max)) of warp g
   int32_t* counts;      // [p * PARTS_MAX + part]: 1 + spilled + (flushed << 16); 0 = not published
   int4* cands;          // [(p * PARTS_MAX + part) * CAP + slot]: (v, cond bits, uncond bits, 0); spilled
                         // tokens in slots [0, SPILL), the registers' survivors from SPILL on
@@ -206,12 +207,14 @@ __device__ __forceinline__ PhiloxPos philox_pos(uint64_t seed, uint64_t offset, 
   return S;
 }
 
-// The 16 words of counter blocks q0 .. q0+3 (tokens 4*q0 .. 4*q0+15).
-__device__ __forceinline__ void philox_x4(const PhiloxPos& S, uint32_t q0, uint32_t (&w)[16]) {
-  uint32_t c0[4], c1[4], c2[4], c3[4];
+// The 4 NB words of counter blocks q0 .. q0+NB-1 (tokens 4*q0 .. 4*(q0+NB)-1),
+// the blocks interleaved.
+template <int NB>
+__device__ __forceinline__ void philox_xn(const PhiloxPos& S, uint32_t q0, uint32_t (&w)[4 * NB]) {
+  uint32_t c0[NB], c1[NB], c2[NB], c3[NB];
   uint32_t k0 = S.k0, k1 = S.k1;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {  // round 1
+  for (int i = 0; i < NB; ++i) {  // round 1
     const uint64_t p0 = (uint64_t)kPhM0 * (q0 + (uint32_t)i);  // one wide multiply: both halves
     c0[i] = S.r1w0;
     c1[i] = S.r1w1;
@@ -221,7 +224,7 @@ __device__ __forceinline__ void philox_x4(const PhiloxPos& S, uint32_t q0, uint3
   k0 += kPhW0;
   k1 += kPhW1;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {  // round 2: word 0 is the same for every block
+  for (int i = 0; i < NB; ++i) {  // round 2: word 0 is the same for every block
     const uint64_t p1 = (uint64_t)kPhM1 * c2[i];
     const uint32_t n0 = (uint32_t)(p1 >> 32) ^ c1[i] ^ k0, n2 = S.r2hi0 ^ c3[i] ^ k1;
     c0[i] = n0;
@@ -234,7 +237,7 @@ __device__ __forceinline__ void philox_x4(const PhiloxPos& S, uint32_t q0, uint3
     k0 += kPhW0;
     k1 += kPhW1;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < NB; ++i) {
       const uint64_t p0 = (uint64_t)kPhM0 * c0[i], p1 = (uint64_t)kPhM1 * c2[i];
       const uint32_t n0 = (uint32_t)(p1 >> 32) ^ c1[i] ^ k0, n2 = (uint32_t)(p0 >> 32) ^ c3[i] ^ k1;
       c0[i] = n0;
@@ -244,7 +247,7 @@ __device__ __forceinline__ void philox_x4(const PhiloxPos& S, uint32_t q0, uint3
     }
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < NB; ++i) {
     w[4 * i + 0] = c0[i];
     w[4 * i + 1] = c1[i];
     w[4 * i + 2] = c2[i];
@@ -374,6 +377,7 @@ struct EpiRow {
   bool act, pen_on, noisy, ovf;
   int b, l, p;
   float A, Bc;               // y = A*c - Bc*u ~ guided/T up to a per-position constant
+  float Am, Bg;              // the same as Am * (own row) + Bg * (partner's row)
   const uint32_t* hrow;      // the request's history bitmap row (pen_on)
   float m, S;                // this row's max and sum of exp(x - m) over the columns seen
   float Bh, Mb;              // running max of unpenalised approximate scores, its magnitude
@@ -440,13 +444,12 @@ __device__ __forceinline__ void epi_chunk(const SampleParams& P, const LmParams&
   // the cond row's value of token j is in the lower half-warp, the uncond
   // row's in the upper: the lower thread scores tokens 0-15 of the chunk,
   // the upper one tokens 16-31
-  float cv[16], uv[16];
+  // mine: this thread's row at its tokens; got: the partner's row there
+  float mine[16], got[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    const float snd = br ? x[j] : x[16 + j];
-    const float got = __shfl_xor_sync(0xffffffffu, snd, 16);
-    cv[j] = br ? got : x[j];
-    uv[j] = br ? x[16 + j] : got;
+    got[j] = __shfl_xor_sync(0xffffffffu, br ? x[j] : x[16 + j], 16);
+    mine[j] = br ? x[16 + j] : x[j];
   }
   if (R.act) {
     // statistics of the own row (four independent chains)
@@ -465,40 +468,44 @@ __device__ __forceinline__ void epi_chunk(const SampleParams& P, const LmParams&
     for (int j = 0; j < 32; ++j)
       if (j < nval) a4[j & 3] = __fadd_rn(a4[j & 3], ex2_approx(__fmaf_rn(x[j], kLog2e, ml)));
     R.S = __fadd_rn(R.S, __fadd_rn(__fadd_rn(a4[0], a4[1]), __fadd_rn(a4[2], a4[3])));
-    // approximate scores of this thread's 16 tokens
-    const int vb = v0 + br * 16;
-    const int nv = FULL ? 16 : min(16, Q.V - vb);
-    if (nv > 0) {
-      uint32_t hb = 0u;
-      if (R.pen_on) hb = (__ldg(R.hrow + (vb >> 5)) >> (vb & 31)) & 0xffffu;
-      // approximate scores need no particular rounding (the margins cover it)
-      float y[16];
-      float ym[2] = {kNegInf, kNegInf}, ca[2] = {0.f, 0.f}, ua[2] = {0.f, 0.f};
+    // approximate scores of this thread's 16 tokens, in two halves of 8
+    // (shorter live ranges than one pass over 16)
+    const bool philox = R.noisy && P.noise_kind != YAPD_NOISE_EXPLICIT;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        y[j] = __fmaf_rn(R.A, cv[j], -__fmul_rn(R.Bc, uv[j]));
+    for (int hf = 0; hf < 2; ++hf) {
+      const int vb = v0 + br * 16 + hf * 8;
+      const int nv = FULL ? 8 : min(8, Q.V - vb);
+      if (nv <= 0) continue;
+      uint32_t hb = 0u;
+      if (R.pen_on) hb = (__ldg(R.hrow + (vb >> 5)) >> (vb & 31)) & 0xffu;
+      // approximate scores need no particular rounding (the margins cover
+      // it): y = A c - Bc u as Am * mine + Bg * got
+      float y[8];
+      float ym[2] = {kNegInf, kNegInf}, ma[2] = {0.f, 0.f}, ga[2] = {0.f, 0.f};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        y[j] = __fmaf_rn(R.Am, mine[hf * 8 + j], __fmul_rn(R.Bg, got[hf * 8 + j]));
         if (j < nv) {
           ym[j & 1] = fmaxf(ym[j & 1], y[j]);
-          ca[j & 1] = fmaxf(ca[j & 1], fabsf(cv[j]));
-          ua[j & 1] = fmaxf(ua[j & 1], fabsf(uv[j]));
+          ma[j & 1] = fmaxf(ma[j & 1], fabsf(mine[hf * 8 + j]));
+          ga[j & 1] = fmaxf(ga[j & 1], fabsf(got[hf * 8 + j]));
         }
       }
       const float ymax = fmaxf(ym[0], ym[1]);
-      // Bound of keep_margin over this chunk's tokens: mag <= |A||c| +
-      // |Bc||u| <= mgmax, |y| <= mgmax, |G| < 17 for 24-bit uniforms; plus the
-      // error of the approximate Gumbel and of the FMA form of y.
-      const float mgmax = __fmaf_rn(fabsf(R.A), fmaxf(ca[0], ca[1]), __fmul_rn(fabsf(R.Bc), fmaxf(ua[0], ua[1]))) *
-                          1.0001f;
+      // Bound of keep_margin over these tokens: mag <= |A||c| + |Bc||u| <=
+      // mgmax, |y| <= mgmax, |G| < 17 for 24-bit uniforms; plus the error of
+      // the approximate Gumbel and of the FMA form of y.
+      const float mgmax =
+          __fmaf_rn(fabsf(R.Am), fmaxf(ma[0], ma[1]), __fmul_rn(fabsf(R.Bg), fmaxf(ga[0], ga[1]))) * 1.0001f;
       const float mb = 2.2e-3f + 2e-5f * (2.0f * mgmax + R.Mb + 17.0f + fabsf(R.Bh));
-      uint32_t w[16];
+      uint32_t w[8];
       uint32_t surv = 0u;  // tokens that may pass the keep test
-      const bool philox = R.noisy && P.noise_kind != YAPD_NOISE_EXPLICIT;
       if (philox) {
-        philox_x4(R.ph, (uint32_t)(vb >> 2), w);
+        philox_xn<2>(R.ph, (uint32_t)(vb >> 2), w);
         // Gumbel noise obeys G = -ln(-ln u) <= -ln(1 - u) (as -ln u >= 1 - u).
         // A token passes the keep test only if y + G >= Bh - keep_margin,
-        // which needs G >= T = Bh - ymax - mb, i.e. 1 - u <= e^-T: every token
-        // with a smaller uniform is ruled out by one integer compare.
+        // which needs G >= T = Bh - ymax - mb, i.e. 1 - u <= e^-T: every
+        // token with a smaller uniform is ruled out by one integer compare.
         uint32_t kthr = 0u;  // in units of the word: uniform u >= k * 2^-24 iff word >= k << 8
         const float T = R.Bh - ymax - mb;
         if (R.Bh > kNegInf && T > 0.0f) {
@@ -508,33 +515,38 @@ __device__ __forceinline__ void epi_chunk(const SampleParams& P, const LmParams&
         }
         uint32_t wmax = 0u;
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
+        for (int j = 0; j < 8; ++j)
           if (j < nv) wmax = max(wmax, w[j]);
         if (wmax >= kthr) {  // rarely: build the mask
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
+          for (int j = 0; j < 8; ++j)
             if (j < nv && w[j] >= kthr) surv |= 1u << j;
         }
       } else if (R.noisy) {
-        surv = nv >= 16 ? 0xffffu : ((1u << nv) - 1u);  // explicit noise (parity tests): every token
+#pragma unroll
+        for (int j = 0; j < 8; ++j) w[j] = 0u;
+        surv = (1u << nv) - 1u;  // explicit noise (parity tests): every token
       } else {
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
+        for (int j = 0; j < 8; ++j) {
+          w[j] = 0u;
           if (j < nv && y[j] >= R.Bh - mb) surv |= 1u << j;
+        }
       }
       while (surv) {
         const int j = __ffs(surv) - 1;
         surv &= surv - 1u;
-        float yj = 0.f, cj = 0.f, uj = 0.f;
+        float yj = 0.f, mj = 0.f, gj = 0.f;
         uint32_t wj = 0u;
 #pragma unroll
-        for (int k = 0; k < 16; ++k)
+        for (int k = 0; k < 8; ++k)
           if (k == j) {
             yj = y[k];
-            cj = cv[k];
-            uj = uv[k];
+            mj = mine[hf * 8 + k];
+            gj = got[hf * 8 + k];
             wj = w[k];
           }
+        const float cj = br ? gj : mj, uj = br ? mj : gj;
         const float mgj = __fmaf_rn(fabsf(R.A), fabsf(cj), __fmul_rn(fabsf(R.Bc), fabsf(uj))) * 1.0001f;
         float G = 0.f;
         if (philox)
@@ -565,12 +577,13 @@ __device__ __forceinline__ void epi_chunk(const SampleParams& P, const LmParams&
   if (R.act) keep_raise(R, obh, omb);
 }
 
-// Epilogue warp: drains its lane group's accumulator rows (half of each
-// tile's columns), then publishes the unit's statistics and kept tokens.
+// Epilogue warp: drains its lane group's accumulator rows (every NG-th
+// 32-column chunk of each tile), then publishes the unit's statistics and
+// kept tokens.
 __device__ __forceinline__ void lm_epilogue(const SampleParams& P, const LmParams& Q, LmSmem& sm, uint32_t tbase,
                                             int warp, int lane) {
   const int sp = warp & 3;            // the lane group a warp may access is its warp id mod 4
-  const int h = (warp - 2) >> 2;      // column half of each tile
+  const int g = (warp - 2) >> 2;      // which of the lane group's NG warps
   const int t16 = lane & 15, br = lane >> 4;
   const int rql = sp / Q.lh, lhi = sp - rql * Q.lh;
   const int pl = sp * 16 + t16;
@@ -587,13 +600,15 @@ __device__ __forceinline__ void lm_epilogue(const SampleParams& P, const LmParam
     R.p = R.b * Q.L + R.l;
     R.act = !bad && lm_work(P, R.b, R.l) && lm_supported(P, R.b);
     R.pen_on = R.noisy = false;
-    R.A = R.Bc = 0.f;
+    R.A = R.Bc = R.Am = R.Bg = 0.f;
     R.hrow = nullptr;
     if (R.act) {
       const float T = param_f(P.temperature, P.temperature_s, R.b);
       const float sA = T > 0.0f ? __fdiv_rn(1.0f, T) : 1.0f;
       R.A = __fmul_rn(P.cfg_1pw, sA);
       R.Bc = __fmul_rn(P.cfg_w, sA);
+      R.Am = br ? -R.Bc : R.A;
+      R.Bg = br ? R.A : -R.Bc;
       const float rep = param_f(P.rep_penalty, P.rep_penalty_s, R.b);
       R.pen_on = P.history_kind == YAPD_HISTORY_BITMAP && P.history != nullptr && rep != 1.0f;
       R.noisy = T > 0.0f || !P.zero_temp_greedy;
@@ -615,28 +630,32 @@ __device__ __forceinline__ void lm_epilogue(const SampleParams& P, const LmParam
     for (int t = t0; t < t1; ++t) {
       const int a = tc & 1;
       const uint32_t aph = (uint32_t)(tc >> 1) & 1u;
+      // the tile's 32-column chunks c with c = rot (mod NG) are this warp's;
+      // the rotation moves with the tile so that the warps share the work
+      const int rot = (g + tc) % NG;
       ++tc;
       if (bad) continue;
-      const bool got = !lm_aborted(sm) && mbar_wait_bounded(&sm.tfull[a], aph, P.wait_ns);
-      if (!__all_sync(0xffffffffu, got)) {
+      const bool arrived = !lm_aborted(sm) && mbar_wait_bounded(&sm.tfull[a], aph, P.wait_ns);
+      if (!__all_sync(0xffffffffu, arrived)) {
         bad = true;
         lm_abort(sm, P.status);
         continue;
       }
       tc_fence_after();
-      const int c0 = h * (BN / 2);
       const int ncols = min(BN, Q.V - t * BN);
-      const int nch = (wact && ncols > c0) ? min(4, (ncols - c0 + 31) >> 5) : 0;
+      const int nct = wact ? (ncols + 31) >> 5 : 0;  // chunks of the tile that hold tokens
+      const int nch = nct > rot ? (nct - rot + NG - 1) / NG : 0;
       for (int ch = 0; ch < nch; ++ch) {
+        const int c = rot + ch * NG;
         float x[32];
         __syncwarp();
-        tmem_ld32(lane_addr + (uint32_t)(a * BN + c0 + ch * 32), x);
+        tmem_ld32(lane_addr + (uint32_t)(a * BN + c * 32), x);
         if (ch == nch - 1) {  // the buffer is free once its last columns are in registers
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&sm.tempty[a]);
         }
-        const int v0 = t * BN + c0 + ch * 32;
+        const int v0 = t * BN + c * 32;
         if (v0 + 32 <= Q.V)
           epi_chunk<true>(P, Q, sm, R, x, v0, part, pl, br, dump);
         else
@@ -649,7 +668,7 @@ __device__ __forceinline__ void lm_epilogue(const SampleParams& P, const LmParam
       }
     }
     if (R.act && !bad) {
-      Q.stats[(((size_t)R.p * PARTS_MAX + part) * 2 + h) * 2 + br] = make_float2(R.m, R.S);
+      Q.stats[(((size_t)R.p * PARTS_MAX + part) * NG + g) * 2 + br] = make_float2(R.m, R.S);
 #pragma unroll
       for (int k = 0; k < KEEP; ++k) {
         if (R.kv[k] < 0) continue;
@@ -660,7 +679,7 @@ __device__ __forceinline__ void lm_epilogue(const SampleParams& P, const LmParam
       if (R.ovf) atomicOr(P.status, YAPD_STATUS_CANDIDATE_OVERFLOW);
     }
     named_sync(1, EPI_WARPS * 32);
-    if (h == 0 && br == 0) {
+    if (g == 0 && br == 0) {
       const int nf = sm.cnt[pl], ns = min(sm.spl[pl], SPILL);
       // published only when no role of this CTA failed: the resolve kernel
       // takes a position whose parts are all published
@@ -751,8 +770,8 @@ __device__ __forceinline__ void resolve_position(const SampleParams& P, const Lm
     return;
   }
   float mc = kNegInf, sc = 0.f, mu = kNegInf, su = 0.f;
-  if (lane < 2 * Q.parts) {
-    const size_t e = ((base + (size_t)(lane >> 1)) * 2 + (size_t)(lane & 1)) * 2;
+  if (lane < NG * Q.parts) {
+    const size_t e = ((base + (size_t)(lane / NG)) * NG + (size_t)(lane % NG)) * 2;
     const float2 ec = Q.stats[e], eu = Q.stats[e + 1];
     mc = ec.x;
     sc = ec.y;
@@ -874,7 +893,7 @@ static size_t workspace_bytes(int32_t B, int32_t L) {
   if (B <= 0 || L <= 0) return 256;
   const size_t n = (size_t)B * (size_t)L;
   return 256 + align256(n * sizeof(float2)) + align256(n * PARTS_MAX * sizeof(int32_t)) +
-         align256(n * PARTS_MAX * 4 * sizeof(float2)) + align256(n * PARTS_MAX * CAP * sizeof(int4));
+         align256(n * PARTS_MAX * 2 * NG * sizeof(float2)) + align256(n * PARTS_MAX * CAP * sizeof(int4));
 }
 
 // Smallest number of token ranges per 64-position block whose units fill the
@@ -1016,7 +1035,7 @@ extern "C" int yapd_lmhead_select_step(const yapd_lmhead_args* h, void* stream) 
   Q.counts = reinterpret_cast<int32_t*>(ws + off);
   off += align256(n_pos * PARTS_MAX * sizeof(int32_t));
   Q.stats = reinterpret_cast<float2*>(ws + off);
-  off += align256(n_pos * PARTS_MAX * 4 * sizeof(float2));
+  off += align256(n_pos * PARTS_MAX * 2 * NG * sizeof(float2));
   Q.cands = reinterpret_cast<int4*>(ws + off);
   P.cfg_w = a->cfg_scale;
   P.cfg_1pw = a->cfg_one_plus;

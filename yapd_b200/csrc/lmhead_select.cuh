@@ -433,7 +433,8 @@ __device__ __forceinline__ void keep_raise(EpiRow& R, float s, float mag) {
 // are tokens (every chunk but the vocabulary's last).
 template <bool FULL>
 __device__ __forceinline__ void epi_chunk(const SampleParams& P, const LmParams& Q, LmSmem& sm, EpiRow& R,
-                                          const float (&x)[32], int v0, int part, int pl, int br, bool dump) {
+                                          const float (&x)[32], int v0, uint32_t hw, int part, int pl, int br,
+                                          bool dump) {
   const int nval = FULL ? 32 : min(32, Q.V - v0);
   if (dump) {
     float* drow = Q.dump + (((int64_t)R.b * 2 + br) * Q.L + R.l) * Q.V + v0;
@@ -476,8 +477,7 @@ __device__ __forceinline__ void epi_chunk(const SampleParams& P, const LmParams&
       const int vb = v0 + br * 16 + hf * 8;
       const int nv = FULL ? 8 : min(8, Q.V - vb);
       if (nv <= 0) continue;
-      uint32_t hb = 0u;
-      if (R.pen_on) hb = (__ldg(R.hrow + (vb >> 5)) >> (vb & 31)) & 0xffu;
+      const uint32_t hb = (hw >> (vb & 31)) & 0xffu;  // history bits of these tokens
       // approximate scores need no particular rounding (the margins cover
       // it): y = A c - Bc u as Am * mine + Bg * got
       float y[8];
@@ -647,6 +647,9 @@ __device__ __forceinline__ void lm_epilogue(const SampleParams& P, const LmParam
       const int nch = nct > rot ? (nct - rot + NG - 1) / NG : 0;
       for (int ch = 0; ch < nch; ++ch) {
         const int c = rot + ch * NG;
+        // the chunk's history word, fetched before the accumulator load so
+        // that the two latencies overlap
+        const uint32_t hw = R.pen_on ? __ldg(R.hrow + ((t * BN + c * 32) >> 5)) : 0u;
         float x[32];
         __syncwarp();
         tmem_ld32(lane_addr + (uint32_t)(a * BN + c * 32), x);
@@ -657,9 +660,9 @@ __device__ __forceinline__ void lm_epilogue(const SampleParams& P, const LmParam
         }
         const int v0 = t * BN + c * 32;
         if (v0 + 32 <= Q.V)
-          epi_chunk<true>(P, Q, sm, R, x, v0, part, pl, br, dump);
+          epi_chunk<true>(P, Q, sm, R, x, v0, hw, part, pl, br, dump);
         else
-          epi_chunk<false>(P, Q, sm, R, x, v0, part, pl, br, dump);
+          epi_chunk<false>(P, Q, sm, R, x, v0, hw, part, pl, br, dump);
       }
       if (nch == 0) {
         tc_fence_before();

@@ -467,11 +467,26 @@ __device__ __forceinline__ void epi_chunk(const SampleParams& P, const LmParams&
       R.m = cm;
     }
     const float ml = -__fmul_rn(R.m, kLog2e);
-    float a4[4] = {0.f, 0.f, 0.f, 0.f};
+    if (FULL) {  // packed pairs: one f32x2 FMA and one f32x2 add per two elements
+      const unsigned long long l2 = f2_pack(kLog2e, kLog2e), m2 = f2_pack(ml, ml);
+      unsigned long long acc[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (j < nval) a4[j & 3] = __fadd_rn(a4[j & 3], ex2_approx(__fmaf_rn(x[j], kLog2e, ml)));
-    R.S = __fadd_rn(R.S, __fadd_rn(__fadd_rn(a4[0], a4[1]), __fadd_rn(a4[2], a4[3])));
+      for (int j = 0; j < 32; j += 2) {
+        float e0, e1;
+        f2_unpack(f2_fma(f2_pack(x[j], x[j + 1]), l2, m2), e0, e1);
+        acc[(j >> 1) & 1] = f2_add(acc[(j >> 1) & 1], f2_pack(ex2_approx(e0), ex2_approx(e1)));
+      }
+      float s0, s1, s2, s3;
+      f2_unpack(acc[0], s0, s1);
+      f2_unpack(acc[1], s2, s3);
+      R.S = __fadd_rn(R.S, __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3)));
+    } else {
+      float a4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < nval) a4[j & 3] = __fadd_rn(a4[j & 3], ex2_approx(__fmaf_rn(x[j], kLog2e, ml)));
+      R.S = __fadd_rn(R.S, __fadd_rn(__fadd_rn(a4[0], a4[1]), __fadd_rn(a4[2], a4[3])));
+    }
     // approximate scores of this thread's 16 tokens, in two halves of 8
     // (shorter live ranges than one pass over 16)
     const bool philox = R.noisy && P.noise_kind != YAPD_NOISE_EXPLICIT;

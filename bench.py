@@ -78,6 +78,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=16)
+    ap.add_argument("--requests", type=int, default=None,
+                    help="requests per GPU instead of the configuration's (small cases for profiling)")
     ap.add_argument("--unfused", action="store_true",
                     help="configuration 4: time the cuBLAS head GEMM + select step as the main line")
     return ap.parse_args()
@@ -175,13 +177,13 @@ def cfg4_chain(inp):
 LOGIT_PAD = 8200  # config 4 logits row length: V = 8194 rounded up to 8 (16 bytes)
 
 
-def make_inputs(cfg: int, rank: int, device):
+def make_inputs(cfg: int, rank: int, device, requests=None):
     """The per-GPU shard: config defaults, Philox noise (production mode).
 
     Configuration 4 returns one logits buffer and a ``gemm`` dict holding the
     device operands of the head GEMM that fills it every step."""
     if cfg == 4:
-        inp = cfg4_chain(WL.make_config(4, seed=100 + rank, explicit_noise=False, lmhead_logits=False))
+        inp = cfg4_chain(WL.make_config(4, seed=100 + rank, B=requests, explicit_noise=False, lmhead_logits=False))
         g = torch.Generator(device=device).manual_seed(7 + 131 * rank)
         hid = [inp.meta["hidden"].to(device)]
         for _ in range(N_HIDDEN - 1):
@@ -196,7 +198,7 @@ def make_inputs(cfg: int, rank: int, device):
         gemm = {"hidden": hid, "weight": wp, "weight_v": w, "out": out}
         logits = out.view(inp.logits.shape[0], inp.logits.shape[1], LOGIT_PAD)[:, :, : inp.V]
         return inp, [logits], gemm
-    inp = WL.make_config(cfg, seed=100 + rank, explicit_noise=False,
+    inp = WL.make_config(cfg, seed=100 + rank, B=requests, explicit_noise=False,
                          masked="ragged" if cfg in (2, 3) else "all")
     g = torch.Generator(device=device).manual_seed(7 + 131 * rank)
     bufs = [inp.logits.to(device)]
@@ -530,7 +532,7 @@ def run_ours(args, ws, rank, local):
     dist = dist_init(ws, local)
     dev = torch.device("cuda", local)
     cfg = args.config
-    inp, bufs, gemm = make_inputs(cfg, rank, dev)
+    inp, bufs, gemm = make_inputs(cfg, rank, dev, args.requests)
     total = args.warmup + args.steps + Runner.G + args.e2e_steps + 8
     fused = cfg == 4 and not args.unfused
     R = Runner(inp, bufs, dev, total, gemm, fused=fused)

@@ -2193,6 +2193,62 @@ __device__ __forceinline__ float hdepth(const PosCtx& X, float K2mz, float c, fl
   return CFG ? __fmaf_rn(c, X.A2, __fmaf_rn(u, -X.B2, K2mz)) : __fmaf_rn(c, X.A2, K2mz);
 }
 
+// Exact scores of every kept token (depth d >= dH) of the staged rows, this
+// thread's vectors and scalar elements, into `kb`.  Tokens of one Philox
+// block share it, and a token whose noise cannot lift it to the thread's best
+// score so far skips the logarithms: the Gumbel noise obeys
+// G = -ln(-ln u) <= -ln(1 - u) (as -ln u >= 1 - u), so with s0 its exact score
+// before the noise, s0 + G < best - tiny whenever 1 - u > e^-(best - tiny - s0);
+// `tiny` covers the rounding of s0 + G, and such a token scores strictly below
+// a token already scored, whatever the tie rule.
+template <class C, bool CFG>
+__device__ __forceinline__ void kept_pass(const SampleParams& P, const PosCtx& X, const ScoreCtx& K,
+                                          const RowRef<C>& R, const Span& S, float K2mz, float dH, Pick& kb) {
+  const bool philox = K.noisy && P.noise_kind != YAPD_NOISE_EXPLICIT;
+  uint32_t blk = 0xffffffffu;
+  Philox4 r{0u, 0u, 0u, 0u};
+  auto one = [&](int v, float c, float u) {
+    if (!(hdepth<CFG>(X, K2mz, c, u) >= dH)) return;
+    const float vals = exact_val_cu(P, X, c, u);
+    const bool hb = K.pen_on ? hist_bit_k(P, K, v) : false;
+    const float s0 = (K.pen_on && hb) ? penalize(vals, K.rep, K.rrep) : vals;
+    float es = s0;
+    if (philox) {
+      if ((uint32_t)v >> 2 != blk) {
+        blk = (uint32_t)v >> 2;
+        r = philox4x32_10(blk, (uint32_t)K.pos, (uint32_t)P.offset, (uint32_t)(P.offset >> 32) & 0x7fffffffu,
+                          (uint32_t)P.seed, (uint32_t)(P.seed >> 32));
+      }
+      const uint32_t w = philox_word(r, (uint32_t)v & 3u);
+      const float uu = uniform_from_word(w);
+      if (kb.score > kNegInf && kb.score < __int_as_float(0x7f800000)) {
+        const float t = kb.score - (1e-6f * fabsf(kb.score) + 1e-6f) - s0;
+        if (t > 0.0f) {
+          const float q = ex2_approx(-t * kLog2e) * 1.0001f;  // e^-t, rounded up past ex2.approx's error
+          if (__fsub_rn(1.0f, uu) > q) return;
+        }
+      }
+      es = __fadd_rn(s0, gumbel_from_uniform(uu));
+    } else if (K.noisy) {
+      es = __fadd_rn(s0, noise_at(P, K.b, K.pos, K.l, v));
+    }
+    const Pick cand{es, vals, v};
+    if (es == es && es > kNegInf && pick_better(cand, kb, K.turbo)) kb = cand;
+  };
+  for (int j = S.j0 + gtid<C>(); j < S.j1; j += C::NT) {
+    const int v0 = j * C::W - S.head;
+#pragma unroll 1
+    for (int i = 0; i < C::W; ++i) {
+      const int v = v0 + i;
+      one(v, load_elem_smem<C>(R.sc, R.gc, v), CFG ? load_elem_smem<C>(R.su, R.gu, v) : 0.f);
+    }
+  }
+  for (int e = gtid<C>(); e < S.nscal; e += C::NT) {
+    const int v = scalar_v(S, e);
+    one(v, load_elem_smem<C>(R.sc, R.gc, v), CFG ? load_elem_smem<C>(R.su, R.gu, v) : 0.f);
+  }
+}
+
 // Histogram bin of a depth d <= 0: j = rint(-kHistPerUnit * d), so bin j
 // holds d in (-(j + 1/2) / kHistPerUnit, -(j - 1/2) / kHistPerUnit]; -1 past
 // the binned range (and for non-finite d).  Rounding by the 1.5 * 2^23 shift
@@ -2643,33 +2699,7 @@ __device__ __noinline__ bool select_hist(const SampleParams& P, const ItemParams
           const Pick cand{es, vals, v};
           if (es == es && es > kNegInf && pick_better(cand, kb, K.turbo)) kb = cand;
         }
-        if (nA > C::NT) {
-          // more kept tokens than the list holds: every thread scores its own
-          for (int j = S.j0 + tid; j < S.j1; j += C::NT) {
-            const int v0 = j * C::W - S.head;
-#pragma unroll 1
-            for (int i = 0; i < C::W; ++i) {
-              const int v = v0 + i;
-              const float c = load_elem_smem<C>(R.sc, R.gc, v);
-              const float u = CFG ? load_elem_smem<C>(R.su, R.gu, v) : 0.f;
-              if (!(hdepth<CFG>(X, K2mz, c, u) >= dH)) continue;
-              const float vals = exact_val_cu(P, X, c, u);
-              const float es = exact_score<C>(P, K, v, vals);
-              const Pick cand{es, vals, v};
-              if (es == es && es > kNegInf && pick_better(cand, kb, K.turbo)) kb = cand;
-            }
-          }
-          for (int e = tid; e < S.nscal; e += C::NT) {
-            const int v = scalar_v(S, e);
-            const float c = load_elem_smem<C>(R.sc, R.gc, v);
-            const float u = CFG ? load_elem_smem<C>(R.su, R.gu, v) : 0.f;
-            if (!(hdepth<CFG>(X, K2mz, c, u) >= dH)) continue;
-            const float vals = exact_val_cu(P, X, c, u);
-            const float es = exact_score<C>(P, K, v, vals);
-            const Pick cand{es, vals, v};
-            if (es == es && es > kNegInf && pick_better(cand, kb, K.turbo)) kb = cand;
-          }
-        }
+        if (nA > C::NT) kept_pass<C, CFG>(P, X, K, R, S, K2mz, dH, kb);  // more kept tokens than the list holds
         best_kept = block_pick<C>(kb, K.turbo, sm, slot);
       }
       if (tid < nP) hd.pid[tid] = cand_id(sm.cand[tid]);
@@ -2709,23 +2739,7 @@ __device__ __noinline__ bool select_hist(const SampleParams& P, const ItemParams
   if (nA <= C::NT) {
     for (int q = tid; q < nA; q += C::NT) score_tok(sm.klist[q]);
   } else {
-    // more kept tokens than the list holds: every thread scores its own
-    for (int j = S.j0 + tid; j < S.j1; j += C::NT) {
-      const int v0 = j * C::W - S.head;
-#pragma unroll 1
-      for (int i = 0; i < C::W; ++i) {
-        const int v = v0 + i;
-        const float c = load_elem_smem<C>(R.sc, R.gc, v);
-        const float u = CFG ? load_elem_smem<C>(R.su, R.gu, v) : 0.f;
-        if (hdepth<CFG>(X, K2mz, c, u) >= dH) score_tok(v);
-      }
-    }
-    for (int e = tid; e < S.nscal; e += C::NT) {
-      const int v = scalar_v(S, e);
-      const float c = load_elem_smem<C>(R.sc, R.gc, v);
-      const float u = CFG ? load_elem_smem<C>(R.su, R.gu, v) : 0.f;
-      if (hdepth<CFG>(X, K2mz, c, u) >= dH) score_tok(v);
-    }
+    kept_pass<C, CFG>(P, X, K, R, S, K2mz, dH, bp);  // more kept tokens than the list holds
   }
   // ---- exact resolution of the bands ----
   float Sk = X.S;

@@ -1041,6 +1041,7 @@ __device__ __noinline__ int argmax_smem(const SampleParams& P, const PosCtx X, c
   constexpr int NC = 4;
   float best = kNegInf;
   int cv[NC];
+  float cs[NC];  // their approximate scores: a list entry the best has left behind is dropped
   int nc = 0;
   bool ovf = false;
   for (int v4 = 4 * gtid<C>(); v4 < V; v4 += 4 * C::NT) {
@@ -1057,23 +1058,75 @@ __device__ __noinline__ int argmax_smem(const SampleParams& P, const PosCtx X, c
       keep |= in ? (1u << i) : 0u;
     }
     if (!keep) continue;
-    float g[4] = {0.f, 0.f, 0.f, 0.f};
-    if (K.noisy) noise4_kept(P, K, v4, keep, g);
     const unsigned hb = K.pen_on ? hist4(P, K.b, v4) : 0u;
+    float va[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      va[i] = __fmaf_rn(zz[i], kLn2, X.Kval);
+      if ((hb >> i) & 1u) va[i] = va[i] > 0.f ? __fmul_rn(va[i], K.rrep) : __fmul_rn(va[i], K.rep);
+    }
+    float g[4] = {0.f, 0.f, 0.f, 0.f};
+    if (K.noisy && P.noise_kind != YAPD_NOISE_EXPLICIT && best > kNegInf) {
+      // The Gumbel noise obeys G = -ln(-ln u) <= -ln(1 - u) (as -ln u >=
+      // 1 - u): a token whose bound va - ln(1 - u) stays below the thread's
+      // threshold (the best so far less its margin, less the rounding of
+      // va + G) cannot pass the test below, and skips the logarithms.
+      const Philox4 r = philox4x32_10((uint32_t)v4 >> 2, (uint32_t)K.pos, (uint32_t)P.offset,
+                                      (uint32_t)(P.offset >> 32) & 0x7fffffffu, (uint32_t)P.seed,
+                                      (uint32_t)(P.seed >> 32));
+      const float thr = best - score_margin(best);
+      const float tiny = 1e-6f * fabsf(thr) + 1e-6f;
+      unsigned todo = keep;
+      while (todo) {
+        const int i = __ffs(todo) - 1;
+        todo &= todo - 1u;
+        const uint32_t w = i == 0 ? r.x : i == 1 ? r.y : i == 2 ? r.z : r.w;
+        const float uu = uniform_from_word(w);
+        const float vi = i == 0 ? va[0] : i == 1 ? va[1] : i == 2 ? va[2] : va[3];
+        const float t = thr - vi - tiny;
+        if (t > 0.0f && __fsub_rn(1.0f, uu) > ex2_approx(-t * kLog2e) * 1.0001f) {
+          keep &= ~(1u << i);
+          continue;
+        }
+        const float gi = gumbel_from_uniform(uu);
+        g[0] = i == 0 ? gi : g[0];
+        g[1] = i == 1 ? gi : g[1];
+        g[2] = i == 2 ? gi : g[2];
+        g[3] = i == 3 ? gi : g[3];
+      }
+    } else if (K.noisy) {
+      noise4_kept(P, K, v4, keep, g);
+    }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int v = v4 + i;
       if (!((keep >> i) & 1u)) continue;
-      const float z = zz[i];
-      float va = __fmaf_rn(z, kLn2, X.Kval);
-      if ((hb >> i) & 1u) va = va > 0.f ? __fmul_rn(va, K.rrep) : __fmul_rn(va, K.rep);
-      const float sc = K.noisy ? __fadd_rn(va, g[i]) : va;
+      const float sc = K.noisy ? __fadd_rn(va[i], g[i]) : va[i];
       // (the bound x - margin(x) rises with x: a token within the final
       // margin was within the margin of the running best when it came)
       if (!(sc >= best - score_margin(best))) continue;
-      best = fmaxf(best, sc);
-      if (nc < NC) cv[nc++] = v;
-      else ovf = true;
+      if (sc > best) {
+        // a new best: drop the entries below its margin (they cannot be
+        // within the final margin either), keeping the list short
+        best = sc;
+        const float lo = best - score_margin(best);
+        int m = 0;
+#pragma unroll
+        for (int q = 0; q < NC; ++q)
+          if (q < nc && cs[q] >= lo) {
+            cv[m] = cv[q];
+            cs[m] = cs[q];
+            ++m;
+          }
+        nc = m;
+      }
+      if (nc < NC) {
+        cv[nc] = v;
+        cs[nc] = sc;
+        ++nc;
+      } else {
+        ovf = true;
+      }
     }
   }
   const float gbest = red_max1<C>(best, sm, slot);

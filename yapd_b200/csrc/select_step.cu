@@ -215,8 +215,8 @@ struct Hand {
   // histogram select handed to the tail: band P / band K / kept-token ids,
   // their counts, the counts and masses above and between the bands, and the
   // group's best kept token when the kept set is larger than aid
-  int hs_nP, hs_nK, hs_nA, hs_sep, hs_kept;
-  float hs_na, hs_ma, hs_mP, hs_nb, hs_mb;
+  int hs_nP, hs_nK, hs_nA, hs_sep, hs_kept;  // hs_sep: 0 no band K, 1 band K in kid, 2 S_k in hs_sk
+  float hs_na, hs_ma, hs_mP, hs_nb, hs_mb, hs_sk;
   int pid[32], kid[32], aid[64];
 };
 
@@ -2416,110 +2416,131 @@ __device__ __forceinline__ void hpass_sums(const PosCtx& X, const RowRef<C>& R, 
   s = s0 + s1;
 }
 
-// The scan (the group's first warp; lane l owns bins [l*PER, l*PER + PER),
-// bin 0 the top).  Finds the bin jk where the count from the top reaches k,
-// the bins jp1 <= jp2 where the mass from the top reaches the lower / upper
-// top-p target (top_p times the bounds of S_k that bin jk gives, or times
-// S_all), and lays out the bands: band P = bins [ja, jb] (the top-p
-// crossing, merged with jk when they touch; jk alone without top-p) and, when
-// jk lies further down, band K = bin jk with the bins between them summed.
+// The scan (the group's first warp).  The bins are taken 128 at a time, bin 0
+// (the top) first, lane l holding bins 128 q + 4 l + (0..3) of block q, with
+// warp prefix sums carried from block to block; each search stops at the
+// first block that holds its crossing (the crossings usually lie in the first
+// block).  Finds the bin jk where the count from the top reaches k, the bins
+// jp1 <= jp2 where the mass from the top reaches the lower / upper top-p
+// target (top_p times the bounds of S_k that bin jk gives, or times S_all),
+// and lays out the bands: band P = bins [ja, jb] (the top-p crossing, merged
+// with jk when they touch; jk alone without top-p) and, when jk lies further
+// down, band K = bin jk with the bins between them summed.
 // sm.hsi: [0] ok, [1] ja, [2] jb, [3] jk, [4] sep, [5] count between;
 // sm.hsf: [0] mass between.
 template <class C>
 __device__ __forceinline__ void hist_scan(Smem<C>& sm, bool topk_on, int k, bool topp_on, float top_p, float S_all) {
-  constexpr int PER = kHistBins / 32;
+  constexpr int NBLK = kHistBins / 128;
+  const unsigned full = 0xffffffffu;
   const int lane = threadIdx.x & 31;
-  int cnt[PER];
-  float ms[PER];
+  // block q: this lane's running bin masses from the top of its four (lm),
+  // and the block's mass before this lane (em) and through it (im)
+  auto blk_mass = [&](int q, float (&lm)[4], float& em, float& im) {
+    const int j0 = q * 128 + 4 * lane;
+    const uint4 m4 = *reinterpret_cast<const uint4*>(sm.hq + j0);
+    lm[0] = hist_mass(m4.x, j0);
+    lm[1] = lm[0] + hist_mass(m4.y, j0 + 1);
+    lm[2] = lm[1] + hist_mass(m4.z, j0 + 2);
+    lm[3] = lm[2] + hist_mass(m4.w, j0 + 3);
+    im = lm[3];
 #pragma unroll
-  for (int q = 0; q < PER / 4; ++q) {
-    const int4 c4 = reinterpret_cast<const int4*>(sm.hc + lane * PER)[q];
-    const uint4 m4 = reinterpret_cast<const uint4*>(sm.hq + lane * PER)[q];
-    cnt[4 * q] = c4.x;
-    cnt[4 * q + 1] = c4.y;
-    cnt[4 * q + 2] = c4.z;
-    cnt[4 * q + 3] = c4.w;
-    const int j0 = lane * PER + 4 * q;
-    ms[4 * q] = hist_mass(m4.x, j0);
-    ms[4 * q + 1] = hist_mass(m4.y, j0 + 1);
-    ms[4 * q + 2] = hist_mass(m4.z, j0 + 2);
-    ms[4 * q + 3] = hist_mass(m4.w, j0 + 3);
-  }
-  int segc = 0;
-  float segm = 0.f;
-#pragma unroll
-  for (int i = 0; i < PER; ++i) {
-    segc += cnt[i];
-    segm += ms[i];
-  }
-  int pc = segc;
-  float pm = segm;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int yc = __shfl_up_sync(0xffffffffu, pc, o);
-    const float ym = __shfl_up_sync(0xffffffffu, pm, o);
-    if (lane >= o) {
-      pc += yc;
-      pm += ym;
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(full, im, o);
+      if (lane >= o) im += y;
     }
-  }
-  const int basec = pc - segc;
-  const float basem = __fsub_rn(pm, segm);
+    em = __shfl_up_sync(full, im, 1);
+    if (lane == 0) em = 0.f;
+  };
   bool ok = true;
   int jk = -1;
   float slo = S_all, shi = S_all;
   if (topk_on) {
-    int c = basec, my = -1;
-    float m = basem, mex = 0.f, minc = 0.f;
+    int cbase = 0;
+    float mbase = 0.f;
+#pragma unroll 1
+    for (int q = 0; q < NBLK; ++q) {
+      const int j0 = q * 128 + 4 * lane;
+      const int4 c4 = *reinterpret_cast<const int4*>(sm.hc + j0);
+      const int lc[4] = {c4.x, c4.x + c4.y, c4.x + c4.y + c4.z, c4.x + c4.y + c4.z + c4.w};
+      int ic = lc[3];
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int c2 = c + cnt[i];
-      const float m2 = m + ms[i];
-      if (my < 0 && c2 >= k) {
-        my = lane * PER + i;
-        mex = m;
-        minc = m2;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(full, ic, o);
+        if (lane >= o) ic += y;
       }
-      c = c2;
-      m = m2;
+      const int ec = cbase + ic - lc[3];
+      float lm[4], em, im;
+      blk_mass(q, lm, em, im);
+      const unsigned bk = __ballot_sync(full, cbase + ic >= k);
+      if (bk) {
+        const int sl = __ffs(bk) - 1;
+        int i = 3;
+        if (ec + lc[2] >= k) i = 2;
+        if (ec + lc[1] >= k) i = 1;
+        if (ec + lc[0] >= k) i = 0;
+        const float before = __fadd_rn(mbase, em);
+        const float lmi = i == 0 ? lm[0] : i == 1 ? lm[1] : i == 2 ? lm[2] : lm[3];
+        const float lmp = i == 1 ? lm[0] : i == 2 ? lm[1] : lm[2];
+        const float lo = i == 0 ? before : __fadd_rn(before, lmp);
+        const float hi = __fadd_rn(before, lmi);
+        jk = q * 128 + 4 * sl + __shfl_sync(full, i, sl);
+        slo = __shfl_sync(full, lo, sl);
+        shi = __shfl_sync(full, hi, sl);
+        break;
+      }
+      cbase += __shfl_sync(full, ic, 31);
+      mbase += __shfl_sync(full, im, 31);
     }
-    const unsigned bk = __ballot_sync(0xffffffffu, my >= 0);
-    if (!bk) {
-      ok = false;  // the k-th token lies below the binned range
-    } else {
-      const int sl = __ffs(bk) - 1;
-      jk = __shfl_sync(0xffffffffu, my, sl);
-      slo = __shfl_sync(0xffffffffu, mex, sl);
-      shi = __shfl_sync(0xffffffffu, minc, sl);
-    }
+    if (jk < 0) ok = false;  // the k-th token lies below the binned range
   }
   int ja = jk, jb = jk;
   if (ok && topp_on) {
     // the fixed-point masses are exact to about 2^-16 per token: 1e-4 slack
     const float tlo = __fmul_rn(__fmul_rn(top_p, slo), 0.9999f);
     const float thi = __fmul_rn(__fmul_rn(top_p, shi), 1.0001f);
+    // with top-k the cut never lies below the k-th token: blocks past jk's
+    // could only clamp to jk (and tlo < slo is always reached before it)
+    const int qlast = topk_on ? (jk >> 7) : NBLK - 1;
     int a1 = -1, a2 = -1;
-    float m = basem;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const float m2 = m + ms[i];
-      if (a1 < 0 && m2 >= tlo) a1 = lane * PER + i;
-      if (a2 < 0 && m2 >= thi) a2 = lane * PER + i;
-      m = m2;
-    }
-    const unsigned b1 = __ballot_sync(0xffffffffu, a1 >= 0), b2 = __ballot_sync(0xffffffffu, a2 >= 0);
-    if (!b1) {
-      ok = false;
-    } else {
-      ja = __shfl_sync(0xffffffffu, a1, __ffs(b1) - 1);
-      jb = b2 ? __shfl_sync(0xffffffffu, a2, __ffs(b2) - 1) : -1;
-      if (topk_on) {
-        // the top-p cut never lies below the k-th token
-        if (jb < 0 || jb > jk) jb = jk;
-        if (ja > jk) ja = jk;
-      } else if (jb < 0) {
-        ok = false;
+    float mbase = 0.f;
+    // the first bin of block q whose running mass reaches t (lane sl is the
+    // first lane whose four bins reach it)
+    auto first_at = [&](int q, const float (&lm)[4], float before, float t, unsigned bal) {
+      const int sl = __ffs(bal) - 1;
+      int i = 3;
+      if (__fadd_rn(before, lm[2]) >= t) i = 2;
+      if (__fadd_rn(before, lm[1]) >= t) i = 1;
+      if (__fadd_rn(before, lm[0]) >= t) i = 0;
+      return q * 128 + 4 * sl + __shfl_sync(full, i, sl);
+    };
+#pragma unroll 1
+    for (int q = 0; q <= qlast; ++q) {
+      float lm[4], em, im;
+      blk_mass(q, lm, em, im);
+      const float before = __fadd_rn(mbase, em);
+      const float end = __fadd_rn(before, lm[3]);
+      if (a1 < 0) {
+        const unsigned b1 = __ballot_sync(full, end >= tlo);
+        if (b1) a1 = first_at(q, lm, before, tlo, b1);
       }
+      const unsigned b2 = __ballot_sync(full, end >= thi);
+      if (b2) {
+        a2 = first_at(q, lm, before, thi, b2);
+        break;
+      }
+      mbase += __shfl_sync(full, im, 31);
+    }
+    if (a1 < 0) {
+      if (topk_on) a1 = jk;
+      else ok = false;
+    }
+    ja = a1;
+    jb = a2;
+    if (topk_on) {
+      if (jb < 0 || jb > jk) jb = jk;
+      if (ja > jk) ja = jk;
+    } else if (jb < 0) {
+      ok = false;
     }
   }
   const bool sep = ok && topp_on && topk_on && jk > jb + 1;
@@ -2528,12 +2549,21 @@ __device__ __forceinline__ void hist_scan(Smem<C>& sm, bool topk_on, int k, bool
   int nbt = 0;
   float mbt = 0.f;
   if (sep) {
+#pragma unroll 1
+    for (int q = (jb + 1) >> 7; q <= ((jk - 1) >> 7); ++q) {
+      const int j0 = q * 128 + 4 * lane;
+      const int4 c4 = *reinterpret_cast<const int4*>(sm.hc + j0);
+      const uint4 m4 = *reinterpret_cast<const uint4*>(sm.hq + j0);
+      const int cc[4] = {c4.x, c4.y, c4.z, c4.w};
+      const uint32_t mq[4] = {m4.x, m4.y, m4.z, m4.w};
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int j = lane * PER + i;
-      const bool in = j > jb && j < jk;
-      nbt += in ? cnt[i] : 0;
-      mbt += in ? ms[i] : 0.f;
+      for (int i = 0; i < 4; ++i) {
+        const int j = j0 + i;
+        if (j > jb && j < jk) {
+          nbt += cc[i];
+          mbt += hist_mass(mq[i], j);
+        }
+      }
     }
     nbt = warp_sum_i(nbt);
     mbt = warp_sum(mbt);
@@ -2730,13 +2760,28 @@ __device__ __noinline__ bool select_hist(const SampleParams& P, const ItemParams
   // S_k already guarantee what the exact resolution checks: band P's first
   // member kept, every token below band P dropped, the k-th token in band K)
   {
-    bool hand = topp_on && nP <= 32 && nK <= 32 && (!topk_on || sep);
+    bool hand = topp_on && nP <= 32 && (!topk_on || sep);
     float s_lo = X.S, s_hi = X.S;
+    bool sk_exact = false;
     if (hand && sep) {
       const int kl = Q.top_k - (int)(n_above + (float)nP + n_between);
       s_lo = __fadd_rn(__fadd_rn(m_above, m_bandP), fmaxf(m_between, 0.f));
       s_hi = __fadd_rn(s_lo, m_bandK);
       hand = kl >= 1 && kl <= nK;
+      if (hand && nK > 32) {
+        // band K too large for the tail warp's lanes: S_k here, exactly as
+        // the resolution below computes it (rank by (exact value, id))
+        float part = 0.f;
+        for (int q = tid; q < nK; q += C::NT) {
+          const unsigned long long key = sm.cand[C::BAND - 1 - q];
+          int rank = 0;
+          for (int j2 = 0; j2 < nK; ++j2) rank += (sm.cand[C::BAND - 1 - j2] > key) ? 1 : 0;
+          if (rank < kl) part += sm.cande[C::BAND - 1 - q];
+        }
+        s_lo = __fadd_rn(s_lo, block_sum1<C>(part, sm, slot));
+        s_hi = s_lo;
+        sk_exact = true;
+      }
     }
     hand = hand && m_above < __fmul_rn(__fmul_rn(Q.top_p, s_lo), 0.99999f) &&
            __fadd_rn(m_above, m_bandP) >= __fmul_rn(__fmul_rn(Q.top_p, s_hi), 1.00001f);
@@ -2756,7 +2801,7 @@ __device__ __noinline__ bool select_hist(const SampleParams& P, const ItemParams
         best_kept = block_pick<C>(kb, K.turbo, sm, slot);
       }
       if (tid < nP) hd.pid[tid] = cand_id(sm.cand[tid]);
-      if (tid < nK) hd.kid[tid] = cand_id(sm.cand[C::BAND - 1 - tid]);
+      if (!sk_exact && tid < nK) hd.kid[tid] = cand_id(sm.cand[C::BAND - 1 - tid]);
       if (nA <= 64 && tid < nA) hd.aid[tid] = sm.klist[tid];
       if (tid == 0) {
         hd.m[0] = X.mc;
@@ -2768,7 +2813,8 @@ __device__ __noinline__ bool select_hist(const SampleParams& P, const ItemParams
         hd.hs_nP = nP;
         hd.hs_nK = nK;
         hd.hs_nA = nA;
-        hd.hs_sep = sep ? 1 : 0;
+        hd.hs_sep = sk_exact ? 2 : (sep ? 1 : 0);
+        hd.hs_sk = s_lo;
         hd.hs_kept = best_kept;
         hd.hs_na = n_above;
         hd.hs_ma = m_above;
@@ -3150,7 +3196,9 @@ __device__ __noinline__ void tail_hist(const SampleParams& P, KSmem<C>& ks, int 
     u = CFG ? load_elem_smem<C>(R.su, R.gu, v) : 0.f;
   };
   float Sk = X.S;
-  if (h.hs_sep) {
+  if (h.hs_sep == 2) {
+    Sk = h.hs_sk;  // the group computed S_k (band K wider than a warp)
+  } else if (h.hs_sep) {
     // S_k: everything above band K plus its first k - n_above members
     const int kl = Q.top_k - (int)(h.hs_na + (float)nP + h.hs_nb);
     unsigned long long key = 0ull;

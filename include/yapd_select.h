@@ -19,7 +19,9 @@
  * Conventions: every pointer is a device pointer unless stated; shapes are
  * row-major; the functions enqueue work on `stream` (a cudaStream_t, or NULL
  * for the legacy default stream) and never synchronise.  They allocate no
- * memory: scratch comes from the caller's workspace.  A negative return value
+ * memory: scratch comes from the caller's workspace, which must be zero-filled
+ * before its first use (a select step keeps its scheduling counters in the
+ * workspace header and leaves them at zero when it ends).  A negative return value
  * is a host-side validation error (nothing was launched); YAPD_OK means the
  * kernels were enqueued.  Device-side conditions (a bounded wait that expired)
  * are recorded in the workspace status word, read by yapd_read_status; a

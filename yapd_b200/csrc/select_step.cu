@@ -183,6 +183,11 @@ struct SampleParams {
   int32_t* work_w;          // work list (each CTA writes its own entries)
   unsigned long long* pos_count;  // optional: += positions sampled this step
   int64_t wait_ns;          // limit of each pipeline wait (drains: kWaitLimitNs)
+  // select step: the launch's scheduling counters in the workspace header
+  // ([0] CTAs past the preamble, [1] work-list entries appended, [2] entries
+  // claimed, [3] CTAs finished); zero between calls (the last CTA to finish
+  // clears them)
+  uint32_t* sched;
   UnmaskParams U;
 };
 
@@ -613,6 +618,59 @@ __device__ int cta_prepare(const SampleParams& P, int* scan, ReqTable* rt = null
   }
   __syncthreads();
   return tot;
+}
+
+// Select step, preamble of the grouped kernel's claimed schedule: CTA c
+// scans only its share of the positions, [c * span, (c + 1) * span), marks
+// the sampled ones -2 (until they are sampled) and initialises the outputs of
+// the others (sampled -1, pmi NaN), keeps its first `cap` sampled positions
+// for itself (own[], in position order) and appends the rest to the launch's
+// work list (one reservation on sched[1] per round of blockDim positions).
+// Returns the number of own positions.
+__device__ int cta_prepare_share(const SampleParams& P, int* own, int cap, int* scan) {
+  const UnmaskParams& U = P.U;
+  const int total = U.B * U.L;
+  const int grid = (int)gridDim.x;
+  const int span = (total + grid - 1) / grid;
+  const int p0 = min((int)blockIdx.x * span, total), p1 = min(p0 + span, total);
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
+  int done = 0;
+  for (int r0 = p0; r0 < p1; r0 += blockDim.x) {
+    const int p = r0 + (int)threadIdx.x;
+    bool smp = false;
+    if (p < p1) {
+      const int b = divu(p, P.div_L);
+      smp = P.dense || (U.is_commit[b] == 0 && xt_at(U, b, p - b * U.L) == U.mask_id);
+      if (smp) {
+        P.sampled[p] = -2;
+      } else {
+        P.sampled[p] = -1;
+        U.pmi[p] = __int_as_float(0x7fc00000);
+      }
+    }
+    const unsigned bal = __ballot_sync(0xffffffffu, smp);
+    if (lane == 0) scan[w] = __popc(bal);
+    __syncthreads();
+    int before = 0, cnt = 0;
+    for (int q = 0; q < nwarp; ++q) {
+      const int c = scan[q];
+      before += q < w ? c : 0;
+      cnt += c;
+    }
+    const int rank = done + before + __popc(bal & ((1u << lane) - 1u));  // among the CTA's sampled positions
+    const int first_app = max(done, cap);                                // first rank appended this round
+    const int n_app = max(0, done + cnt - first_app);
+    if (threadIdx.x == 0 && n_app > 0) scan[nwarp] = (int)atomicAdd(P.sched + 1, (unsigned)n_app);
+    __syncthreads();
+    if (smp) {
+      if (rank < cap) own[rank] = p;
+      else P.work_w[scan[nwarp] + (rank - first_app)] = p;
+    }
+    done += cnt;
+    __syncthreads();
+  }
+  if (P.pos_count && threadIdx.x == 0 && done > 0) atomicAdd(P.pos_count, (unsigned long long)done);
+  return min(done, cap);
 }
 
 // ------------------------------------------------------------ sample kernel
@@ -1673,6 +1731,8 @@ struct KSmem {
   Hand hand[C::NSTAGE];       // the group -> tail warp record of the stage's position
   int issued[C::NSTAGE];      // copies armed on full[s] ...
   int landed[C::NSTAGE];      // ... and waited for (read only after the final barrier)
+  int nodyn;                  // claimed schedule: this CTA stopped claiming (other CTAs' entries were late)
+  int own[C::NSTAGE];         // claimed schedule: this CTA's own first positions
   int scan[32];               // per-warp counts of the fused preamble
   Smem<C> g[C::NG];
   alignas(128) unsigned char stage[C::NSTAGE][C::STAGE_BYTES];
@@ -3318,17 +3378,92 @@ __device__ __noinline__ void tail_hist(const SampleParams& P, KSmem<C>& ks, int 
   __syncwarp();
 }
 
-// The grouped pipeline over this CTA's items 0..n_my-1 (global item index
-// first + k * stride): NG groups of NT threads, each working one position at
-// a time from a shared NSTAGE-deep ring of staged rows, and one tail warp per
-// group.  Local item `it` uses stage it % NSTAGE and group it % NG (NG
-// divides NSTAGE, so each stage serves one group).  The group runs the
-// statistics and either finishes the position or hands its band to the
-// group's tail warp; the tail warp finishes a handed band, then issues the
-// copies of item it + NSTAGE into the stage.  Threads past C::NTHREADS only
-// take part in the CTA barriers.
+// Acquire load of a counter other CTAs update.
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Every CTA of the launch has appended its work-list entries (a bounded
+// wait; false if it ran out, and then this CTA claims nothing: the last CTA
+// to pass its preamble never waits, so every entry is still claimed).
+__device__ __forceinline__ bool preambles_done(const SampleParams& P) {
+  if (ld_acquire_u32(P.sched) >= gridDim.x) return true;
+  if (P.wait_ns < 0) return false;
+  const uint64_t t0 = globaltimer_ns();
+  while (ld_acquire_u32(P.sched) < gridDim.x) {
+    if (globaltimer_ns() - t0 > (uint64_t)P.wait_ns) return false;
+    __nanosleep(200);
+  }
+  return true;
+}
+
+// The parameters of this CTA's local item `it` (one thread).  Static
+// schedule: item it is the global entry first + it * stride.  Claimed
+// schedule (`dyn`, the select step): items it < n_stat are the CTA's own
+// positions (own[]), later ones are claimed from the launch's work list, the
+// c-th claim taking entry c, once every CTA has appended its entries.  False:
+// no item (every entry claimed, or the other CTAs' entries were not ready in
+// time; the CTA then claims nothing more, so that a group's items end at its
+// first empty one and no claimed entry is left behind it).
+template <class C>
+__device__ __forceinline__ bool next_item(const SampleParams& P, KSmem<C>& ks, int it, int n_stat, int first,
+                                          int stride, bool dyn, ItemParams& Q) {
+  if (!dyn) {
+    Q = load_params(P, item_pos<C>(P, first + it * stride));
+    return true;
+  }
+  if (it < n_stat) {
+    Q = load_params(P, ks.own[it]);
+    return true;
+  }
+  if (*(volatile int*)&ks.nodyn) return false;
+  if (!preambles_done(P)) {
+    *(volatile int*)&ks.nodyn = 1;
+    return false;
+  }
+  const int n_list = (int)ld_acquire_u32(P.sched + 1);  // final: every CTA has appended
+  const int idx = (int)atomicAdd(P.sched + 2, 1u);
+  if (idx >= n_list) return false;
+  // another CTA wrote this entry: read it from L2, not from a stale L1 line
+  Q = load_params(P, __ldcg(P.work_w + idx));
+  return true;
+}
+
+// Issue local item Q into `stage`, or (no item) complete the stage's phase
+// empty, with Q.pos = -1 for its group.
+template <class C>
+__device__ __forceinline__ void issue_or_close(const SampleParams& P, KSmem<C>& ks, int stage, bool has,
+                                               const ItemParams& Q) {
+  if (has) {
+    issue_item<C>(P, ks, stage, Q);
+  } else {
+    ks.hand[stage].Q.pos = -1;
+    mbar_arrive_expect_tx(&ks.full[stage], 0u);
+  }
+  atomicAdd(&ks.issued[stage], 1);
+}
+
+// The grouped pipeline over this CTA's items: NG groups of NT threads, each
+// working one position at a time from a shared NSTAGE-deep ring of staged
+// rows, and one tail warp per group.  Local item `it` uses stage it % NSTAGE
+// and group it % NG (NG divides NSTAGE, so each stage serves one group).  The
+// group runs the statistics and either finishes the position or hands its
+// band to the group's tail warp; the tail warp finishes a handed band, then
+// refills a stage its group has released.  Static schedule: n_stat items,
+// global entries first + k * stride, the stage of item it refilled with item
+// it + NSTAGE.  Claimed schedule (`dyn`): the CTA's own n_stat items, then
+// claimed ones; a group stops at its first empty item (claims are made in
+// the order of the local items, so every later one is empty too), and when a
+// group has two or more stages the refill lags one item (the stage of item
+// it - NG takes item it - NG + NSTAGE), so that when the claims run out every
+// group holds at most one position besides the one it is working.  Threads
+// past C::NTHREADS only take part in the CTA barriers.
 template <class C, bool CFG>
-__device__ __forceinline__ void group_phase(const SampleParams& P, KSmem<C>& ks, int n_my, int first, int stride) {
+__device__ __forceinline__ void group_phase(const SampleParams& P, KSmem<C>& ks, int n_stat, int first, int stride,
+                                            bool dyn = false) {
+  constexpr int LAG = C::NSTAGE >= 2 * C::NG ? C::NG : 0;
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::NSTAGE; ++s) {
       mbar_init(&ks.full[s], 1);
@@ -3336,15 +3471,19 @@ __device__ __forceinline__ void group_phase(const SampleParams& P, KSmem<C>& ks,
       ks.issued[s] = 0;
       ks.landed[s] = 0;
     }
+    ks.nodyn = 0;
     fence_mbar_init();
   }
   __syncthreads();
+  const int n_my = dyn ? 0x7fffffff : n_stat;  // static: the loop bound
   if (threadIdx.x == 0) {
     // the stages may have been read through the generic proxy before
     fence_proxy_async_smem();
+    bool more = true;
     for (int s = 0; s < C::NSTAGE && s < n_my; ++s) {
-      issue_item<C>(P, ks, s, load_params(P, item_pos<C>(P, first + s * stride)));
-      atomicAdd(&ks.issued[s], 1);
+      ItemParams Q{};
+      more = more && next_item<C>(P, ks, s, n_stat, first, stride, dyn, Q);
+      issue_or_close<C>(P, ks, s, more, Q);
     }
   }
   if (threadIdx.x < C::NG * C::NT) {
@@ -3361,29 +3500,37 @@ __device__ __forceinline__ void group_phase(const SampleParams& P, KSmem<C>& ks,
       if (csync_or<C>(!ok)) break;
       if (tid == 0) atomicAdd(&ks.landed[stage], 1);
       const ItemParams Q = ks.hand[stage].Q;
-      compute_item<C, CFG>(P, ks, sm, slot, stage, Q);
+      const bool empty = Q.pos < 0;
+      if (!empty) compute_item<C, CFG>(P, ks, sm, slot, stage, Q);
       __syncwarp();
       if ((threadIdx.x & 31) == 0) mbar_arrive(&ks.ready[stage]);
+      if (empty) break;
     }
   } else if (threadIdx.x < C::NTHREADS) {
     // ---- tail warp of group g ----
     const int g = (threadIdx.x - C::NG * C::NT) >> 5;
+    const int lane = threadIdx.x & 31;
     for (int it = g; it < n_my; it += C::NG) {
       const int stage = it % C::NSTAGE;
       const uint32_t parity = (uint32_t)(it / C::NSTAGE) & 1u;
-      const int ref_it = it + C::NSTAGE;
+      const int ref_it = dyn ? it - LAG + C::NSTAGE : it + C::NSTAGE;
       ItemParams refill{};
-      if (ref_it < n_my) refill = load_params(P, item_pos<C>(P, first + ref_it * stride));
+      bool has = false;
+      if (!dyn && ref_it < n_my) {
+        refill = load_params(P, item_pos<C>(P, first + ref_it * stride));
+        has = true;
+      }
       if (!mbar_wait_bounded(&ks.ready[stage], parity, P.wait_ns)) {
-        if ((threadIdx.x & 31) == 0) atomicOr(P.status, (unsigned)YAPD_STATUS_WAIT_TIMEOUT);
+        if (lane == 0) atomicOr(P.status, (unsigned)YAPD_STATUS_WAIT_TIMEOUT);
         break;
       }
+      if (ks.hand[stage].Q.pos < 0) break;  // the group's items ended here
       if (ks.hand[stage].handed == 1) tail_finish<C, CFG>(P, ks, stage);
       else if (ks.hand[stage].handed == 2) tail_hist<C, CFG>(P, ks, stage);
-      if ((threadIdx.x & 31) == 0 && ref_it < n_my) {
+      if (lane == 0 && (dyn ? it >= LAG : ref_it < n_my)) {
+        if (dyn) has = next_item<C>(P, ks, ref_it, n_stat, first, stride, true, refill);
         fence_proxy_async_smem();
-        issue_item<C>(P, ks, stage, refill);
-        atomicAdd(&ks.issued[stage], 1);
+        issue_or_close<C>(P, ks, ref_it % C::NSTAGE, has, refill);
       }
       __syncwarp();
     }
@@ -3404,11 +3551,33 @@ template <class C, bool CFG>
 __global__ void __launch_bounds__(C::NTHREADS, 1) sample_kernel(const __grid_constant__ SampleParams P) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   KSmem<C>& ks = *reinterpret_cast<KSmem<C>*>(smem_raw);
-  const int n_items = P.fused ? cta_prepare(P, ks.scan) : P.n_identity;
   const int first = blockIdx.x, stride = gridDim.x;
-  if (first >= n_items) return;
-  const int n_my = (n_items - first + stride - 1) / stride;
-  group_phase<C, CFG>(P, ks, n_my, first, stride);
+  if (!P.fused) {
+    const int n_items = P.n_identity;
+    if (first >= n_items) return;
+    group_phase<C, CFG>(P, ks, (n_items - first + stride - 1) / stride, first, stride);
+    return;
+  }
+  // select step: each CTA scans its share of the positions, works its first
+  // NSTAGE sampled ones itself and appends the rest to the launch's work
+  // list; then every CTA claims list entries until none are left, so that
+  // CTAs whose positions were cheap take more of them
+  const int n_own = cta_prepare_share(P, ks.own, C::NSTAGE, ks.scan);
+  __threadfence();  // this CTA's work-list entries before its count below
+  __syncthreads();
+  if (threadIdx.x == 0) atomicAdd(P.sched, 1u);
+  group_phase<C, CFG>(P, ks, n_own, first, stride, true);
+  // the last CTA to finish clears the counters for the next call
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(P.sched + 3, 1u) == gridDim.x - 1) {
+      atomicExch(P.sched, 0u);
+      atomicExch(P.sched + 1, 0u);
+      atomicExch(P.sched + 2, 0u);
+      atomicExch(P.sched + 3, 0u);
+    }
+  }
 }
 
 // ------------------------------------------------------- warp-per-position path
@@ -4843,6 +5012,7 @@ int yapd_select_step(const yapd_select_args* a, void* stream) {
   P.status = reinterpret_cast<uint32_t*>(ws);
   P.work_w = reinterpret_cast<int32_t*>(ws + 256);
   P.pcu = reinterpret_cast<float2*>(ws + 256 + align256(n_pos * sizeof(int32_t)));
+  P.sched = reinterpret_cast<uint32_t*>(ws + 64);
 
   P.n_identity = 0;
   P.cfg_w = a->cfg_scale;

@@ -265,6 +265,7 @@ struct Smem;
 template <class C>
 struct KSmem;
 constexpr int kHistBins = 512;  // bins of the histogram bracket
+constexpr int kKqPerWarp = 96;  // kept_pass queue: 32 lanes x at most 3 Philox blocks per vector
 
 template <class C>
 __device__ __forceinline__ float load_elem_global(const char* row, int v) {
@@ -1722,6 +1723,7 @@ struct Smem {
   int hsi[8];                 // histogram select: the scan's crossings ...
   float hsf[8];               // ... and its mass bounds
   int klist[C::NT];           // histogram select: ids of the tokens above band P (kept)
+  uint32_t kq[C::NW * kKqPerWarp];  // kept_pass: each warp's queue of (Philox block, keep mask) units
 };
 
 template <class C>
@@ -2306,59 +2308,114 @@ __device__ __forceinline__ float hdepth(const PosCtx& X, float K2mz, float c, fl
   return CFG ? __fmaf_rn(c, X.A2, __fmaf_rn(u, -X.B2, K2mz)) : __fmaf_rn(c, X.A2, K2mz);
 }
 
-// Exact scores of every kept token (depth d >= dH) of the staged rows, this
-// thread's vectors and scalar elements, into `kb`.  Tokens of one Philox
-// block share it, and a token whose noise cannot lift it to the thread's best
-// score so far skips the logarithms: the Gumbel noise obeys
-// G = -ln(-ln u) <= -ln(1 - u) (as -ln u >= 1 - u), so with s0 its exact score
-// before the noise, s0 + G < best - tiny whenever 1 - u > e^-(best - tiny - s0);
-// `tiny` covers the rounding of s0 + G, and such a token scores strictly below
-// a token already scored, whatever the tie rule.
+// Exact scores of every kept token (depth d >= dH) of the staged rows into
+// `kb`.  Each warp takes its lanes' vectors together: the lanes' kept tokens,
+// grouped by Philox block, go to the warp's queue in shared memory (sm.kq),
+// and the lanes then score the queued blocks round-robin, so that a warp
+// spends one scoring slot per 32 kept blocks instead of one per token of a
+// vector that any lane keeps.  Tokens of one block share its Philox word
+// set, and a token whose noise cannot lift it to the best score known (the
+// warp's best so far, or `thr`, the score of a token the group has already
+// scored) skips the logarithms: the Gumbel noise obeys G = -ln(-ln u) <=
+// -ln(1 - u) (as -ln u >= 1 - u), so with s0 its exact score before the
+// noise, s0 + G < best - tiny whenever 1 - u > e^-(best - tiny - s0); `tiny`
+// covers the rounding of s0 + G, and such a token scores strictly below a
+// token already scored, whatever the tie rule.
 template <class C, bool CFG>
 __device__ __forceinline__ void kept_pass(const SampleParams& P, const PosCtx& X, const ScoreCtx& K,
-                                          const RowRef<C>& R, const Span& S, float K2mz, float dH, Pick& kb) {
+                                          const RowRef<C>& R, const Span& S, float K2mz, float dH, Pick& kb,
+                                          Smem<C>& sm, float thr) {
   const bool philox = K.noisy && P.noise_kind != YAPD_NOISE_EXPLICIT;
-  uint32_t blk = 0xffffffffu;
-  Philox4 r{0u, 0u, 0u, 0u};
-  auto one = [&](int v, float c, float u) {
-    if (!(hdepth<CFG>(X, K2mz, c, u) >= dH)) return;
-    const float vals = exact_val_cu(P, X, c, u);
-    const bool hb = K.pen_on ? hist_bit_k(P, K, v) : false;
-    const float s0 = (K.pen_on && hb) ? penalize(vals, K.rep, K.rrep) : vals;
-    float es = s0;
-    if (philox) {
-      if ((uint32_t)v >> 2 != blk) {
-        blk = (uint32_t)v >> 2;
-        r = philox4x32_10(blk, (uint32_t)K.pos, (uint32_t)P.offset, (uint32_t)(P.offset >> 32) & 0x7fffffffu,
-                          (uint32_t)P.seed, (uint32_t)(P.seed >> 32));
+  const int lane = threadIdx.x & 31;
+  uint32_t* q = sm.kq + (gtid<C>() >> 5) * kKqPerWarp;
+  float best = kb.score > thr ? kb.score : thr;
+  // the kept tokens v4 + i (bit i of keep) of one Philox block
+  auto unit = [&](int v4, unsigned keep) {
+    Philox4 r{0u, 0u, 0u, 0u};
+    if (philox)
+      r = philox4x32_10((uint32_t)v4 >> 2, (uint32_t)K.pos, (uint32_t)P.offset,
+                        (uint32_t)(P.offset >> 32) & 0x7fffffffu, (uint32_t)P.seed, (uint32_t)(P.seed >> 32));
+    while (keep) {
+      const int i = __ffs(keep) - 1;
+      keep &= keep - 1u;
+      const int v = v4 + i;
+      const float c = load_elem_smem<C>(R.sc, R.gc, v);
+      const float u = CFG ? load_elem_smem<C>(R.su, R.gu, v) : 0.f;
+      const float vals = exact_val_cu(P, X, c, u);
+      const bool hb = K.pen_on ? hist_bit_k(P, K, v) : false;
+      const float s0 = (K.pen_on && hb) ? penalize(vals, K.rep, K.rrep) : vals;
+      float es = s0;
+      if (philox) {
+        const float uu = uniform_from_word(philox_word(r, (uint32_t)i));
+        if (best > kNegInf && best < __int_as_float(0x7f800000)) {
+          const float t = best - (1e-6f * fabsf(best) + 1e-6f) - s0;
+          if (t > 0.0f) {
+            const float qb = ex2_approx(-t * kLog2e) * 1.0001f;  // e^-t, rounded up past ex2.approx's error
+            if (__fsub_rn(1.0f, uu) > qb) continue;
+          }
+        }
+        es = __fadd_rn(s0, gumbel_from_uniform(uu));
+      } else if (K.noisy) {
+        es = __fadd_rn(s0, noise_at(P, K.b, K.pos, K.l, v));
       }
-      const uint32_t w = philox_word(r, (uint32_t)v & 3u);
-      const float uu = uniform_from_word(w);
-      if (kb.score > kNegInf && kb.score < __int_as_float(0x7f800000)) {
-        const float t = kb.score - (1e-6f * fabsf(kb.score) + 1e-6f) - s0;
-        if (t > 0.0f) {
-          const float q = ex2_approx(-t * kLog2e) * 1.0001f;  // e^-t, rounded up past ex2.approx's error
-          if (__fsub_rn(1.0f, uu) > q) return;
+      const Pick cand{es, vals, v};
+      if (es == es && es > kNegInf && pick_better(cand, kb, K.turbo)) {
+        kb = cand;
+        best = fmaxf(best, es);
+      }
+    }
+  };
+  const int nk = (S.j1 - S.j0 + C::NT - 1) / C::NT;
+  for (int k = 0; k < nk; ++k) {
+    const int j = S.j0 + gtid<C>() + k * C::NT;
+    // this lane's kept tokens of vector j, as (block, mask) units
+    uint32_t un[3] = {0u, 0u, 0u};
+    int nu = 0;
+    if (j < S.j1) {
+      const uint4 a = lds128(R.sc + j * 16);
+      const uint4 bq = CFG ? lds128(R.su + j * 16) : a;
+      const int v0 = j * C::W - S.head;
+      unsigned m = 0u;
+#pragma unroll
+      for (int i = 0; i < C::W; ++i)
+        m |= (hdepth<CFG>(X, K2mz, velem<C>(a, i), CFG ? velem<C>(bq, i) : 0.f) >= dH ? 1u : 0u) << i;
+#pragma unroll
+      for (int t = 0; t < 3; ++t) {
+        if (m) {
+          const int i = __ffs(m) - 1;
+          const int v4 = (v0 + i) & ~3;
+          const int i0 = v4 - v0;  // -3..W-1: bit of token v4 in m
+          const unsigned blk = i0 >= 0 ? (m >> i0) & 15u : (m << (-i0)) & 15u;
+          m &= i0 >= 0 ? ~(15u << i0) : ~(15u >> (-i0));
+          un[t] = ((uint32_t)v4 << 4) | blk;
+          ++nu;
         }
       }
-      es = __fadd_rn(s0, gumbel_from_uniform(uu));
-    } else if (K.noisy) {
-      es = __fadd_rn(s0, noise_at(P, K.b, K.pos, K.l, v));
     }
-    const Pick cand{es, vals, v};
-    if (es == es && es > kNegInf && pick_better(cand, kb, K.turbo)) kb = cand;
-  };
-  for (int j = S.j0 + gtid<C>(); j < S.j1; j += C::NT) {
-    const int v0 = j * C::W - S.head;
-#pragma unroll 1
-    for (int i = 0; i < C::W; ++i) {
-      const int v = v0 + i;
-      one(v, load_elem_smem<C>(R.sc, R.gc, v), CFG ? load_elem_smem<C>(R.su, R.gu, v) : 0.f);
+    int incl = nu;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
     }
+    const int total = __shfl_sync(0xffffffffu, incl, 31);
+    if (total == 0) continue;
+#pragma unroll
+    for (int t = 0; t < 3; ++t)
+      if (t < nu) q[incl - nu + t] = un[t];
+    __syncwarp();
+    for (int t = lane; t < total; t += 32) {
+      const uint32_t e = q[t];
+      unit((int)(e >> 4), e & 15u);
+    }
+    best = warp_max(best);
+    __syncwarp();
   }
   for (int e = gtid<C>(); e < S.nscal; e += C::NT) {
     const int v = scalar_v(S, e);
-    one(v, load_elem_smem<C>(R.sc, R.gc, v), CFG ? load_elem_smem<C>(R.su, R.gu, v) : 0.f);
+    const float c = load_elem_smem<C>(R.sc, R.gc, v);
+    const float u = CFG ? load_elem_smem<C>(R.su, R.gu, v) : 0.f;
+    if (hdepth<CFG>(X, K2mz, c, u) >= dH) unit(v & ~3, 1u << (v & 3));
   }
 }
 
@@ -2857,7 +2914,12 @@ __device__ __noinline__ bool select_hist(const SampleParams& P, const ItemParams
           const Pick cand{es, vals, v};
           if (es == es && es > kNegInf && pick_better(cand, kb, K.turbo)) kb = cand;
         }
-        if (nA > C::NT) kept_pass<C, CFG>(P, X, K, R, S, K2mz, dH, kb);  // more kept tokens than the list holds
+        if (nA > C::NT) {
+          // more kept tokens than the list holds: all of them, against the
+          // best score of the listed ones
+          const float thr = red_max1<C>(kb.score, sm, slot);
+          kept_pass<C, CFG>(P, X, K, R, S, K2mz, dH, kb, sm, thr);
+        }
         best_kept = block_pick<C>(kb, K.turbo, sm, slot);
       }
       if (tid < nP) hd.pid[tid] = cand_id(sm.cand[tid]);
@@ -2895,10 +2957,12 @@ __device__ __noinline__ bool select_hist(const SampleParams& P, const ItemParams
     const Pick cand{es, vals, v};
     if (es == es && es > kNegInf && pick_better(cand, bp, K.turbo)) bp = cand;
   };
-  if (nA <= C::NT) {
-    for (int q = tid; q < nA; q += C::NT) score_tok(sm.klist[q]);
-  } else {
-    kept_pass<C, CFG>(P, X, K, R, S, K2mz, dH, bp);  // more kept tokens than the list holds
+  for (int q = tid; q < nA && q < C::NT; q += C::NT) score_tok(sm.klist[q]);
+  if (nA > C::NT) {
+    // more kept tokens than the list holds: all of them, against the best
+    // score of the listed ones
+    const float thr = red_max1<C>(bp.score, sm, slot);
+    kept_pass<C, CFG>(P, X, K, R, S, K2mz, dH, bp, sm, thr);
   }
   // ---- exact resolution of the bands ----
   float Sk = X.S;

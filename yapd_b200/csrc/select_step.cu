@@ -2233,7 +2233,7 @@ __device__ __forceinline__ void hpass_max(const PosCtx& X, const RowRef<C>& R, c
   if constexpr (C::BF16) {
     uint32_t c2 = 0xff80ff80u, u2 = 0xff80ff80u;
     const unsigned long long A2p = f2_pack(A2, A2), nB2p = f2_pack(nB2, nB2), zp = f2_pack(0.f, 0.f);
-#pragma unroll 2
+#pragma unroll 1
     for (int j = S.j0 + tid; j < S.j1; j += C::NT) {
       const uint4 a = lds128(R.sc + j * 16);
       c2 = bmax2(c2, bmax2(bmax2(a.x, a.y), bmax2(a.z, a.w)));

@@ -94,9 +94,32 @@ def dist_env():
     return ws, rank, local
 
 
+_STDOUT_FD = None
+
+
+def quiet_stdout():
+    """Under torchrun, whatever libraries write to the process's stdout (NCCL's
+    version banner) goes to stderr, so that stdout carries only the JSON line."""
+    global _STDOUT_FD
+    if _STDOUT_FD is None:
+        sys.stdout.flush()
+        _STDOUT_FD = os.dup(1)
+        os.dup2(2, 1)
+
+
+def emit(line: dict):
+    """Print the bench's JSON line on the real stdout."""
+    sys.stdout.flush()
+    if _STDOUT_FD is not None:
+        os.write(_STDOUT_FD, (json.dumps(line) + "\n").encode())
+    else:
+        print(json.dumps(line), flush=True)
+
+
 def dist_init(ws, local):
     if ws > 1:
         import torch.distributed as dist
+        quiet_stdout()
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
@@ -520,7 +543,7 @@ def run_reference(args, ws, rank):
                        "parallelism": "host cores"},
             "cpu_baseline": cb,
             "e2e": {"value": v, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def count_now(R) -> int:
@@ -705,7 +728,7 @@ def run_ours(args, ws, rank, local):
                 "l2": f"{N_HIDDEN} rotating hidden-state buffers ({N_HIDDEN * h.numel() * 2 / 1e6:.0f} MB) "
                       f"and a {inp.logits.numel() * 2 / 1e6:.0f} MB logits buffer > L2"})
             line["gpu_launches"] = (LAUNCHES_PER_STEP + 1) * args.steps
-        print(json.dumps(line), flush=True)
+        emit(line)
     if dist:
         del R
         dist.destroy_process_group()
@@ -905,7 +928,7 @@ def run_turbo(args, ws, rank, local):
                     "h2d_bytes_per_step": bufs[0].numel() * 4, "d2h_bytes_per_step": TURBO_ROWS * 4},
             "gpu_launches": steps, "clocks": ck, "cpu_baseline": cpu,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     if dist:
         del g
         dist.destroy_process_group()

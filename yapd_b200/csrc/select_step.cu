@@ -494,6 +494,10 @@ __device__ __forceinline__ void unmask_request(const UnmaskParams& U, int dense,
 
 // One warp per request: the block-state update after the sample kernel.
 __global__ void unmask_kernel(const __grid_constant__ UnmaskParams U, int dense) {
+  // launched as a programmatic dependent of the sampling kernel: its CTAs
+  // may be resident before that kernel ends, and wait here until it has
+  // finished and its writes are visible (no effect on an ordinary launch)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (b < U.B) unmask_request(U, dense, b);
 }
@@ -3631,6 +3635,8 @@ __global__ void __launch_bounds__(C::NTHREADS, 1) sample_kernel(const __grid_con
   __syncthreads();
   if (threadIdx.x == 0) atomicAdd(P.sched, 1u);
   group_phase<C, CFG>(P, ks, n_own, first, stride, true);
+  // this CTA's work is done: the state update may be scheduled
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   // the last CTA to finish clears the counters for the next call
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -4795,7 +4801,11 @@ __global__ void __launch_bounds__(WCfg::NTHREADS, 1) wsample_kernel(const __grid
   // wide bands left for the whole CTA (the ring is free now)
   for (int w = 0; w < WCfg::NWARP; ++w)
     if (ws.pend[w].n > 0) cta_finish_wide<CFG>(P, ws, w);
-  if (ws.nflag == 0) return;  // nothing deferred: no grouped pass
+  if (ws.nflag == 0) {
+    // nothing deferred: no grouped pass; the state update may be scheduled
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    return;
+  }
   // compact the deferred entries to the front of this CTA's work-list slots
   if (warp == 0) {
     int j = 0;
@@ -5142,7 +5152,19 @@ int yapd_select_step(const yapd_select_args* a, void* stream) {
   rc = launch_sample(P, a->logits_dtype, 1 << 30, st);
   if (rc != YAPD_OK) return rc;
   if (a->prof_event_end) cudaEventRecordWithFlags(static_cast<cudaEvent_t>(a->prof_event_end), st, ev_flags);
-  unmask_kernel<<<(a->B + 3) / 4, 128, 0, st>>>(U, P.dense);
+  // the state update may be scheduled while the sampling kernel's last CTAs
+  // run; it waits for that kernel's completion on the device
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3((unsigned)((a->B + 3) / 4));
+  lc.blockDim = dim3(128);
+  lc.dynamicSmemBytes = 0;
+  lc.stream = st;
+  cudaLaunchAttribute la[1];
+  la[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  la[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = la;
+  lc.numAttrs = 1;
+  if (cudaLaunchKernelEx(&lc, unmask_kernel, U, (int)P.dense) != cudaSuccess) return YAPD_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? YAPD_OK : YAPD_ERR_LAUNCH;
 }
 

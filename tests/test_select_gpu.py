@@ -8,6 +8,7 @@ import torch
 from oracle import select_oracle as O
 from tests.golden import cases
 from tests.parity_util import compare, run_gpu
+from yapd_b200 import _native as N
 from yapd_b200.workloads import make_config
 
 pytestmark = pytest.mark.gpu
@@ -185,6 +186,26 @@ def test_status_word_clear():
     inp = make_config(0, seed=1)
     run_gpu(inp)
     assert S.read_status() == 0
+
+
+@pytest.mark.parametrize("B,L", [(3, 5), (40, 32), (300, 27)])
+def test_claimed_schedule_counters_return_to_zero(B, L):
+    """The grouped kernel's scheduling counters (workspace bytes 64-79: CTAs
+    past the preamble, entries appended, entries claimed, CTAs finished) are
+    zero after every call, whether the positions are fewer than the CTAs,
+    fill each CTA's own stages, or spill into the claimed list; two calls in
+    a row on the same workspace give the oracle's result."""
+    from yapd_b200 import select as S
+    inp = make_config(3, seed=13, B=B, L=L, V=600, masked="ragged", explicit_noise=False)
+    for offset in (0, 1):
+        gpu = run_gpu(inp, noise="philox", seed=5, offset=offset, dense=False, scalar_minp=True)
+        ws = S.workspace(N.lib().yapd_select_workspace_size(B, L), torch.device("cuda"))
+        assert ws[64:80].cpu().view(torch.int32).tolist() == [0, 0, 0, 0]
+        assert S.read_status() == 0
+        orc = O.select_step(inp, noise="philox", seed=5, offset=offset)
+        pos = (inp.xt == inp.mask_id) & ~inp.is_commit[:, None]
+        gt, _ = O.philox_noise(5, offset, inp.B, inp.L, inp.V)
+        compare(inp, gpu, orc, gt, positions=pos)
 
 
 @pytest.mark.parametrize("scale", [0.9, 1.1, 1.3, 2.0])

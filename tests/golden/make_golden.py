@@ -1,7 +1,7 @@
 """Generate the select-step golden fixtures from the unmodified reference.
 
-Run in a container that holds an m8than/yapd source checkout (default
-``/root/reference``, or ``$YAPD_REFERENCE_ROOT``):
+Run where an m8than/yapd source checkout is available (its location in
+``$YAPD_REFERENCE_ROOT``, else ``ref_loader.REF_ROOT``'s default):
 
     python -m tests.golden.make_golden
 

@@ -663,7 +663,7 @@ __device__ int cta_prepare_share(const SampleParams& P, int* own, int cap, int* 
       cnt += c;
     }
     const int rank = done + before + __popc(bal & ((1u << lane) - 1u));  // among the CTA's sampled positions
-    const int first_app = max(done, cap);                                // first rank appended this round
+    const int first_app = max(done, cap);                                // first rank appended in this pass
     const int n_app = max(0, done + cnt - first_app);
     if (threadIdx.x == 0 && n_app > 0) scan[nwarp] = (int)atomicAdd(P.sched + 1, (unsigned)n_app);
     __syncthreads();

@@ -38,7 +38,7 @@
 extern "C" {
 #endif
 
-#define YAPD_ABI_VERSION 3
+#define YAPD_ABI_VERSION 4  /* 4: the workspace must be zero-filled before its first call */
 
 /* Return codes (host-side validation; nothing is launched on error). */
 #define YAPD_OK 0

@@ -20,7 +20,7 @@ YAPD_NOISE_PHILOX = 0
 YAPD_NOISE_EXPLICIT = 1
 YAPD_MAX_V = 8208
 YAPD_MAX_L = 32
-YAPD_ABI_VERSION = 3
+YAPD_ABI_VERSION = 4
 YAPD_STATUS_WAIT_TIMEOUT = 1
 YAPD_STATUS_INTERNAL = 2
 YAPD_STATUS_ROWS_SKIPPED = 4
